@@ -1,0 +1,92 @@
+/*
+ * vkb.h -- C ABI of libvkb.so, the B200 (sm_100a) quantised matrix-multiply hot path of volta-kernel-bakeoff.
+ *
+ * Every entry point replaces one "contender launcher" of the reference harness, whose convention is
+ *     bool launch(int M, const uint32_t* q, const half* s, const half* x, float* y, int N, int K)
+ * (reference src/bakeoff.cu:263-280, src/stage2.cuh:221-224, src/stage4_tc.cuh:197-200): the caller owns every device
+ * buffer, the call is asynchronous on the given stream, and an unsupported shape launches nothing and writes nothing.
+ *
+ * Conventions of this library:
+ *   - return 0: launched. return > 0: VKB_E* below, nothing launched, nothing written. return < 0: -(cudaError_t) of
+ *     a CUDA runtime error, or -(VKB_NCCL_BASE + ncclResult_t) of an NCCL error. Nothing exits, traps or asserts.
+ *   - stream: a cudaStream_t (NULL = the legacy default stream).
+ *   - Weight formats (byte-identical to the reference, src/bakeoff.cu:5-8, :210-219, :486-490; src/stage2.cuh:235-244;
+ *     src/stage3_lut.cuh:4, :90-97), one fp16 scale per 32 consecutive values of a row, scales [N][K/32]:
+ *       Q4  uint32 [N][K/8]   word w of a row holds codes 8w..8w+7, code i in nibble i, stored as code + 8 (-8..7)
+ *       Q8  int8   [N][K]     one two's-complement code per value (-127..127)
+ *       Q2  uint32 [N][K/16]  word w holds codes 16w..16w+15, code i in bits 2i..2i+1, stored as code + 2 (-2..1)
+ *     value = code * scale. Activations x are fp16 [M][K] row-major; outputs y are fp16 [M][N] row-major (the _f32
+ *     variants write fp32, exactly the reference launchers' float* y).
+ *   - K must be a multiple of 32. The fast path (TMA-staged, tensor cores) needs K % 256 == 0 and 16-byte aligned
+ *     q, s and x; other shapes run a plain CUDA-core kernel with the same results.
+ *   - Thread-safe: per-device one-time set-up is guarded; tensor-map caches are per host thread.
+ *   - Launches use programmatic dependent launch (PDL) unless vkb_set_pdl(0): the weight stream of call i+1 overlaps
+ *     the tail of call i; activations and outputs are still ordered after the previous kernel on the stream.
+ */
+#ifndef VKB_H
+#define VKB_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st* vkb_stream_t; /* == cudaStream_t */
+
+enum {
+    VKB_OK = 0,
+    VKB_EUNSUPPORTED = 1, /* shape, token count or format not supported: nothing launched */
+    VKB_EINVAL = 2,       /* null pointer or out-of-range argument: nothing launched */
+    VKB_ENOCOMM = 3,      /* multi-GPU call without a communicator */
+    VKB_EDEVICE = 4,      /* a kernel reported a device-side timeout (see vkb_device_status) */
+};
+#define VKB_NCCL_BASE 1000
+
+enum { VKB_FMT_Q4 = 0, VKB_FMT_Q8 = 1, VKB_FMT_Q2 = 2 };
+
+/* ---- decode GEMV: y[M][N] = x[M][K] . W[N][K]^T, 1 <= M <= 8 ------------------------------------------------------
+ * Replace fused_q4_v2w<M> / fused_q4_v3 (reference src/stage2.cuh:61-92, :217-224; src/stage5_gap8.cuh:57-137,
+ * :203-205), fused_q8<M> (src/bakeoff.cu:115-155, :272-280) and q2w_alu_v3 (src/stage3_lut.cuh:155-185; the
+ * reference has 1 token only). fp16 output. */
+int vkb_gemv_q4(const void* q, const void* s, const void* x, void* y, int N, int K, int M, vkb_stream_t stream);
+int vkb_gemv_q8(const void* q, const void* s, const void* x, void* y, int N, int K, int M, vkb_stream_t stream);
+int vkb_gemv_q2(const void* q, const void* s, const void* x, void* y, int N, int K, int M, vkb_stream_t stream);
+/* The same with fp32 output, the reference launchers' own float* y (src/bakeoff.cu:263-280). */
+int vkb_gemv_q4_f32(const void* q, const void* s, const void* x, float* y, int N, int K, int M, vkb_stream_t stream);
+int vkb_gemv_q8_f32(const void* q, const void* s, const void* x, float* y, int N, int K, int M, vkb_stream_t stream);
+int vkb_gemv_q2_f32(const void* q, const void* s, const void* x, float* y, int N, int K, int M, vkb_stream_t stream);
+/* Format chosen at run time (fmt = VKB_FMT_*), out_f32 selects the fp32 output. */
+int vkb_gemv(int fmt, const void* q, const void* s, const void* x, void* y, int out_f32, int N, int K, int M,
+             vkb_stream_t stream);
+
+/* ---- MoE decode, one launch ----------------------------------------------------------------------------------------
+ * Replaces moe_fused_q4 + MoePtrs (reference src/bakeoff.cu:157-186, :826-830), where the host picked one pointer set
+ * per expert, with a device-side index list:
+ *   qpool [E_local][N][K/8] (Q4; Q8/Q2 analogously), spool [E_local][N][K/32] fp16 -- the experts e0..e0+E_local-1
+ *   idx   int32 [T][topk] global expert ids (distinct per token in the reference's usage; duplicates are allowed)
+ *   x     fp16 [T][K], y fp16 [T][topk][N]: y[t][j] = W_{idx[t][j]} . x[t]
+ * Slots whose expert is outside [e0, e0 + E_local) are not written (expert parallelism: each rank fills its own). All
+ * slots of one expert share a single pass over that expert's weights (up to 8 tokens per pass). */
+int vkb_moe_q4(const void* qpool, const void* spool, const int32_t* idx, int T, int topk, const void* x, void* y,
+               int E_local, int e0, int N, int K, vkb_stream_t stream);
+int vkb_moe(int fmt, const void* qpool, const void* spool, const int32_t* idx, int T, int topk, const void* x, void* y,
+            int out_f32, int E_local, int e0, int N, int K, vkb_stream_t stream);
+
+/* ---- status --------------------------------------------------------------------------------------------------------- */
+/* Human-readable text of a return code. */
+const char* vkb_strerror(int code);
+/* Synchronises the current device, returns (and clears) the device-side status bits that kernels raise when a bounded
+ * wait gives up (1 = pipeline wait timeout, 2 = drain timeout, 4 = peer timeout). 0 = healthy. */
+int vkb_device_status(unsigned int* bits);
+/* Enable (1) or disable (0) programmatic dependent launch for later calls on this host thread; returns the old value. */
+int vkb_set_pdl(int enable);
+/* Library version, e.g. 100 for 0.1.0. */
+int vkb_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* VKB_H */

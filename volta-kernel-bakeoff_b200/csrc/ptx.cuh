@@ -1,0 +1,170 @@
+// Thin inline-PTX wrappers for sm_100a: mbarriers, TMA (cp.async.bulk / cp.async.bulk.tensor), programmatic
+// dependent launch, the m16n8k16 tensor-core MMA, and the bounded waits every kernel in this library uses.
+//
+// Every spin in this library goes through wait_parity(): it gives up after VKB_WAIT_NS of %globaltimer time, records
+// the failure in the device-wide status word (vkb_dev_status) and returns false, so a lost copy or a logic error shows
+// up as an error code on the host instead of a hung GPU.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <stdint.h>
+
+#ifndef VKB_WAIT_NS
+#define VKB_WAIT_NS 2000000000ull  // 2 s: far above any legitimate wait (a whole previous kernel under PDL)
+#endif
+
+namespace vkb {
+
+// Status bits a kernel can raise (read and cleared by vkb_device_status()).
+enum : unsigned { DEV_ERR_WAIT_TIMEOUT = 1u, DEV_ERR_DRAIN_TIMEOUT = 2u, DEV_ERR_PEER_TIMEOUT = 4u };
+
+}  // namespace vkb
+
+// One status word per translation unit (device variables are not shared across TUs without relocatable device
+// code); each TU that launches kernels exposes a host accessor through VKB_STATUS_ACCESSOR and vkb_device_status()
+// reads them all.
+static __device__ unsigned int vkb_dev_status;
+
+#define VKB_STATUS_ACCESSOR(fn)                                                        \
+    int fn(unsigned* bits) {                                                           \
+        unsigned v = 0, zero = 0;                                                      \
+        cudaError_t e = cudaMemcpyFromSymbol(&v, vkb_dev_status, sizeof(v));            \
+        if (e == cudaSuccess) e = cudaMemcpyToSymbol(vkb_dev_status, &zero, sizeof(v)); \
+        *bits |= v;                                                                    \
+        return e == cudaSuccess ? 0 : -(int)e;                                         \
+    }
+
+namespace vkb {
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ uint64_t globaltimer() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+__device__ __forceinline__ void raise_status(unsigned bits) { atomicOr(&vkb_dev_status, bits); }
+
+// ---- mbarrier -------------------------------------------------------------------------------------------------
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void fence_mbar_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+                 : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar_addr, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(bar_addr), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// Wait for the phase with the given parity to complete. Bounded: false (and a status bit) after VKB_WAIT_NS.
+__device__ __forceinline__ bool wait_parity(uint64_t* bar, uint32_t parity, unsigned err = DEV_ERR_WAIT_TIMEOUT) {
+    const uint32_t a = smem_u32(bar);
+    if (mbar_try_wait(a, parity)) return true;
+    const uint64_t t0 = globaltimer();
+    for (uint32_t i = 0;; ++i) {
+        if (mbar_try_wait(a, parity)) return true;
+        if ((i & 255u) == 255u && globaltimer() - t0 > VKB_WAIT_NS) {
+            raise_status(err);
+            return false;
+        }
+    }
+}
+
+// ---- TMA ------------------------------------------------------------------------------------------------------
+
+// 2-D tiled tensor load (no multicast) into this CTA's shared memory, completing bytes on bar.
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];"
+        ::"r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y)
+        : "memory");
+}
+
+// 1-D bulk copy global -> shared (both addresses 16-byte aligned, bytes a multiple of 16), completing on bar.
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+        ::"r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
+
+__device__ __forceinline__ void prefetch_tmap(const CUtensorMap* map) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
+// ---- programmatic dependent launch ------------------------------------------------------------------------------
+
+// Block until every grid this one depends on has completed and its memory is visible (no-op without PDL).
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+// Let the next grid in the stream start its prologue (it still waits in pdl_wait() for this grid to finish).
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// ---- named barriers (a subset of the CTA's warps) ----------------------------------------------------------------
+
+__device__ __forceinline__ void named_sync(uint32_t id, uint32_t nthreads) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
+// ---- m16n8k16 f16 x f16 -> f32 ----------------------------------------------------------------------------------
+
+__device__ __forceinline__ void mma_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                          uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// ---- small bit helpers ------------------------------------------------------------------------------------------
+
+__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
+    uint32_t r;
+    asm("prmt.b32 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(sel));
+    return r;
+}
+
+// (a & b) | c in one LOP3
+__device__ __forceinline__ uint32_t and_or(uint32_t a, uint32_t b, uint32_t c) {
+    uint32_t r;
+    asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(r) : "r"(a), "r"(b), "r"(c));
+    return r;
+}
+
+__device__ __forceinline__ uint32_t h2_sub(uint32_t a, uint32_t b) {
+    uint32_t r;
+    asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+    return r;
+}
+
+__device__ __forceinline__ uint32_t h2_fma(uint32_t a, uint32_t b, uint32_t c) {
+    uint32_t r;
+    asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(c));
+    return r;
+}
+
+}  // namespace vkb

@@ -1,0 +1,459 @@
+// Quantised matrix-vector product for 1..8 tokens (decode), dense or MoE, on sm_100a.
+//
+//   y[m][n] = sum_k x[m][k] * code[n][k] * scale[n][k/32]
+//
+// Weight formats are the bakeoff's, byte for byte (reference src/bakeoff.cu:5-8, :210-219, :486-490;
+// src/stage3_lut.cuh:4, :90-97):
+//   Q4  u32 [N][K/8]   word w of a row holds codes 8w..8w+7, code i in nibble i, stored as code + 8
+//   Q8  i8  [N][K]     one two's-complement code per value
+//   Q2  u32 [N][K/16]  word w holds codes 16w..16w+15, code i in bits 2i..2i+1, stored as code + 2
+//   scales fp16 [N][K/32]; x fp16 [T][K]; y fp16 or fp32.
+//
+// Design (one CTA per SM, persistent over 16-row tiles):
+//   * warp NW (the producer) streams 16-row x KS-column stages of codes and scales into a shared-memory ring with
+//     2-D TMA tiles (128-byte swizzle, so the consumers' reads are bank-conflict free); the weight stages are issued
+//     before griddepcontrol.wait, so under programmatic dependent launch the next call's weight stream overlaps the
+//     previous call's tail. The activations (after the wait) come in as 1-D bulk copies.
+//   * warps 0..NW-1 split each stage's K range and run the m16n8k16 tensor-core MMA with the weights as A (16 rows)
+//     and the tokens as B (8 columns). The codes enter the MMA exactly: the fp16 magic-number trick (0x6400 | n is
+//     the half 1024 + n) turns two codes into one f16x2 with one LOP3 and one HSUB2/HFMA2, and every 32-value group is
+//     accumulated on its own (two k16 steps) and then scaled in fp32, so the result is the exact-code fp32-sum class
+//     of the reference's fused kernels (tolerance 1e-4 of sum|x*w|), not the fp16-rounded-weight class.
+//   * inside one k16 step the order of k is free as long as A and B agree; each format picks the order that makes its
+//     unpack cheapest and permutes the activations to match with PRMT.
+//   * per-tile partial sums of the NW warps are added in shared memory and written by warp 0.
+#pragma once
+
+#include "ptx.cuh"
+
+namespace vkb {
+
+enum : int { FMT_Q4 = 0, FMT_Q8 = 1, FMT_Q2 = 2 };
+
+template <int F> struct FmtTraits;
+template <> struct FmtTraits<FMT_Q4> { static constexpr int BITS = 4, KS_UNIT = 256; };
+template <> struct FmtTraits<FMT_Q8> { static constexpr int BITS = 8, KS_UNIT = 256; };
+template <> struct FmtTraits<FMT_Q2> { static constexpr int BITS = 2, KS_UNIT = 512; };
+
+constexpr int QMV_NW = 8;          // consumer warps per CTA
+constexpr int QMV_ROWS = 16;       // weight rows per tile (the MMA's M)
+constexpr int QMV_MAXTOK = 8;      // tokens per MMA column group (the MMA's N)
+constexpr int QMV_BOX_BYTES = 16 * 128;   // one 16-row x 128-byte TMA box
+
+enum : int { QMV_DENSE = 0, QMV_MOE = 1 };
+
+struct QmvArgs {
+    const __half* x;         // [T][K]
+    void* y;                 // dense: [T][N]; MoE: [T*topk][N]
+    const int32_t* idx;      // MoE: [T*topk] global expert ids
+    int N, K;                // rows per matrix (per expert), inner dimension
+    int T;                   // dense: tokens (M); MoE: tokens
+    int topk;                // MoE: slots per token
+    int E_local, e0;         // MoE: experts held in this pool, id of the first one
+    int KS, nchunks;         // stage width in k values, stages per row tile
+    int nstage;              // ring depth
+    int stage_bytes;         // shared bytes per stage (1024-aligned)
+    int xpitch;              // shared bytes per staged activation row
+    int xrows;               // staged activation rows per buffer (<= 8)
+    int tilesN;              // ceil(N / 16)
+    int ring_off, x_off, red_off, bar_off, moe_off;   // shared-memory carve-up (bytes from the aligned base)
+};
+
+// ---- per-format unpack: one 32-bit word of codes -> the four f16x2 A registers this thread feeds the MMA ----------
+
+// Q4, word t of a group: (c0,c4) (c1,c5) | (c2,c6) (c3,c7); exact code values.
+__device__ __forceinline__ void unpack_q4(uint32_t v, uint32_t (&a)[4]) {
+    const uint32_t M = 0x64006400u;
+    const uint32_t vs = v >> 8;
+    a[0] = h2_sub(and_or(v, 0x000F000Fu, M), 0x64086408u);                 // 1024 + n - 1032
+    a[1] = h2_fma(and_or(v, 0x00F000F0u, M), 0x2C002C00u, 0xD480D480u);    // (1024 + 16n)/16 - 72
+    a[2] = h2_sub(and_or(vs, 0x000F000Fu, M), 0x64086408u);
+    a[3] = h2_fma(and_or(vs, 0x00F000F0u, M), 0x2C002C00u, 0xD480D480u);
+}
+
+// Q8, words 2t and 2t+1 of a group: (c0,c1) (c2,c3) | (c4,c5) (c6,c7).
+__device__ __forceinline__ void unpack_q8(uint32_t w0, uint32_t w1, uint32_t (&a)[4]) {
+    const uint32_t u0 = w0 ^ 0x80808080u, u1 = w1 ^ 0x80808080u;   // offset binary: c + 128
+    a[0] = h2_sub(prmt(u0, 0x64646464u, 0x4140u), 0x64806480u);    // 1024 + c + 128 - 1152
+    a[1] = h2_sub(prmt(u0, 0x64646464u, 0x4342u), 0x64806480u);
+    a[2] = h2_sub(prmt(u1, 0x64646464u, 0x4140u), 0x64806480u);
+    a[3] = h2_sub(prmt(u1, 0x64646464u, 0x4342u), 0x64806480u);
+}
+
+// Q2, half h of word p (already shifted right by 8h): (c0,c8) (c1,c9) | (c2,c10) (c3,c11) of that half.
+__device__ __forceinline__ void unpack_q2(uint32_t vs, uint32_t (&a)[4]) {
+    const uint32_t M = 0x64006400u;
+    a[0] = h2_sub(and_or(vs, 0x00030003u, M), 0x64026402u);                // 1024 + u - 1026
+    a[1] = h2_fma(and_or(vs, 0x000C000Cu, M), 0x34003400u, 0xDC08DC08u);   // (1024 + 4u)/4 - 258
+    a[2] = h2_fma(and_or(vs, 0x00300030u, M), 0x2C002C00u, 0xD420D420u);   // (1024 + 16u)/16 - 66
+    a[3] = h2_fma(and_or(vs, 0x00C000C0u, M), 0x24002400u, 0xCC80CC80u);   // (1024 + 64u)/64 - 18
+}
+
+// Byte offset, inside a stage, of what thread (row r, lane-in-quad t) reads for stage-local group G.
+template <int F>
+__device__ __forceinline__ uint32_t code_off(int G, int r, int t) {
+    const int sw = r & 7;
+    if constexpr (F == FMT_Q4) {
+        return (G >> 3) * QMV_BOX_BYTES + r * 128 + ((((G & 7)) ^ sw) << 4) + 4 * t;
+    } else if constexpr (F == FMT_Q8) {
+        return (G >> 2) * QMV_BOX_BYTES + r * 128 + (((2 * (G & 3) + (t >> 1)) ^ sw) << 4) + 8 * (t & 1);
+    } else {
+        return (G >> 4) * QMV_BOX_BYTES + r * 128 + ((((G & 15) >> 1) ^ sw) << 4) + 8 * (G & 1) + 4 * (t >> 1);
+    }
+}
+
+template <int F>
+__device__ __forceinline__ void load_a(const uint8_t* stage, int G, int r, int t, uint32_t (&a)[4]) {
+    const uint8_t* p = stage + code_off<F>(G, r, t);
+    if constexpr (F == FMT_Q4) {
+        unpack_q4(*reinterpret_cast<const uint32_t*>(p), a);
+    } else if constexpr (F == FMT_Q8) {
+        const uint2 w = *reinterpret_cast<const uint2*>(p);
+        unpack_q8(w.x, w.y, a);
+    } else {
+        unpack_q2(*reinterpret_cast<const uint32_t*>(p) >> (8 * (t & 1)), a);
+    }
+}
+
+// The B registers (two k16 steps) of token row xr (nullptr = a padding column) for the group at global k = k0.
+template <int F>
+__device__ __forceinline__ void load_b(const uint8_t* xr, int k0, int t, uint32_t (&b)[4]) {
+    if (xr == nullptr) {
+        b[0] = b[1] = b[2] = b[3] = 0u;
+        return;
+    }
+    if constexpr (F == FMT_Q2) {
+        const int base = k0 + 16 * (t >> 1) + 4 * (t & 1);
+        const uint2 xa = *reinterpret_cast<const uint2*>(xr + 2 * base);
+        const uint2 xb = *reinterpret_cast<const uint2*>(xr + 2 * base + 16);
+        b[0] = prmt(xa.x, xb.x, 0x5410u);   // (x0, x8)
+        b[1] = prmt(xa.x, xb.x, 0x7632u);   // (x1, x9)
+        b[2] = prmt(xa.y, xb.y, 0x5410u);   // (x2, x10)
+        b[3] = prmt(xa.y, xb.y, 0x7632u);   // (x3, x11)
+    } else {
+        const uint4 v = *reinterpret_cast<const uint4*>(xr + 2 * (k0 + 8 * t));
+        if constexpr (F == FMT_Q4) {
+            b[0] = prmt(v.x, v.z, 0x5410u);   // (x0, x4)
+            b[1] = prmt(v.x, v.z, 0x7632u);   // (x1, x5)
+            b[2] = prmt(v.y, v.w, 0x5410u);   // (x2, x6)
+            b[3] = prmt(v.y, v.w, 0x7632u);   // (x3, x7)
+        } else {
+            b[0] = v.x; b[1] = v.y; b[2] = v.z; b[3] = v.w;
+        }
+    }
+}
+
+// One stage (16 rows x KS) for this warp's share of its groups [G0, G1), accumulating into acc.
+template <int F>
+__device__ __forceinline__ void consume_stage(const uint8_t* stage, int KS, int G0, int G1, int kchunk, int KG,
+                                              const uint8_t* xr, int g, int t, float (&acc)[4]) {
+    constexpr int BITS = FmtTraits<F>::BITS;
+    const int nb = KS * BITS / 8 / 128;
+    const __half* sc = reinterpret_cast<const __half*>(stage + nb * QMV_BOX_BYTES);
+    const int spitch = KS / 32;   // halves per scale row
+    const int gbase = kchunk / 32;
+#pragma unroll 2
+    for (int G = G0; G < G1; ++G) {
+        if (gbase + G >= KG) break;   // past K (warp-uniform)
+        uint32_t b[4], ar[4], ar8[4];
+        load_b<F>(xr, kchunk + 32 * G, t, b);
+        load_a<F>(stage, G, g, t, ar);
+        load_a<F>(stage, G, g + 8, t, ar8);
+        float d[4] = {0.f, 0.f, 0.f, 0.f};
+        mma_16816(d, ar[0], ar8[0], ar[1], ar8[1], b[0], b[1]);
+        mma_16816(d, ar[2], ar8[2], ar[3], ar8[3], b[2], b[3]);
+        const float s0 = __half2float(sc[g * spitch + G]);
+        const float s1 = __half2float(sc[(g + 8) * spitch + G]);
+        acc[0] = fmaf(d[0], s0, acc[0]);
+        acc[1] = fmaf(d[1], s0, acc[1]);
+        acc[2] = fmaf(d[2], s1, acc[2]);
+        acc[3] = fmaf(d[3], s1, acc[3]);
+    }
+}
+
+template <typename OutT> __device__ __forceinline__ OutT to_out(float v);
+template <> __device__ __forceinline__ __half to_out<__half>(float v) { return __float2half_rn(v); }
+template <> __device__ __forceinline__ float to_out<float>(float v) { return v; }
+
+// ---- MoE routing tables (built redundantly and deterministically by every CTA) ---------------------------------
+//
+// A "segment" is one expert with up to 8 of its (token, slot) pairs: the tokens of one MMA column group. Slots of an
+// expert are taken in increasing slot order, so every CTA builds the identical table.
+struct MoeTables {
+    int* cnt;       // [E_local]
+    int* off;       // [E_local + 1]  first position of each expert in `slots`
+    int* segoff;    // [E_local + 1]  first segment of each expert
+    int* slots;     // [T*topk]      slot ids grouped by expert
+    int* seg;       // [T*topk]      (expert << 16) | first position in `slots`
+};
+
+__device__ __forceinline__ MoeTables moe_tables(uint8_t* base, int E_local, int nslots) {
+    MoeTables t;
+    int* p = reinterpret_cast<int*>(base);
+    t.cnt = p; p += E_local;
+    t.off = p; p += E_local + 1;
+    t.segoff = p; p += E_local + 1;
+    t.slots = p; p += nslots;
+    t.seg = p;
+    return t;
+}
+
+// Returns the number of segments. Call with all threads of the CTA.
+__device__ __forceinline__ int moe_route(const QmvArgs& a, MoeTables tb) {
+    const int nslots = a.T * a.topk;
+    const int tid = threadIdx.x, nth = blockDim.x;
+    for (int e = tid; e < a.E_local; e += nth) tb.cnt[e] = 0;
+    __syncthreads();
+    for (int i = tid; i < nslots; i += nth) {
+        const int e = __ldg(a.idx + i) - a.e0;
+        if (e >= 0 && e < a.E_local) atomicAdd(&tb.cnt[e], 1);
+    }
+    __syncthreads();
+    if (tid < 32) {   // one warp: exclusive scans, then a stable placement of the slots
+        const int lane = tid;
+        int run_off = 0, run_seg = 0;
+        for (int b = 0; b < a.E_local; b += 32) {
+            const int e = b + lane;
+            const int c = e < a.E_local ? tb.cnt[e] : 0;
+            const int s = (c + QMV_MAXTOK - 1) / QMV_MAXTOK;
+            int ic = c, is = s;
+#pragma unroll
+            for (int d = 1; d < 32; d <<= 1) {
+                const int vc = __shfl_up_sync(0xffffffffu, ic, d);
+                const int vs = __shfl_up_sync(0xffffffffu, is, d);
+                if (lane >= d) { ic += vc; is += vs; }
+            }
+            if (e < a.E_local) {
+                tb.off[e] = run_off + ic - c;
+                tb.segoff[e] = run_seg + is - s;
+                tb.cnt[e] = 0;   // from here on: placement cursor
+            }
+            run_off += __shfl_sync(0xffffffffu, ic, 31);
+            run_seg += __shfl_sync(0xffffffffu, is, 31);
+        }
+        if (lane == 0) {
+            tb.off[a.E_local] = run_off;
+            tb.segoff[a.E_local] = run_seg;
+        }
+        __syncwarp();
+        // 32 slots at a time, in slot order; a slot's rank = lanes below it with the same expert
+        for (int i0 = 0; i0 < nslots; i0 += 32) {
+            const int i = i0 + lane;
+            int e = i < nslots ? __ldg(a.idx + i) - a.e0 : -1;
+            if (e < 0 || e >= a.E_local) e = -1;
+            const unsigned same = __match_any_sync(0xffffffffu, e);
+            const int rank = __popc(same & ((1u << lane) - 1u));
+            const int leader = __ffs(same) - 1;
+            int base = (e >= 0 && lane == leader) ? tb.cnt[e] : 0;
+            base = __shfl_sync(0xffffffffu, base, leader);
+            if (e >= 0) tb.slots[tb.off[e] + base + rank] = i;
+            __syncwarp();
+            if (e >= 0 && lane == leader) tb.cnt[e] = base + __popc(same);
+            __syncwarp();
+        }
+    }
+    __syncthreads();
+    for (int e = tid; e < a.E_local; e += nth) {
+        const int first = tb.off[e], n = tb.off[e + 1] - first, s0 = tb.segoff[e];
+        for (int c = 0; c * QMV_MAXTOK < n; ++c) tb.seg[s0 + c] = (e << 16) | (first + c * QMV_MAXTOK);
+    }
+    __syncthreads();
+    return tb.segoff[a.E_local];
+}
+
+// ---- the kernel ---------------------------------------------------------------------------------------------------
+
+// Barrier block layout (uint64 slots from bar_off): full[nstage], empty[nstage], xfull[2], xempty[2], redfull[2],
+// redfree[2].
+__host__ __device__ constexpr int qmv_nbars(int nstage) { return 2 * nstage + 8; }
+
+template <int F, int MODE, typename OutT>
+__global__ void __launch_bounds__(32 * (QMV_NW + 1), 1)
+qmv_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap ts, const QmvArgs a) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* ring = sm + a.ring_off;
+    uint8_t* xbuf = sm + a.x_off;
+    float4* red = reinterpret_cast<float4*>(sm + a.red_off);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(sm + a.bar_off);
+    uint64_t* full = bars;
+    uint64_t* empty = bars + a.nstage;
+    uint64_t* xfull = bars + 2 * a.nstage;
+    uint64_t* xempty = xfull + 2;
+    uint64_t* redfull = xfull + 4;
+    uint64_t* redfree = xfull + 6;
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int KG = a.K / 32;
+
+    pdl_trigger();   // the next call may start its weight prefetch now (it still waits for us before touching y)
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < a.nstage; ++i) {
+            mbar_init(&full[i], 1);
+            mbar_init(&empty[i], QMV_NW);
+        }
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(&xfull[i], 1);
+            mbar_init(&xempty[i], QMV_NW);
+            mbar_init(&redfull[i], QMV_NW);
+            mbar_init(&redfree[i], 1);
+        }
+        fence_mbar_init();
+    }
+
+    int nseg = 1;
+    MoeTables tb{};
+    if constexpr (MODE == QMV_MOE) {
+        tb = moe_tables(sm + a.moe_off, a.E_local, a.T * a.topk);
+        nseg = moe_route(a, tb);   // contains __syncthreads
+    } else {
+        __syncthreads();
+    }
+
+    const int total = nseg * a.tilesN;
+    const int w0 = (int)(((long long)blockIdx.x * total) / gridDim.x);
+    const int w1 = (int)(((long long)(blockIdx.x + 1) * total) / gridDim.x);
+
+    // segment accessors: expert (weight row base), token count, and the slot (dense: token) of column j
+    auto seg_expert = [&](int s) -> int {
+        if constexpr (MODE == QMV_MOE) return tb.seg[s] >> 16; else return 0;
+    };
+    auto seg_first = [&](int s) -> int {
+        if constexpr (MODE == QMV_MOE) return tb.seg[s] & 0xFFFF; else return 0;
+    };
+    auto seg_count = [&](int s) -> int {
+        if constexpr (MODE == QMV_MOE) return min(QMV_MAXTOK, tb.off[(tb.seg[s] >> 16) + 1] - seg_first(s));
+        else return a.T;
+    };
+    auto seg_slot = [&](int s, int j) -> int {
+        if constexpr (MODE == QMV_MOE) return tb.slots[seg_first(s) + j]; else return j;
+    };
+
+    constexpr int BITS = FmtTraits<F>::BITS;
+    const int nb = a.KS * BITS / 8 / 128;
+    const uint32_t stage_tx = (uint32_t)(nb * QMV_BOX_BYTES + a.KS);   // codes + 16 rows x KS/32 scales
+
+    if (warp == QMV_NW) {
+        // ===================== producer (one thread) =====================
+        if (lane == 0) {
+            prefetch_tmap(&tq);
+            prefetch_tmap(&ts);
+            const int total_it = (w1 - w0) * a.nchunks;
+            const int pre = min(total_it, a.nstage);
+            int issued = 0;
+            auto issue_w = [&](int it) {
+                const int w = w0 + it / a.nchunks, c = it % a.nchunks;
+                const int s = w / a.tilesN, tile = w % a.tilesN;
+                const int row = seg_expert(s) * a.N + tile * QMV_ROWS;
+                uint8_t* st = ring + (it % a.nstage) * a.stage_bytes;
+                uint64_t* fb = &full[it % a.nstage];
+                mbar_arrive_expect_tx(fb, stage_tx);
+                const int xb0 = c * a.KS * BITS / 8;
+                for (int j = 0; j < nb; ++j) tma_load_2d(st + j * QMV_BOX_BYTES, &tq, xb0 + 128 * j, row, fb);
+                tma_load_2d(st + nb * QMV_BOX_BYTES, &ts, c * (a.KS / 32), row, fb);
+                ++issued;
+            };
+            int xsegs = 0;
+            bool ok = true;
+            auto issue_x = [&](int s) {   // activations of the next segment this CTA meets, double-buffered
+                const int xb = xsegs & 1;
+                if (xsegs >= 2) ok = wait_parity(&xempty[xb], ((xsegs >> 1) - 1) & 1);
+                if (!ok) return;
+                const int cnt = seg_count(s);
+                uint8_t* dst = xbuf + xb * a.xrows * a.xpitch;
+                mbar_arrive_expect_tx(&xfull[xb], (uint32_t)(cnt * a.K * 2));
+                for (int j = 0; j < cnt; ++j) {
+                    int tok = seg_slot(s, j);
+                    if constexpr (MODE == QMV_MOE) tok /= a.topk;
+                    bulk_load(dst + j * a.xpitch, a.x + (size_t)tok * a.K, (uint32_t)(a.K * 2), &xfull[xb]);
+                }
+                ++xsegs;
+            };
+            for (int it = 0; it < pre; ++it) issue_w(it);   // the weights do not depend on the previous grid
+            pdl_wait();                                     // the activations may
+            int last_seg = -1;
+            for (int it = 0; it < pre && ok; it += a.nchunks) {
+                const int s = (w0 + it / a.nchunks) / a.tilesN;
+                if (s != last_seg) { issue_x(s); last_seg = s; }
+            }
+            for (int it = pre; it < total_it && ok; ++it) {
+                const int s = (w0 + it / a.nchunks) / a.tilesN;
+                if (s != last_seg) { issue_x(s); last_seg = s; if (!ok) break; }
+                ok = wait_parity(&empty[it % a.nstage], ((it / a.nstage) - 1) & 1);
+                if (!ok) break;
+                issue_w(it);
+            }
+            // drain: every copy this CTA issued lands before the CTA may exit (bounded as well)
+            for (int it = max(0, issued - a.nstage); it < issued; ++it)
+                if (!wait_parity(&full[it % a.nstage], (it / a.nstage) & 1, DEV_ERR_DRAIN_TIMEOUT)) break;
+            for (int j = max(0, xsegs - 2); j < xsegs; ++j)
+                if (!wait_parity(&xfull[j & 1], (j >> 1) & 1, DEV_ERR_DRAIN_TIMEOUT)) break;
+        }
+        return;
+    }
+
+    // ===================== consumers (warps 0..NW-1) =====================
+    const int g = lane >> 2, t = lane & 3;
+    const int gpw = (a.KS / 32) / QMV_NW;
+    const int G0 = warp * gpw, G1 = G0 + gpw;
+    OutT* y = reinterpret_cast<OutT*>(a.y);
+    pdl_wait();   // y may still be read or written by the previous grid
+
+    int cur_seg = -1, segs_seen = 0, cnt = 0;
+    const uint8_t* xr = nullptr;
+    int it = 0, ntile = 0;
+    bool ok = true;
+    for (int w = w0; w < w1 && ok; ++w, ++ntile) {
+        const int s = w / a.tilesN, tile = w % a.tilesN;
+        if (s != cur_seg) {
+            if (cur_seg >= 0) {
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&xempty[(segs_seen - 1) & 1]);
+            }
+            cur_seg = s;
+            const int xb = segs_seen & 1;
+            ok = wait_parity(&xfull[xb], (segs_seen >> 1) & 1);
+            ++segs_seen;
+            cnt = seg_count(s);
+            xr = g < cnt ? xbuf + xb * a.xrows * a.xpitch + g * a.xpitch : nullptr;
+            if (!ok) break;
+        }
+        float acc[4] = {0.f, 0.f, 0.f, 0.f};
+        for (int c = 0; c < a.nchunks; ++c, ++it) {
+            const int st = it % a.nstage;
+            if (!wait_parity(&full[st], (it / a.nstage) & 1)) { ok = false; break; }
+            consume_stage<F>(ring + st * a.stage_bytes, a.KS, G0, G1, c * a.KS, KG, xr, g, t, acc);
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[st]);
+        }
+        if (!ok) break;
+        // cross-warp reduction of the tile (double-buffered, bounded mbarrier handshakes), then the write-back
+        const int tp = ntile & 1, use = ntile >> 1;
+        if (use > 0 && !wait_parity(&redfree[tp], (use - 1) & 1)) { ok = false; break; }
+        red[(tp * QMV_NW + warp) * 32 + lane] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&redfull[tp]);
+        if (warp == 0) {
+            if (!wait_parity(&redfull[tp], use & 1)) { ok = false; break; }
+            float4 r = red[(tp * QMV_NW) * 32 + lane];
+#pragma unroll
+            for (int v = 1; v < QMV_NW; ++v) {
+                const float4 q = red[(tp * QMV_NW + v) * 32 + lane];
+                r.x += q.x; r.y += q.y; r.z += q.z; r.w += q.w;
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&redfree[tp]);
+            const int n0 = tile * QMV_ROWS + g, n1 = n0 + 8;
+            const float vals[4] = {r.x, r.y, r.z, r.w};
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                const int col = 2 * t + (q & 1);
+                const int n = (q < 2) ? n0 : n1;
+                if (col < cnt && n < a.N) y[(size_t)seg_slot(s, col) * a.N + n] = to_out<OutT>(vals[q]);
+            }
+        }
+    }
+}
+
+}  // namespace vkb

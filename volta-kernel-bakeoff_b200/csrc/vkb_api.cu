@@ -1,0 +1,355 @@
+// libvkb.so: the extern "C" entry points of include/vkb.h for the decode GEMV and MoE kernels, with argument
+// validation, launch planning (stage width, ring depth, grid), TMA descriptor set-up and the status calls.
+#include <cuda_runtime.h>
+
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <mutex>
+#include <unordered_map>
+
+#include "../../include/vkb.h"
+#include "qmv.cuh"
+#include "qmv_simple.cuh"
+#include "vkb_internal.h"
+
+namespace vkb {
+
+VKB_STATUS_ACCESSOR(status_take_qmv)
+
+StatusList status_accessors() {
+    static const StatusTake list[] = {status_take_qmv};
+    return {list, list + sizeof(list) / sizeof(list[0])};
+}
+
+// ---- per-device facts, computed once ---------------------------------------------------------------------------
+
+const DeviceInfo& device_info(int dev) {
+    static DeviceInfo info[kMaxDevices];
+    static std::once_flag once[kMaxDevices];
+    std::call_once(once[dev], [dev] {
+        DeviceInfo d{};
+        cudaDeviceGetAttribute(&d.sm_count, cudaDevAttrMultiProcessorCount, dev);
+        cudaDeviceGetAttribute(&d.smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+        cudaDeviceGetAttribute(&d.smem_per_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev);
+        cudaDeviceGetAttribute(&d.cc_major, cudaDevAttrComputeCapabilityMajor, dev);
+        info[dev] = d;
+    });
+    return info[dev];
+}
+
+int current_device(int* dev) {
+    const cudaError_t e = cudaGetDevice(dev);
+    if (e != cudaSuccess) return -(int)e;
+    if (*dev < 0 || *dev >= kMaxDevices) return VKB_EINVAL;
+    return 0;
+}
+
+thread_local int t_pdl = -1;
+// PDL is not used on the legacy NULL stream, whose implicit synchronisation with every other stream does not mix
+// with programmatic serialisation; any created stream (or the per-thread default stream) gets it.
+static bool pdl_stream_ok(cudaStream_t st) { return st != nullptr && st != cudaStreamLegacy; }
+bool pdl_enabled() {
+    if (t_pdl < 0) {
+        const char* e = getenv("VKB_PDL");
+        t_pdl = (e && e[0] == '0') ? 0 : 1;
+    }
+    return t_pdl != 0;
+}
+
+// ---- TMA descriptors --------------------------------------------------------------------------------------------
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            p = nullptr;
+        return reinterpret_cast<EncodeTiledFn>(p);
+    }();
+    return fn;
+}
+
+struct MapKey {
+    const void* ptr;
+    uint64_t rows, row_bytes;
+    uint32_t box0, box1, dtype, swz;
+    bool operator==(const MapKey& o) const { return memcmp(this, &o, sizeof(MapKey)) == 0; }
+};
+struct MapKeyHash {
+    size_t operator()(const MapKey& k) const {
+        const uint64_t* w = reinterpret_cast<const uint64_t*>(&k);
+        uint64_t h = 1469598103934665603ull;
+        for (size_t i = 0; i < sizeof(MapKey) / 8; ++i) h = (h ^ w[i]) * 1099511628211ull;
+        return (size_t)h;
+    }
+};
+
+// A 2-D row-major tensor of `rows` x `row_bytes` (elements of dtype), boxes of box0 elements x box1 rows. Cached per
+// host thread (weights are long-lived; a pointer that is freed and reused for a same-shaped tensor gets the same,
+// still valid, descriptor).
+int get_tmap_2d(CUtensorMap* out, const void* ptr, uint64_t rows, uint64_t row_bytes, CUtensorMapDataType dtype,
+                uint32_t elem_bytes, uint32_t box0, uint32_t box1, CUtensorMapSwizzle swz) {
+    thread_local std::unordered_map<MapKey, CUtensorMap, MapKeyHash> cache;
+    MapKey key{};
+    key.ptr = ptr; key.rows = rows; key.row_bytes = row_bytes; key.box0 = box0; key.box1 = box1;
+    key.dtype = (uint32_t)dtype; key.swz = (uint32_t)swz;
+    auto it = cache.find(key);
+    if (it != cache.end()) { *out = it->second; return 0; }
+    EncodeTiledFn enc = encode_fn();
+    if (!enc) return -(int)cudaErrorNotSupported;
+    cuuint64_t dims[2] = {row_bytes / elem_bytes, rows};
+    cuuint64_t strides[1] = {row_bytes};
+    cuuint32_t box[2] = {box0, box1};
+    cuuint32_t estr[2] = {1, 1};
+    CUtensorMap m;
+    const CUresult r = enc(&m, dtype, 2, const_cast<void*>(ptr), dims, strides, box, estr,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return -(int)cudaErrorInvalidValue;
+    if (cache.size() > 65536) cache.clear();
+    cache.emplace(key, m);
+    *out = m;
+    return 0;
+}
+
+// ---- decode / MoE planning ---------------------------------------------------------------------------------------
+
+static int fmt_bits(int fmt) { return fmt == VKB_FMT_Q4 ? 4 : fmt == VKB_FMT_Q8 ? 8 : 2; }
+static int ks_unit(int fmt) { return fmt == VKB_FMT_Q2 ? 512 : 256; }
+
+struct QmvPlan {
+    QmvArgs a;
+    int smem;
+    int grid;
+};
+
+static int round_up(int v, int m) { return (v + m - 1) / m * m; }
+
+// Stage: 16 rows x KS values, about 16 KB of codes; ring as deep as fits, preferring a footprint that lets a second
+// CTA (the next call, under PDL) share the SM.
+static bool plan_qmv(int fmt, int N, int K, int xrows, int moe_slots, int E_local, const DeviceInfo& d, QmvPlan* p) {
+    const int bits = fmt_bits(fmt), unit = ks_unit(fmt);
+    const int ks_max = 8192 / bits;   // 1 KB of codes per row per stage
+    const int nchunks = (K + ks_max - 1) / ks_max;
+    const int KS = round_up((K + nchunks - 1) / nchunks, unit);
+    const int nb = KS * bits / 8 / 128;
+    const int stage_bytes = round_up(nb * QMV_BOX_BYTES + KS, 1024);
+    const int xpitch = round_up(K * 2, 128) + 64;
+    const int xbufs = moe_slots > 0 ? 2 : 1;
+    const int xbytes = round_up(xbufs * xrows * xpitch, 16);
+    const int redbytes = 2 * QMV_NW * 32 * 16;
+    const int moebytes = moe_slots > 0 ? round_up(4 * (3 * E_local + 2 + 2 * moe_slots), 16) : 0;
+    const int slack = 1024;
+    auto fixed_for = [&](int nstage) { return 8 * qmv_nbars(nstage) + xbytes + redbytes + moebytes + slack; };
+    const int pair_budget = d.smem_per_sm / 2 - 1024;   // two CTAs per SM
+    const int solo_budget = d.smem_optin;
+    int nstage = 0, budget = pair_budget;
+    for (int pass = 0; pass < 2; ++pass) {
+        budget = pass == 0 ? pair_budget : solo_budget;
+        nstage = 16;
+        while (nstage >= 2 && nstage * stage_bytes + fixed_for(nstage) > budget) --nstage;
+        if (nstage >= 4 || (pass == 1 && nstage >= 2)) break;
+    }
+    if (nstage < 2) return false;
+    QmvArgs& a = p->a;
+    a.N = N; a.K = K; a.KS = KS; a.nchunks = nchunks; a.nstage = nstage; a.stage_bytes = stage_bytes;
+    a.xpitch = xpitch; a.xrows = xrows; a.tilesN = (N + QMV_ROWS - 1) / QMV_ROWS;
+    a.ring_off = 0;
+    a.x_off = nstage * stage_bytes;
+    a.red_off = a.x_off + xbytes;
+    a.bar_off = a.red_off + redbytes;
+    a.moe_off = a.bar_off + 8 * qmv_nbars(nstage);
+    p->smem = a.moe_off + moebytes + slack;
+    return true;
+}
+
+template <int F, int MODE, typename OutT>
+static int launch_qmv(const QmvPlan& p, const CUtensorMap& tq, const CUtensorMap& ts, int grid, cudaStream_t st,
+                      int dev) {
+    auto kern = qmv_kernel<F, MODE, OutT>;
+    static std::once_flag once[kMaxDevices];
+    static cudaError_t attr_err[kMaxDevices];
+    std::call_once(once[dev], [&] {
+        attr_err[dev] = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             device_info(dev).smem_optin);
+    });
+    if (attr_err[dev] != cudaSuccess) return -(int)attr_err[dev];
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(32 * (QMV_NW + 1));
+    cfg.dynamicSmemBytes = p.smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl_enabled() && pdl_stream_ok(st) ? 1 : 0;
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, tq, ts, p.a);
+    return e == cudaSuccess ? 0 : -(int)e;
+}
+
+template <int F, typename OutT>
+static int launch_simple(const void* q, const void* s, const void* x, void* y, const int32_t* idx, int N, int K,
+                         int M, int topk, int E_local, int e0, int slots, cudaStream_t st) {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3((unsigned)((N + 7) / 8), (unsigned)(idx ? slots : 1));
+    cfg.blockDim = dim3(256);
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl_enabled() && pdl_stream_ok(st) ? 1 : 0;
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, qmv_simple_kernel<F, OutT>, q, (const __half*)s,
+                                             (const __half*)x, (OutT*)y, idx, N, K, M, topk, E_local, e0);
+    return e == cudaSuccess ? 0 : -(int)e;
+}
+
+static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// Common body of the dense and MoE entry points.
+template <int F>
+static int qmv_entry(const void* q, const void* s, const void* x, void* y, bool f32, const int32_t* idx, int N, int K,
+                     int M, int topk, int E_local, int e0, cudaStream_t st) {
+    const bool moe = idx != nullptr;
+    if (!q || !s || !x || !y) return VKB_EINVAL;
+    if (N < 1 || K < 32 || M < 1) return VKB_EINVAL;
+    if (K % 32 != 0) return VKB_EUNSUPPORTED;
+    if (!moe && M > QMV_MAXTOK) return VKB_EUNSUPPORTED;
+    if (moe && (topk < 1 || E_local < 1 || E_local > 32767 || (long long)M * topk > 32767)) return VKB_EUNSUPPORTED;
+    if (F == FMT_Q2 && K % 64 != 0) return VKB_EUNSUPPORTED;
+    const long long rows = moe ? (long long)E_local * N : N;
+    if (rows > (1ll << 31) - 1) return VKB_EUNSUPPORTED;
+    int dev = 0;
+    if (int r = current_device(&dev)) return r;
+    const DeviceInfo& d = device_info(dev);
+    const int slots = moe ? M * topk : 0;
+
+    const bool fast = K % 256 == 0 && aligned16(q) && aligned16(s) && aligned16(x);
+    QmvPlan p{};
+    const int xrows = moe ? (slots < QMV_MAXTOK ? slots : QMV_MAXTOK) : M;
+    if (fast && plan_qmv(F, N, K, xrows, slots, E_local, d, &p)) {
+        constexpr int BITS = FmtTraits<F>::BITS;
+        CUtensorMap tq, ts;
+        int r = get_tmap_2d(&tq, q, (uint64_t)rows, (uint64_t)K * BITS / 8, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, 128,
+                            QMV_ROWS, CU_TENSOR_MAP_SWIZZLE_128B);
+        if (r) return r;
+        r = get_tmap_2d(&ts, s, (uint64_t)rows, (uint64_t)K / 16, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2,
+                        (uint32_t)(p.a.KS / 32), QMV_ROWS, CU_TENSOR_MAP_SWIZZLE_NONE);
+        if (r) return r;
+        p.a.x = (const __half*)x;
+        p.a.y = y;
+        p.a.idx = idx;
+        p.a.T = M;
+        p.a.topk = topk;
+        p.a.E_local = E_local;
+        p.a.e0 = e0;
+        int grid;
+        if (moe) {
+            grid = d.sm_count;
+        } else {
+            grid = p.a.tilesN < d.sm_count ? p.a.tilesN : d.sm_count;
+        }
+        if (moe)
+            return f32 ? launch_qmv<F, QMV_MOE, float>(p, tq, ts, grid, st, dev)
+                       : launch_qmv<F, QMV_MOE, __half>(p, tq, ts, grid, st, dev);
+        return f32 ? launch_qmv<F, QMV_DENSE, float>(p, tq, ts, grid, st, dev)
+                   : launch_qmv<F, QMV_DENSE, __half>(p, tq, ts, grid, st, dev);
+    }
+    // general path: 4-byte aligned words for Q4/Q2, 2-byte aligned fp16
+    if (F != FMT_Q8 && (reinterpret_cast<uintptr_t>(q) & 3u)) return VKB_EUNSUPPORTED;
+    if ((reinterpret_cast<uintptr_t>(s) | reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(y)) & 1u)
+        return VKB_EUNSUPPORTED;
+    return f32 ? launch_simple<F, float>(q, s, x, y, idx, N, K, M, topk, E_local, e0, slots, st)
+               : launch_simple<F, __half>(q, s, x, y, idx, N, K, M, topk, E_local, e0, slots, st);
+}
+
+static int qmv_dispatch(int fmt, const void* q, const void* s, const void* x, void* y, bool f32, const int32_t* idx,
+                        int N, int K, int M, int topk, int E_local, int e0, cudaStream_t st) {
+    switch (fmt) {
+        case VKB_FMT_Q4: return qmv_entry<FMT_Q4>(q, s, x, y, f32, idx, N, K, M, topk, E_local, e0, st);
+        case VKB_FMT_Q8: return qmv_entry<FMT_Q8>(q, s, x, y, f32, idx, N, K, M, topk, E_local, e0, st);
+        case VKB_FMT_Q2: return qmv_entry<FMT_Q2>(q, s, x, y, f32, idx, N, K, M, topk, E_local, e0, st);
+        default: return VKB_EUNSUPPORTED;
+    }
+}
+
+}  // namespace vkb
+
+using namespace vkb;
+
+extern "C" {
+
+int vkb_gemv(int fmt, const void* q, const void* s, const void* x, void* y, int out_f32, int N, int K, int M,
+             vkb_stream_t stream) {
+    return qmv_dispatch(fmt, q, s, x, y, out_f32 != 0, nullptr, N, K, M, 0, 0, 0, (cudaStream_t)stream);
+}
+int vkb_gemv_q4(const void* q, const void* s, const void* x, void* y, int N, int K, int M, vkb_stream_t stream) {
+    return vkb_gemv(VKB_FMT_Q4, q, s, x, y, 0, N, K, M, stream);
+}
+int vkb_gemv_q8(const void* q, const void* s, const void* x, void* y, int N, int K, int M, vkb_stream_t stream) {
+    return vkb_gemv(VKB_FMT_Q8, q, s, x, y, 0, N, K, M, stream);
+}
+int vkb_gemv_q2(const void* q, const void* s, const void* x, void* y, int N, int K, int M, vkb_stream_t stream) {
+    return vkb_gemv(VKB_FMT_Q2, q, s, x, y, 0, N, K, M, stream);
+}
+int vkb_gemv_q4_f32(const void* q, const void* s, const void* x, float* y, int N, int K, int M, vkb_stream_t stream) {
+    return vkb_gemv(VKB_FMT_Q4, q, s, x, y, 1, N, K, M, stream);
+}
+int vkb_gemv_q8_f32(const void* q, const void* s, const void* x, float* y, int N, int K, int M, vkb_stream_t stream) {
+    return vkb_gemv(VKB_FMT_Q8, q, s, x, y, 1, N, K, M, stream);
+}
+int vkb_gemv_q2_f32(const void* q, const void* s, const void* x, float* y, int N, int K, int M, vkb_stream_t stream) {
+    return vkb_gemv(VKB_FMT_Q2, q, s, x, y, 1, N, K, M, stream);
+}
+
+int vkb_moe(int fmt, const void* qpool, const void* spool, const int32_t* idx, int T, int topk, const void* x,
+            void* y, int out_f32, int E_local, int e0, int N, int K, vkb_stream_t stream) {
+    if (!idx) return VKB_EINVAL;
+    return qmv_dispatch(fmt, qpool, spool, x, y, out_f32 != 0, idx, N, K, T, topk, E_local, e0, (cudaStream_t)stream);
+}
+int vkb_moe_q4(const void* qpool, const void* spool, const int32_t* idx, int T, int topk, const void* x, void* y,
+               int E_local, int e0, int N, int K, vkb_stream_t stream) {
+    return vkb_moe(VKB_FMT_Q4, qpool, spool, idx, T, topk, x, y, 0, E_local, e0, N, K, stream);
+}
+
+const char* vkb_strerror(int code) {
+    switch (code) {
+        case VKB_OK: return "ok";
+        case VKB_EUNSUPPORTED: return "unsupported shape, token count or format (nothing launched)";
+        case VKB_EINVAL: return "invalid argument (nothing launched)";
+        case VKB_ENOCOMM: return "no communicator for a multi-GPU call";
+        case VKB_EDEVICE: return "a kernel reported a device-side timeout";
+        default: break;
+    }
+    if (code <= -VKB_NCCL_BASE) return "NCCL error";
+    if (code < 0) return cudaGetErrorString((cudaError_t)(-code));
+    return "unknown vkb status";
+}
+
+int vkb_device_status(unsigned int* bits) {
+    if (!bits) return VKB_EINVAL;
+    cudaError_t e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) return -(int)e;
+    unsigned v = 0;
+    for (auto take : status_accessors())
+        if (int r = take(&v)) return r;
+    *bits = v;
+    return 0;
+}
+
+int vkb_set_pdl(int enable) {
+    const int old = pdl_enabled() ? 1 : 0;
+    t_pdl = enable ? 1 : 0;
+    return old;
+}
+
+int vkb_version(void) { return 100; }
+
+}  // extern "C"

@@ -1,0 +1,40 @@
+// Internal helpers shared by the translation units of libvkb.so (not part of the C ABI).
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace vkb {
+
+constexpr int kMaxDevices = 64;
+
+struct DeviceInfo {
+    int sm_count;
+    int smem_optin;    // max dynamic shared memory per block (opt-in)
+    int smem_per_sm;   // shared memory per SM
+    int cc_major;
+};
+
+// Facts about device `dev`, queried once per process.
+const DeviceInfo& device_info(int dev);
+// The current device, or an error code (see vkb.h).
+int current_device(int* dev);
+// Whether launches on this host thread use programmatic dependent launch.
+bool pdl_enabled();
+// Encode (or fetch from this thread's cache) a 2-D tiled TMA descriptor over a row-major tensor.
+int get_tmap_2d(CUtensorMap* out, const void* ptr, uint64_t rows, uint64_t row_bytes, CUtensorMapDataType dtype,
+                uint32_t elem_bytes, uint32_t box0, uint32_t box1, CUtensorMapSwizzle swz);
+
+// Host accessors of the per-translation-unit device status words (read and clear, OR into *bits).
+using StatusTake = int (*)(unsigned*);
+int status_take_qmv(unsigned* bits);
+struct StatusList {
+    const StatusTake* b;
+    const StatusTake* e;
+    const StatusTake* begin() const { return b; }
+    const StatusTake* end() const { return e; }
+};
+StatusList status_accessors();
+
+}  // namespace vkb

@@ -1,0 +1,222 @@
+"""Python binding of libvkb.so (include/vkb.h, include/vkb_host.h) over ctypes.
+
+Two layers:
+  * the raw C ABI (lib(), plain integers and pointers, return codes) -- what an FFI user of the library sees;
+  * torch-tensor helpers (gemv(), moe(), quantize_pack(), ...) that validate devices, dtypes and shapes, pass the
+    current CUDA stream, and raise VkbError on a non-zero return code.
+
+There is no CPU fallback: every compute call goes to the CUDA kernels in libvkb.so, and importing a compute helper
+without the built library raises.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+import numpy as np
+
+PKG = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+LIB_PATH = os.path.join(PKG, "lib", "libvkb.so")
+
+FMT_Q4, FMT_Q8, FMT_Q2 = 0, 1, 2
+FMT_NAMES = {"q4": FMT_Q4, "q8": FMT_Q8, "q2": FMT_Q2}
+BITS = {FMT_Q4: 4, FMT_Q8: 8, FMT_Q2: 2}
+OK, EUNSUPPORTED, EINVAL, ENOCOMM, EDEVICE = 0, 1, 2, 3, 4
+
+_lib = None
+
+
+class VkbError(RuntimeError):
+    def __init__(self, code: int, where: str = ""):
+        self.code = code
+        super().__init__(f"{where}: vkb error {code}: {strerror(code)}")
+
+
+def lib() -> ctypes.CDLL:
+    """Load libvkb.so (raises if it was not built: there is no fallback)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(LIB_PATH):
+        raise ImportError(f"{LIB_PATH} is missing: build it with python volta-kernel-bakeoff_b200/build.py")
+    L = ctypes.CDLL(LIB_PATH)
+    vp, i, sz = ctypes.c_void_p, ctypes.c_int, ctypes.c_size_t
+    for name in ("vkb_gemv_q4", "vkb_gemv_q8", "vkb_gemv_q2", "vkb_gemv_q4_f32", "vkb_gemv_q8_f32", "vkb_gemv_q2_f32"):
+        f = getattr(L, name)
+        f.argtypes = [vp, vp, vp, vp, i, i, i, vp]
+        f.restype = i
+    L.vkb_gemv.argtypes = [i, vp, vp, vp, vp, i, i, i, i, vp]
+    L.vkb_gemv.restype = i
+    L.vkb_moe_q4.argtypes = [vp, vp, vp, i, i, vp, vp, i, i, i, i, vp]
+    L.vkb_moe_q4.restype = i
+    L.vkb_moe.argtypes = [i, vp, vp, vp, i, i, vp, vp, i, i, i, i, i, vp]
+    L.vkb_moe.restype = i
+    L.vkb_strerror.argtypes = [i]
+    L.vkb_strerror.restype = ctypes.c_char_p
+    L.vkb_device_status.argtypes = [ctypes.POINTER(ctypes.c_uint)]
+    L.vkb_device_status.restype = i
+    L.vkb_set_pdl.argtypes = [i]
+    L.vkb_set_pdl.restype = i
+    L.vkb_version.restype = i
+    L.vkb_quantize.argtypes = [i, vp, i, i, vp, vp]
+    L.vkb_quantize.restype = i
+    L.vkb_pack.argtypes = [i, vp, i, i, i, vp]
+    L.vkb_pack.restype = i
+    L.vkb_packed_bytes.argtypes = [i, i, i]
+    L.vkb_packed_bytes.restype = sz
+    L.vkb_synth_normal.argtypes = [ctypes.c_uint32, sz, ctypes.c_float, vp]
+    L.vkb_synth_normal.restype = i
+    L.vkb_f32_to_f16.argtypes = [vp, sz, vp]
+    L.vkb_f32_to_f16.restype = i
+    L.vkb_synth_topk.argtypes = [ctypes.c_uint32, i, i, i, vp]
+    L.vkb_synth_topk.restype = i
+    _register_optional(L)
+    _lib = L
+    return L
+
+
+def _register_optional(L) -> None:
+    """Entry points added by later parts of the library (bound when present)."""
+    vp, i = ctypes.c_void_p, ctypes.c_int
+    opt = {
+        "vkb_gemm_q4_tc": ([vp, vp, vp, vp, i, i, i, vp], i),
+        "vkb_gemm_q4_tc_f32": ([vp, vp, vp, vp, i, i, i, vp], i),
+        "vkb_dequant_q4": ([vp, vp, vp, i, i, vp], i),
+        "vkb_comm_init": ([i, i, vp, vp], i),
+        "vkb_comm_destroy": ([vp], i),
+        "vkb_comm_unique_id": ([vp], i),
+        "vkb_comm_unique_id_bytes": ([], i),
+        "vkb_moe_q4_ep": ([vp, vp, vp, vp, i, i, vp, vp, i, i, i, vp], i),
+        "vkb_gemm_q4_tc_rowsplit": ([vp, vp, vp, vp, vp, i, i, i, vp, vp], i),
+    }
+    for name, (args, res) in opt.items():
+        if hasattr(L, name):
+            f = getattr(L, name)
+            f.argtypes = args
+            f.restype = res
+
+
+def strerror(code: int) -> str:
+    try:
+        return lib().vkb_strerror(code).decode()
+    except ImportError:
+        return "libvkb.so not loaded"
+
+
+def check(rc: int, where: str = "vkb") -> None:
+    if rc != 0:
+        raise VkbError(rc, where)
+
+
+def device_status() -> int:
+    bits = ctypes.c_uint(0)
+    check(lib().vkb_device_status(ctypes.byref(bits)), "vkb_device_status")
+    return bits.value
+
+
+def set_pdl(enable: bool) -> bool:
+    return bool(lib().vkb_set_pdl(1 if enable else 0))
+
+
+# ---- host-side formats (numpy) ----------------------------------------------------------------------------------
+
+def _p(a: np.ndarray):
+    return ctypes.c_void_p(a.ctypes.data)
+
+
+def synth_normal(seed: int, shape, std: float) -> np.ndarray:
+    out = np.empty(int(np.prod(shape)), np.float32)
+    check(lib().vkb_synth_normal(seed, out.size, std, _p(out)), "vkb_synth_normal")
+    return out.reshape(shape)
+
+
+def to_f16_bits(a: np.ndarray) -> np.ndarray:
+    a = np.ascontiguousarray(a, dtype=np.float32)
+    out = np.empty(a.shape, np.uint16)
+    check(lib().vkb_f32_to_f16(_p(a), a.size, _p(out)), "vkb_f32_to_f16")
+    return out
+
+
+def quantize(fmt: int, w: np.ndarray):
+    """fp32 [N][K] -> (codes int8 [N][K], scales uint16 fp16 bits [N][K/32])."""
+    w = np.ascontiguousarray(w, dtype=np.float32)
+    N, K = w.shape
+    codes = np.empty((N, K), np.int8)
+    scales = np.empty((N, K // 32), np.uint16)
+    check(lib().vkb_quantize(fmt, _p(w), N, K, _p(codes), _p(scales)), "vkb_quantize")
+    return codes, scales
+
+
+def pack(fmt: int, codes: np.ndarray, sabotage: bool = False) -> np.ndarray:
+    codes = np.ascontiguousarray(codes, dtype=np.int8)
+    N, K = codes.shape
+    if fmt == FMT_Q8:
+        out = np.empty((N, K), np.int8)
+    else:
+        out = np.empty((N, K * BITS[fmt] // 32), np.uint32)
+    check(lib().vkb_pack(fmt, _p(codes), N, K, int(sabotage), _p(out)), "vkb_pack")
+    return out
+
+
+def synth_topk(seed: int, T: int, E: int, k: int) -> np.ndarray:
+    idx = np.empty((T, k), np.int32)
+    check(lib().vkb_synth_topk(seed, T, E, k, _p(idx)), "vkb_synth_topk")
+    return idx
+
+
+# ---- torch helpers ----------------------------------------------------------------------------------------------
+
+def _torch():
+    import torch
+    return torch
+
+
+def _stream(stream=None) -> ctypes.c_void_p:
+    torch = _torch()
+    s = stream if stream is not None else torch.cuda.current_stream()
+    return ctypes.c_void_p(s.cuda_stream)
+
+
+def _ptr(t) -> ctypes.c_void_p:
+    return ctypes.c_void_p(t.data_ptr())
+
+
+def gemv(fmt: int, q, s, x, y=None, out_f32: bool = False, stream=None):
+    """y[M][N] = x[M][K] . W[N][K]^T for M <= 8. q: packed codes (uint8/int8/int32 storage), s: fp16 [N][K/32],
+    x: fp16 [M][K] on the same CUDA device. Returns y (fp16, or fp32 with out_f32)."""
+    torch = _torch()
+    M, K = x.shape
+    N = s.shape[0]
+    if y is None:
+        y = torch.empty((M, N), dtype=torch.float32 if out_f32 else torch.float16, device=x.device)
+    rc = lib().vkb_gemv(fmt, _ptr(q), _ptr(s), _ptr(x), _ptr(y), int(out_f32), N, K, M, _stream(stream))
+    check(rc, "vkb_gemv")
+    return y
+
+
+def moe(fmt: int, qpool, spool, idx, x, y=None, E_local: int | None = None, e0: int = 0, out_f32: bool = False,
+        stream=None):
+    """MoE decode: qpool [E_local][N][...], spool [E_local][N][K/32] fp16, idx int32 [T][topk], x fp16 [T][K] ->
+    y [T][topk][N] (slots of non-local experts untouched)."""
+    torch = _torch()
+    E, N = spool.shape[0], spool.shape[1]
+    T, topk = idx.shape
+    K = x.shape[1]
+    if y is None:
+        y = torch.zeros((T, topk, N), dtype=torch.float32 if out_f32 else torch.float16, device=x.device)
+    rc = lib().vkb_moe(fmt, _ptr(qpool), _ptr(spool), _ptr(idx), T, topk, _ptr(x), _ptr(y), int(out_f32),
+                       E if E_local is None else E_local, e0, N, K, _stream(stream))
+    check(rc, "vkb_moe")
+    return y
+
+
+def to_device_packed(packed: np.ndarray, device="cuda"):
+    """numpy packed codes -> a torch uint8 tensor with the same bytes (kept 2-D: [rows][bytes per row])."""
+    torch = _torch()
+    b = np.ascontiguousarray(packed).view(np.uint8).reshape(packed.shape[0], -1)
+    return torch.from_numpy(b.copy()).to(device)
+
+
+def to_device_f16(bits: np.ndarray, device="cuda"):
+    torch = _torch()
+    return torch.from_numpy(np.ascontiguousarray(bits).view(np.int16).copy()).to(device).view(torch.float16)
