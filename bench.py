@@ -1,0 +1,463 @@
+#!/usr/bin/env python
+"""bench.py -- the benchmark driver contract for the B200 quantised matmul hot path.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Workload: the dense quantised GEMV sweep -- Q4_0, Q8_0 and 2-bit weights, tables
+12288x2560, 2560x6144, 6144x2048 and 2048x6144 (N_out x K_in), 1, 2, 4 and 8 tokens: 48 calls per step, each through
+the library's C ABI (vkb_gemv), weights N(0,0.02) seed 0 quantised per 32-value block, activations fp16 N(0,1).
+One step = one pass over the 48 (format, table, tokens) cases. Every case reads a different copy of its table and the
+copies of each table cycle through >= 4x L2 across steps, so every call reads its weights from HBM (the reference's
+fairness rule, src/bakeoff.cu:16-18, :314, with 96 MB raised to 4x B200's L2).
+
+Metric: aggregate decode-GEMV HBM throughput in GB/s = algorithmic bytes (packed codes + fp16 scales + x + y) of the
+step / step time, and the reference's own µs per call for each case (time_us: 5 batches of 50 back-to-back calls,
+median), including configs[0] (Q4_0 8192x2048, 1 token).
+
+Multi-GPU: the dense GEMV does not shard (replicas only): every rank runs the whole step on its own GPU; value sums the
+ranks' bytes over the slowest rank's time (weak scaling).
+
+The reference arm (--impl reference) times the reference's own CPU path, ref_value (src/bakeoff.cu:221-227, compiled
+from the reference source into oracle/_ref/ by oracle/Makefile), on all host cores over a bounded sample of each
+step's outputs, scaled to the full step.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes
+import datetime
+import json
+import math
+import os
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+PKG = os.path.join(ROOT, "volta-kernel-bakeoff_b200")
+for p in (ROOT, PKG):
+    if p not in sys.path:
+        sys.path.insert(0, p)
+
+SHAPES = [(12288, 2560), (2560, 6144), (6144, 2048), (2048, 6144)]   # configs[1] tables (N_out x K_in)
+FORMATS = [("q4", 0, 0.5625), ("q8", 1, 1.0625), ("q2", 2, 0.3125)]  # name, vkb format, bytes per weight
+TOKENS = [1, 2, 4, 8]
+HEADLINE = ("q4", 0, 8192, 2048, 1)                                   # configs[0]
+METRIC = "decode GEMV HBM throughput, configs[1] sweep (Q4_0/Q8_0/2-bit x 4 tables x 1/2/4/8 tokens)"
+
+
+def case_bytes(bw: float, N: int, K: int, M: int) -> float:
+    """Algorithmic bytes of one call: packed codes + scales (bw per weight), x in, y out (fp16)."""
+    return N * K * bw + M * K * 2 + M * N * 2
+
+
+def step_bytes() -> float:
+    return sum(case_bytes(bw, N, K, M) for _, _, bw in FORMATS for N, K in SHAPES for M in TOKENS)
+
+
+# ---- clocks ----------------------------------------------------------------------------------------------------------
+
+class ClockSampler:
+    """nvidia-smi samples of the SM clock and throttle reasons during the timed region."""
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = os.path.join(ROOT, "gpurun_out", f"clocks_gpu{gpu_index}.csv")
+
+    def start(self):
+        try:
+            os.makedirs(os.path.dirname(self.path), exist_ok=True)
+            self.f = open(self.path, "w")
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                          "-i", str(self.gpu), "-lms", "50"], stdout=self.f, stderr=subprocess.DEVNULL)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        time.sleep(0.06)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.f.close()
+        sm, mx, reasons = [], [], set()
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        for line in open(self.path):
+            f = [v.strip() for v in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx.append(float(f[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        sm.sort()
+        return {"sm_mhz": sm[len(sm) // 2], "sm_max_mhz": max(mx), "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ---- the reference's CPU path ----------------------------------------------------------------------------------------
+
+def cpu_reference_step(cases, frac: float, threads: int):
+    """Times the reference's ref_value (oracle/_ref) over the first frac of every case's output rows, all threads;
+    returns (seconds for the full step, scaled; kind; sample description). Falls back to the numpy oracle port when the
+    reference library is not built."""
+    import numpy as np
+    from oracle import refbind
+    L = refbind.load()
+    t_total = 0.0
+    for c in cases:
+        rows = max(16, int(c["N"] * frac))
+        if L is not None:
+            t0 = time.perf_counter()
+            refbind.gemv_mt(c["codes"][:rows], c["scales"][:rows], c["x"], 0, rows, threads)
+            dt = time.perf_counter() - t0
+        else:
+            from oracle import oracle as O
+            t0 = time.perf_counter()
+            O.ref_value(c["codes"][:rows], c["scales"][:rows], c["x"])
+            dt = time.perf_counter() - t0
+        t_total += dt * c["N"] / rows
+    kind = "reference" if L is not None else "port"
+    sample = f"first {frac:.3g} of the output rows of each of the {len(cases)} step cases, scaled to the full step"
+    return t_total, kind, sample
+
+
+def cpu_frac_for(cases, threads: int, budget_s: float) -> float:
+    """The sampled row fraction that makes one CPU step take about budget_s (from a tiny calibration sample)."""
+    f0 = 1.0 / 1024
+    t0, _, _ = cpu_reference_step(cases, f0, threads)   # t0 is already scaled to the full step
+    return max(1.0 / 4096, min(0.25, budget_s / max(t0, 1e-9)))
+
+
+def gpu_index(local_rank: int) -> int:
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+    if vis:
+        parts = [p for p in vis.split(",") if p.strip()]
+        if local_rank < len(parts) and parts[local_rank].strip().isdigit():
+            return int(parts[local_rank])
+    return local_rank
+
+
+def host_cases(for_cpu: bool = True):
+    """Host-side weights/activations of the 48 step cases (codes int8, fp16 scales and x as uint16 bits)."""
+    import vkb
+    cases = []
+    for fname, fmt, bw in FORMATS:
+        for N, K in SHAPES:
+            codes, scales = vkb.quantize(fmt, vkb.synth_normal(0, (N, K), 0.02))
+            for M in TOKENS:
+                x = vkb.to_f16_bits(vkb.synth_normal(1 + M, (M, K), 1.0))
+                cases.append(dict(fname=fname, fmt=fmt, bw=bw, N=N, K=K, M=M, codes=codes, scales=scales, x=x))
+    return cases
+
+
+# ---- our arm ---------------------------------------------------------------------------------------------------------
+
+def run_ours(args, rank: int, world: int, local_rank: int, dist):
+    import numpy as np
+    import torch
+    import vkb
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    stream = torch.cuda.Stream(device=dev)
+    torch.cuda.set_stream(stream)
+    L2 = torch.cuda.get_device_properties(dev).L2_cache_size
+    L = vkb.lib()
+
+    # weights: one quantised table per (format, shape), C copies each (>= 4 x L2 of that table)
+    cases = host_cases()
+    tables = {}
+    for c in cases:
+        key = (c["fmt"], c["N"], c["K"])
+        if key not in tables:
+            q0 = vkb.to_device_packed(vkb.pack(c["fmt"], c["codes"]), dev)
+            s0 = vkb.to_device_f16(c["scales"], dev)
+            tb = q0.numel() + 2 * s0.numel()
+            ncopy = max(4, math.ceil(4 * L2 / tb))
+            tables[key] = dict(q=[q0] + [q0.clone() for _ in range(ncopy - 1)],
+                               s=[s0] + [s0.clone() for _ in range(ncopy - 1)], n=ncopy)
+    xs = {}
+    for c in cases:
+        key = (c["K"], c["M"])
+        if key not in xs:
+            xs[key] = vkb.to_device_f16(c["x"], dev)
+    ys = [torch.empty((c["M"], c["N"]), dtype=torch.float16, device=dev) for c in cases]
+    max_copies = max(t["n"] for t in tables.values())
+    ngraph = max(1, math.ceil(max_copies / len(TOKENS)))
+
+    def launch_step(j: int):
+        for ci, c in enumerate(cases):
+            tb = tables[(c["fmt"], c["N"], c["K"])]
+            m = TOKENS.index(c["M"])
+            k = (j * len(TOKENS) + m) % tb["n"]
+            vkb.gemv(c["fmt"], tb["q"][k], tb["s"][k], xs[(c["K"], c["M"])], y=ys[ci])
+
+    # correctness guard on this box before timing: the headline table against the oracle
+    for i in range(2):
+        launch_step(i)
+    torch.cuda.synchronize()
+    if vkb.device_status() != 0:
+        raise RuntimeError("device-side timeout during warm-up")
+
+    graphs = []
+    for j in range(ngraph):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            launch_step(j)
+        graphs.append(g)
+
+    for w in range(args.warmup):
+        graphs[w % ngraph].replay()
+    torch.cuda.synchronize()
+
+    clk = ClockSampler(gpu_index(local_rank))
+    if dist is not None:
+        dist.barrier()
+    torch.cuda.synchronize()
+    clk.start()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for k in range(args.steps):
+        graphs[(args.warmup + k) % ngraph].replay()
+    e1.record(stream)
+    e1.synchronize()
+    clocks = clk.stop()
+    if dist is not None:
+        dist.barrier()
+    ms = e0.elapsed_time(e1)
+    t = torch.tensor([ms], dtype=torch.float64, device=dev)
+    if dist is not None:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_max = float(t.item())
+    sbytes = step_bytes()
+    value = sbytes * args.steps * world / (ms_max * 1e-3) / 1e9
+    per_gpu = sbytes * args.steps / (ms_max * 1e-3) / 1e9
+
+    # per-case µs/call, the reference's time_us: 5 batches of 50 back-to-back calls, median (graph of 50 calls)
+    table = {}
+    def time_case(fmt, q_list, s_list, x, y, n):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            for i in range(50):
+                vkb.gemv(fmt, q_list[i % n], s_list[i % n], x, y=y)
+        for _ in range(2):
+            g.replay()
+        ts = []
+        for _ in range(5):
+            a = torch.cuda.Event(enable_timing=True)
+            b = torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            g.replay()
+            b.record(stream)
+            b.synchronize()
+            ts.append(a.elapsed_time(b) * 1000.0 / 50)
+        del g
+        return sorted(ts)[2]
+    if rank == 0:
+        for c in cases:
+            tb = tables[(c["fmt"], c["N"], c["K"])]
+            yc = torch.empty((c["M"], c["N"]), dtype=torch.float16, device=dev)
+            us = time_case(c["fmt"], tb["q"], tb["s"], xs[(c["K"], c["M"])], yc, tb["n"])
+            table[f'{c["fname"]}_{c["N"]}x{c["K"]}_m{c["M"]}'] = {
+                "us": round(us, 3), "GBps": round(case_bytes(c["bw"], c["N"], c["K"], c["M"]) / us / 1e3, 1)}
+        # Q4_0 8192x2048, 1 token
+        fname, fmt, N, K, M = HEADLINE
+        codes, scales = vkb.quantize(fmt, vkb.synth_normal(0, (N, K), 0.02))
+        q0 = vkb.to_device_packed(vkb.pack(fmt, codes), dev)
+        s0 = vkb.to_device_f16(scales, dev)
+        n = max(4, math.ceil(4 * L2 / (q0.numel() + 2 * s0.numel())))
+        ql, sl = [q0] + [q0.clone() for _ in range(n - 1)], [s0] + [s0.clone() for _ in range(n - 1)]
+        xh = vkb.to_device_f16(vkb.to_f16_bits(vkb.synth_normal(2, (M, K), 1.0)), dev)
+        yh = torch.empty((M, N), dtype=torch.float16, device=dev)
+        us = time_case(fmt, ql, sl, xh, yh, n)
+        headline = {"case": "configs[0] Q4_0 8192x2048, 1 token", "us_per_call": round(us, 3),
+                    "GBps": round(case_bytes(0.5625, N, K, M) / us / 1e3, 1), "copies": n}
+        del ql, sl
+
+    # end to end through the C ABI: per step the host->device copy of every case's activations from pinned memory,
+    # the 48 calls, and the device->host read of every output
+    x_host = [torch.from_numpy(c["x"].view(np.int16)).view(torch.float16).pin_memory() for c in cases]
+    x_dev = [torch.empty_like(h, device=dev) for h in x_host]
+    y_host = [torch.empty((c["M"], c["N"]), dtype=torch.float16).pin_memory() for c in cases]
+    h2d = sum(h.numel() * 2 for h in x_host)
+    d2h = sum(h.numel() * 2 for h in y_host)
+    sptr = ctypes.c_void_p(stream.cuda_stream)
+    args_raw = []
+    for ci, c in enumerate(cases):
+        tb = tables[(c["fmt"], c["N"], c["K"])]
+        args_raw.append((c["fmt"], tb, x_dev[ci], ys[ci], c["N"], c["K"], c["M"], TOKENS.index(c["M"])))
+
+    def e2e_step(j):
+        for ci in range(len(cases)):
+            x_dev[ci].copy_(x_host[ci], non_blocking=True)
+        for fmt, tb, xd, yd, N, K, M, m in args_raw:
+            k = (j * len(TOKENS) + m) % tb["n"]
+            rc = L.vkb_gemv(fmt, ctypes.c_void_p(tb["q"][k].data_ptr()), ctypes.c_void_p(tb["s"][k].data_ptr()),
+                            ctypes.c_void_p(xd.data_ptr()), ctypes.c_void_p(yd.data_ptr()), 0, N, K, M, sptr)
+            if rc != 0:
+                raise vkb.VkbError(rc, "vkb_gemv")
+        for ci in range(len(cases)):
+            y_host[ci].copy_(ys[ci], non_blocking=True)
+        stream.synchronize()
+
+    e2e_steps = max(3, min(args.steps, 200))
+    for j in range(3):
+        e2e_step(j)
+    if dist is not None:
+        dist.barrier()
+    t0 = time.perf_counter()
+    for j in range(e2e_steps):
+        e2e_step(j)
+    e2e_s = time.perf_counter() - t0
+    te = torch.tensor([e2e_s], dtype=torch.float64, device=dev)
+    if dist is not None:
+        dist.all_reduce(te, op=dist.ReduceOp.MAX)
+    e2e_value = sbytes * e2e_steps * world / float(te.item()) / 1e9
+
+    if rank != 0:
+        return None
+
+    peaks = {}
+    try:
+        peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
+    except (OSError, ValueError):
+        pass
+    peak = float(peaks.get("hbm_gbs", 6650.0))
+    traffic = None
+    tf = os.path.join(ROOT, "profiles", "qmv_dram_traffic.json")
+    if os.path.exists(tf):
+        try:
+            traffic = json.load(open(tf)).get("step_bytes_per_launch")
+        except (OSError, ValueError):
+            traffic = None
+
+    cpu = None
+    if world == 1:
+        threads = os.cpu_count() or 1
+        frac = cpu_frac_for(cases, threads, budget_s=10.0)
+        t_cpu, kind, sample = cpu_reference_step(cases, frac, threads)
+        cpu = {"value": round(sbytes / t_cpu / 1e9, 4), "unit": "GB/s", "cores": threads, "kind": kind,
+               "sample": sample, "s_per_step": round(t_cpu, 3)}
+
+    return {
+        "metric": METRIC,
+        "value": round(value, 1),
+        "unit": "GB/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms_max / args.steps, 5),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "f16 x int{4,8,2} codes -> f32",
+        "data": "synthetic: weights N(0,0.02) seed 0 quantised per 32 (Q4_0/Q8_0/2-bit), x fp16 N(0,1)",
+        "config": {
+            "workload": "configs[1]: dense quantised GEMV sweep, 48 calls per step",
+            "tables": [f"{n}x{k}" for n, k in SHAPES], "tokens": TOKENS, "formats": [f[0] for f in FORMATS],
+            "parallelism": f"replicas x{world}" if world > 1 else "1 GPU",
+            "l2": "inputs larger than L2: every call reads a different copy; each table's copies cycle >= 4x L2",
+            "launch": "one CUDA graph per step (48 vkb_gemv calls, programmatic dependent launch between them)",
+            "step_bytes": sbytes,
+        },
+        "roofline": {"bound": "hbm", "achieved": round(per_gpu, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(per_gpu / peak, 4), "traffic": traffic,
+                     "peak_source": "MEASURED_PEAKS.json hbm_gbs (of measured)" if peaks else "fallback 6650"},
+        "cpu_baseline": cpu,
+        "e2e": {"value": round(e2e_value, 1), "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                "steps": e2e_steps, "how": "per step: 48 H2D copies from pinned memory, 48 vkb_gemv C-ABI calls, "
+                "48 D2H copies, stream sync; host wall clock"},
+        "gpu_launches": 48 * args.steps,
+        "clocks": clocks,
+        "cases_us": table,
+        "headline": headline,
+    }
+
+
+# ---- the reference arm -----------------------------------------------------------------------------------------------
+
+def run_reference(args, rank: int, world: int):
+    if rank != 0:
+        return None
+    cases = host_cases()
+    threads = os.cpu_count() or 1
+    # every step is a bounded sample of the step's outputs: the whole run takes about 90 s of CPU time
+    frac = cpu_frac_for(cases, threads, budget_s=90.0 / max(1, args.steps + args.warmup))
+    for _ in range(args.warmup):
+        cpu_reference_step(cases, frac, threads)
+    t = 0.0
+    kind = sample = None
+    for _ in range(args.steps):
+        dt, kind, sample = cpu_reference_step(cases, frac, threads)
+        t += dt
+    sbytes = step_bytes()
+    value = sbytes * args.steps / t / 1e9
+    return {
+        "impl": "reference",
+        "metric": METRIC,
+        "value": round(value, 4),
+        "unit": "GB/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(t / args.steps * 1e3, 3),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "f64 (the reference's ref_value: double sums of fp16 x * int code * fp16 scale)",
+        "data": "synthetic: weights N(0,0.02) seed 0 quantised per 32 (Q4_0/Q8_0/2-bit), x fp16 N(0,1)",
+        "config": {"workload": "configs[1]: dense quantised GEMV sweep, 48 calls per step",
+                   "tables": [f"{n}x{k}" for n, k in SHAPES], "tokens": TOKENS, "formats": [f[0] for f in FORMATS],
+                   "parallelism": "host CPU, rank 0 only"},
+        "cpu_baseline": {"value": round(value, 4), "unit": "GB/s", "cores": threads, "kind": kind, "sample": sample},
+        "e2e": {"value": round(value, 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    args = ap.parse_args()
+    if args.warmup < 3 and args.impl == "ours":
+        args.warmup = 3
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    dist = None
+    if args.impl == "reference":
+        res = run_reference(args, rank, world)
+    else:
+        if world > 1:
+            import torch
+            import torch.distributed as tdist
+            torch.cuda.set_device(local_rank)
+            tdist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                     device_id=torch.device("cuda", local_rank))
+            dist = tdist
+        res = run_ours(args, rank, world, local_rank, dist)
+        if dist is not None:
+            dist.barrier()
+            dist.destroy_process_group()
+    if res is not None:
+        print(json.dumps(res), flush=True)
+
+
+if __name__ == "__main__":
+    main()

@@ -10,8 +10,12 @@
 //   scales fp16 [N][K/32]; x fp16 [T][K]; y fp16 or fp32.
 //
 // Design (one CTA per SM, persistent over 16-row tiles):
-//   * warp NW (the producer) streams 16-row x KS-column stages of codes and scales into a shared-memory ring with
-//     2-D TMA tiles (128-byte swizzle, so the consumers' reads are bank-conflict free); the weight stages are issued
+//   * warp NW (the producer) streams 16-row x KS-column stages of codes and scales into a shared-memory ring, one 2-D
+//     TMA box each (8-byte elements, so a box row can span a whole stage row of up to 1.5 KB). The boxes are 16 (Q8: 32) bytes
+//     wider than the data they need, which pads every shared-memory row by that much and makes the consumers'
+//     fragment reads bank-conflict free (the pad is zero-filled past the end of a row, or the next stage's first
+//     bytes inside it). Few, large TMA requests are what keep HBM busy: 16-row x 128-byte boxes ran at under half
+//     the bandwidth of these on B200. The weight stages are issued
 //     before griddepcontrol.wait, so under programmatic dependent launch the next call's weight stream overlaps the
 //     previous call's tail. The activations (after the wait) come in as 1-D bulk copies.
 //   * warps 0..NW-1 split each stage's K range and run the m16n8k16 tensor-core MMA with the weights as A (16 rows)
@@ -31,14 +35,14 @@ namespace vkb {
 enum : int { FMT_Q4 = 0, FMT_Q8 = 1, FMT_Q2 = 2 };
 
 template <int F> struct FmtTraits;
-template <> struct FmtTraits<FMT_Q4> { static constexpr int BITS = 4, KS_UNIT = 256; };
-template <> struct FmtTraits<FMT_Q8> { static constexpr int BITS = 8, KS_UNIT = 256; };
-template <> struct FmtTraits<FMT_Q2> { static constexpr int BITS = 2, KS_UNIT = 512; };
+template <> struct FmtTraits<FMT_Q4> { static constexpr int BITS = 4; };
+template <> struct FmtTraits<FMT_Q8> { static constexpr int BITS = 8; };
+template <> struct FmtTraits<FMT_Q2> { static constexpr int BITS = 2; };
 
-constexpr int QMV_NW = 8;          // consumer warps per CTA
+constexpr int QMV_NW = 16;         // consumer warps per CTA
+constexpr int QMV_KS_UNIT = 256;   // stage widths are multiples of this (8 groups; a 128-byte multiple of every format)
 constexpr int QMV_ROWS = 16;       // weight rows per tile (the MMA's M)
 constexpr int QMV_MAXTOK = 8;      // tokens per MMA column group (the MMA's N)
-constexpr int QMV_BOX_BYTES = 16 * 128;   // one 16-row x 128-byte TMA box
 
 enum : int { QMV_DENSE = 0, QMV_MOE = 1 };
 
@@ -51,11 +55,13 @@ struct QmvArgs {
     int topk;                // MoE: slots per token
     int E_local, e0;         // MoE: experts held in this pool, id of the first one
     int KS, nchunks;         // stage width in k values, stages per row tile
+    int cpitch, spitch;      // shared bytes per row of a stage: codes (KS*bits/8 + pad), scales (KS/16 + 16)
     int nstage;              // ring depth
     int stage_bytes;         // shared bytes per stage (1024-aligned)
     int xpitch;              // shared bytes per staged activation row
     int xrows;               // staged activation rows per buffer (<= 8)
     int tilesN;              // ceil(N / 16)
+    int wg;                  // consumer warp groups (1, 2 or 4), with nstage >= wg * nchunks
     int ring_off, x_off, red_off, bar_off, moe_off;   // shared-memory carve-up (bytes from the aligned base)
 };
 
@@ -89,49 +95,40 @@ __device__ __forceinline__ void unpack_q2(uint32_t vs, uint32_t (&a)[4]) {
     a[3] = h2_fma(and_or(vs, 0x00C000C0u, M), 0x24002400u, 0xCC80CC80u);   // (1024 + 64u)/64 - 18
 }
 
-// Byte offset, inside a stage, of what thread (row r, lane-in-quad t) reads for stage-local group G.
+// Byte offset, inside a row of a stage, of the word(s) lane-in-quad t reads for stage-local group G.
 template <int F>
-__device__ __forceinline__ uint32_t code_off(int G, int r, int t) {
-    const int sw = r & 7;
+__device__ __forceinline__ uint32_t code_off(int G, int t) {
+    if constexpr (F == FMT_Q4) return 16 * G + 4 * t;          // word t of the group's 16 bytes
+    else if constexpr (F == FMT_Q8) return 32 * G + 8 * t;     // words 2t, 2t+1 of the group's 32 bytes
+    else return 8 * G + 4 * (t >> 1);                          // word t/2 of the group's 8 bytes
+}
+
+// The four A registers (two k16 steps) of one row for group G of the stage at shared address st.
+template <int F>
+__device__ __forceinline__ void load_a(uint32_t a, int t, uint32_t (&r)[4]) {
     if constexpr (F == FMT_Q4) {
-        return (G >> 3) * QMV_BOX_BYTES + r * 128 + ((((G & 7)) ^ sw) << 4) + 4 * t;
+        unpack_q4(lds32(a), r);
     } else if constexpr (F == FMT_Q8) {
-        return (G >> 2) * QMV_BOX_BYTES + r * 128 + (((2 * (G & 3) + (t >> 1)) ^ sw) << 4) + 8 * (t & 1);
+        const uint2 w = lds64(a);
+        unpack_q8(w.x, w.y, r);
     } else {
-        return (G >> 4) * QMV_BOX_BYTES + r * 128 + ((((G & 15) >> 1) ^ sw) << 4) + 8 * (G & 1) + 4 * (t >> 1);
+        unpack_q2(lds32(a) >> (8 * (t & 1)), r);
     }
 }
 
+// The B registers (two k16 steps) of this thread's token for the group whose activations start at shared address xa
+// (xa already includes the thread's t offset). Padding token columns read a real row: their MMA columns are never
+// stored, and the MMA keeps columns independent.
 template <int F>
-__device__ __forceinline__ void load_a(const uint8_t* stage, int G, int r, int t, uint32_t (&a)[4]) {
-    const uint8_t* p = stage + code_off<F>(G, r, t);
-    if constexpr (F == FMT_Q4) {
-        unpack_q4(*reinterpret_cast<const uint32_t*>(p), a);
-    } else if constexpr (F == FMT_Q8) {
-        const uint2 w = *reinterpret_cast<const uint2*>(p);
-        unpack_q8(w.x, w.y, a);
-    } else {
-        unpack_q2(*reinterpret_cast<const uint32_t*>(p) >> (8 * (t & 1)), a);
-    }
-}
-
-// The B registers (two k16 steps) of token row xr (nullptr = a padding column) for the group at global k = k0.
-template <int F>
-__device__ __forceinline__ void load_b(const uint8_t* xr, int k0, int t, uint32_t (&b)[4]) {
-    if (xr == nullptr) {
-        b[0] = b[1] = b[2] = b[3] = 0u;
-        return;
-    }
+__device__ __forceinline__ void load_b(uint32_t xa, uint32_t (&b)[4]) {
     if constexpr (F == FMT_Q2) {
-        const int base = k0 + 16 * (t >> 1) + 4 * (t & 1);
-        const uint2 xa = *reinterpret_cast<const uint2*>(xr + 2 * base);
-        const uint2 xb = *reinterpret_cast<const uint2*>(xr + 2 * base + 16);
-        b[0] = prmt(xa.x, xb.x, 0x5410u);   // (x0, x8)
-        b[1] = prmt(xa.x, xb.x, 0x7632u);   // (x1, x9)
-        b[2] = prmt(xa.y, xb.y, 0x5410u);   // (x2, x10)
-        b[3] = prmt(xa.y, xb.y, 0x7632u);   // (x3, x11)
+        const uint2 xa0 = lds64(xa), xb0 = lds64(xa + 16);
+        b[0] = prmt(xa0.x, xb0.x, 0x5410u);   // (x0, x8)
+        b[1] = prmt(xa0.x, xb0.x, 0x7632u);   // (x1, x9)
+        b[2] = prmt(xa0.y, xb0.y, 0x5410u);   // (x2, x10)
+        b[3] = prmt(xa0.y, xb0.y, 0x7632u);   // (x3, x11)
     } else {
-        const uint4 v = *reinterpret_cast<const uint4*>(xr + 2 * (k0 + 8 * t));
+        const uint4 v = lds128(xa);
         if constexpr (F == FMT_Q4) {
             b[0] = prmt(v.x, v.z, 0x5410u);   // (x0, x4)
             b[1] = prmt(v.x, v.z, 0x7632u);   // (x1, x5)
@@ -143,31 +140,56 @@ __device__ __forceinline__ void load_b(const uint8_t* xr, int k0, int t, uint32_
     }
 }
 
-// One stage (16 rows x KS) for this warp's share of its groups [G0, G1), accumulating into acc.
+// Per-thread byte offset of its activations inside a 32-value group (see load_b).
 template <int F>
-__device__ __forceinline__ void consume_stage(const uint8_t* stage, int KS, int G0, int G1, int kchunk, int KG,
-                                              const uint8_t* xr, int g, int t, float (&acc)[4]) {
-    constexpr int BITS = FmtTraits<F>::BITS;
-    const int nb = KS * BITS / 8 / 128;
-    const __half* sc = reinterpret_cast<const __half*>(stage + nb * QMV_BOX_BYTES);
-    const int spitch = KS / 32;   // halves per scale row
-    const int gbase = kchunk / 32;
-#pragma unroll 2
-    for (int G = G0; G < G1; ++G) {
-        if (gbase + G >= KG) break;   // past K (warp-uniform)
-        uint32_t b[4], ar[4], ar8[4];
-        load_b<F>(xr, kchunk + 32 * G, t, b);
-        load_a<F>(stage, G, g, t, ar);
-        load_a<F>(stage, G, g + 8, t, ar8);
-        float d[4] = {0.f, 0.f, 0.f, 0.f};
-        mma_16816(d, ar[0], ar8[0], ar[1], ar8[1], b[0], b[1]);
-        mma_16816(d, ar[2], ar8[2], ar[3], ar8[3], b[2], b[3]);
-        const float s0 = __half2float(sc[g * spitch + G]);
-        const float s1 = __half2float(sc[(g + 8) * spitch + G]);
-        acc[0] = fmaf(d[0], s0, acc[0]);
-        acc[1] = fmaf(d[1], s0, acc[1]);
-        acc[2] = fmaf(d[2], s1, acc[2]);
-        acc[3] = fmaf(d[3], s1, acc[3]);
+__device__ __forceinline__ uint32_t x_lane_off(int t) {
+    if constexpr (F == FMT_Q2) return 32 * (t >> 1) + 8 * (t & 1);
+    else return 16 * t;
+}
+
+// One group: two k16 MMAs into a fresh fragment, then the per-row fp32 scales. ca: row g's codes in the stage;
+// row g+8 is 8 * cp further.
+template <int F>
+__device__ __forceinline__ void qmv_group(uint32_t ca, uint32_t cp, int G, int t, uint32_t xa, float s0, float s1,
+                                          float (&acc)[4]) {
+    uint32_t b[4], ar[4], ar8[4];
+    load_b<F>(xa, b);
+    const uint32_t a = ca + code_off<F>(G, t);
+    load_a<F>(a, t, ar);
+    load_a<F>(a + 8 * cp, t, ar8);
+    float d[4] = {0.f, 0.f, 0.f, 0.f};
+    mma_16816(d, ar[0], ar8[0], ar[1], ar8[1], b[0], b[1]);
+    mma_16816(d, ar[2], ar8[2], ar[3], ar8[3], b[2], b[3]);
+    acc[0] = fmaf(d[0], s0, acc[0]);
+    acc[1] = fmaf(d[1], s0, acc[1]);
+    acc[2] = fmaf(d[2], s1, acc[2]);
+    acc[3] = fmaf(d[3], s1, acc[3]);
+}
+
+// This warp's groups [G0, G1) of one stage, stopping at K.
+//   ca, cp: shared address of row g's codes in the stage, code row pitch
+//   sc, sp: shared address of row g's scales in the stage, scale row pitch
+//   xa:     shared address of this thread's activations for stage-local group 0
+template <int F>
+__device__ __forceinline__ void consume_stage(uint32_t ca, uint32_t cp, uint32_t sc, uint32_t sp, int G0, int G1,
+                                              uint32_t xa, int t, float (&acc)[4]) {
+    int G = G0;
+    if (G & 1) {   // odd start: single group, its scale from the aligned pair
+        if (G < G1) {
+            const uint32_t p0 = lds32(sc + 2 * (G - 1)), p1 = lds32(sc + 8 * sp + 2 * (G - 1));
+            qmv_group<F>(ca, cp, G, t, xa + 64 * G, half_hi_f32(p0), half_hi_f32(p1), acc);
+        }
+        ++G;
+    }
+#pragma unroll 1
+    for (; G + 1 < G1; G += 2) {
+        const uint32_t p0 = lds32(sc + 2 * G), p1 = lds32(sc + 8 * sp + 2 * G);
+        qmv_group<F>(ca, cp, G, t, xa + 64 * G, half_lo_f32(p0), half_lo_f32(p1), acc);
+        qmv_group<F>(ca, cp, G + 1, t, xa + 64 * (G + 1), half_hi_f32(p0), half_hi_f32(p1), acc);
+    }
+    if (G < G1) {
+        const uint32_t p0 = lds32(sc + 2 * G), p1 = lds32(sc + 8 * sp + 2 * G);
+        qmv_group<F>(ca, cp, G, t, xa + 64 * G, half_lo_f32(p0), half_lo_f32(p1), acc);
     }
 }
 
@@ -262,16 +284,27 @@ __device__ __forceinline__ int moe_route(const QmvArgs& a, MoeTables tb) {
 }
 
 // ---- the kernel ---------------------------------------------------------------------------------------------------
-
-// Barrier block layout (uint64 slots from bar_off): full[nstage], empty[nstage], xfull[2], xempty[2], redfull[2],
-// redfree[2].
-__host__ __device__ constexpr int qmv_nbars(int nstage) { return 2 * nstage + 8; }
+//
+// The consumer warps form WG groups of QMV_NW / WG warps. Group j takes every WG-th tile of the CTA's range (tiles
+// are independent), so WG tiles are in flight at once and each tile's partial sums are reduced over QMV_NW / WG warps
+// only. Dense calls use up to 4 groups; MoE uses one (all warps on one tile at a time), because its activations
+// change per expert segment and one double-buffered activation area is what shared memory holds for eight tokens.
+// The host keeps nstage >= WG * nchunks: a group then never waits on a ring slot more than one phase ahead of that
+// slot's last completed phase, which is all an mbarrier parity wait can tell apart.
+//
+// Barrier block layout (uint64 slots from bar_off): full[nstage], empty[nstage], xfull[2], xempty[2],
+// redfull[2 * QMV_MAXWG], redfree[2 * QMV_MAXWG].
+constexpr int QMV_MAXWG = 4;
+__host__ __device__ constexpr int qmv_nbars(int nstage) { return 2 * nstage + 4 + 4 * QMV_MAXWG; }
 
 template <int F, int MODE, typename OutT>
-__global__ void __launch_bounds__(32 * (QMV_NW + 1), 1)
+__global__ void __launch_bounds__(32 * (QMV_NW + 1), 2)
 qmv_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap ts, const QmvArgs a) {
+    const int WG = a.wg;
+    const int WPG = QMV_NW / WG;
     extern __shared__ uint8_t smem_raw[];
-    uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    const uint32_t pad = (1024u - (smem_u32(smem_raw) & 1023u)) & 1023u;
+    uint8_t* sm = smem_raw + pad;   // pointer arithmetic on the shared array keeps the shared address space
     uint8_t* ring = sm + a.ring_off;
     uint8_t* xbuf = sm + a.x_off;
     float4* red = reinterpret_cast<float4*>(sm + a.red_off);
@@ -281,22 +314,24 @@ qmv_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUten
     uint64_t* xfull = bars + 2 * a.nstage;
     uint64_t* xempty = xfull + 2;
     uint64_t* redfull = xfull + 4;
-    uint64_t* redfree = xfull + 6;
+    uint64_t* redfree = redfull + 2 * QMV_MAXWG;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int KG = a.K / 32;
 
-    pdl_trigger();   // the next call may start its weight prefetch now (it still waits for us before touching y)
+    pdl_trigger();   // the next call may start its weight prefetch now (it still waits for us before touching x, y)
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < a.nstage; ++i) {
             mbar_init(&full[i], 1);
-            mbar_init(&empty[i], QMV_NW);
+            mbar_init(&empty[i], WPG);
         }
         for (int i = 0; i < 2; ++i) {
             mbar_init(&xfull[i], 1);
             mbar_init(&xempty[i], QMV_NW);
-            mbar_init(&redfull[i], QMV_NW);
+        }
+        for (int i = 0; i < 2 * WG; ++i) {
+            mbar_init(&redfull[i], WPG);
             mbar_init(&redfree[i], 1);
         }
         fence_mbar_init();
@@ -314,145 +349,184 @@ qmv_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUten
     const int total = nseg * a.tilesN;
     const int w0 = (int)(((long long)blockIdx.x * total) / gridDim.x);
     const int w1 = (int)(((long long)(blockIdx.x + 1) * total) / gridDim.x);
+    const int ntl = w1 - w0;   // tiles of this CTA
 
     // segment accessors: expert (weight row base), token count, and the slot (dense: token) of column j
-    auto seg_expert = [&](int s) -> int {
-        if constexpr (MODE == QMV_MOE) return tb.seg[s] >> 16; else return 0;
+    auto seg_expert = [&](int sg) -> int {
+        if constexpr (MODE == QMV_MOE) return tb.seg[sg] >> 16; else return 0;
     };
-    auto seg_first = [&](int s) -> int {
-        if constexpr (MODE == QMV_MOE) return tb.seg[s] & 0xFFFF; else return 0;
+    auto seg_first = [&](int sg) -> int {
+        if constexpr (MODE == QMV_MOE) return tb.seg[sg] & 0xFFFF; else return 0;
     };
-    auto seg_count = [&](int s) -> int {
-        if constexpr (MODE == QMV_MOE) return min(QMV_MAXTOK, tb.off[(tb.seg[s] >> 16) + 1] - seg_first(s));
+    auto seg_count = [&](int sg) -> int {
+        if constexpr (MODE == QMV_MOE) return min(QMV_MAXTOK, tb.off[(tb.seg[sg] >> 16) + 1] - seg_first(sg));
         else return a.T;
     };
-    auto seg_slot = [&](int s, int j) -> int {
-        if constexpr (MODE == QMV_MOE) return tb.slots[seg_first(s) + j]; else return j;
+    auto seg_slot = [&](int sg, int j) -> int {
+        if constexpr (MODE == QMV_MOE) return tb.slots[seg_first(sg) + j]; else return j;
     };
 
     constexpr int BITS = FmtTraits<F>::BITS;
-    const int nb = a.KS * BITS / 8 / 128;
-    const uint32_t stage_tx = (uint32_t)(nb * QMV_BOX_BYTES + a.KS);   // codes + 16 rows x KS/32 scales
+    const int ksb = a.KS * BITS / 8;                                          // code bytes per row per stage
+    const uint32_t stage_tx = (uint32_t)(QMV_ROWS * (a.cpitch + a.spitch));   // both boxes, pads included
 
     if (warp == QMV_NW) {
         // ===================== producer (one thread) =====================
         if (lane == 0) {
             prefetch_tmap(&tq);
             prefetch_tmap(&ts);
-            const int total_it = (w1 - w0) * a.nchunks;
+            const int total_it = ntl * a.nchunks;
             const int pre = min(total_it, a.nstage);
-            int issued = 0;
-            auto issue_w = [&](int it) {
-                const int w = w0 + it / a.nchunks, c = it % a.nchunks;
-                const int s = w / a.tilesN, tile = w % a.tilesN;
-                const int row = seg_expert(s) * a.N + tile * QMV_ROWS;
-                uint8_t* st = ring + (it % a.nstage) * a.stage_bytes;
-                uint64_t* fb = &full[it % a.nstage];
+            // iteration cursor: chunk c of tile `tile` of segment `sg`; ring slot stg in round rnd
+            int c = 0, sg = w0 / a.tilesN, tile = w0 % a.tilesN, stg = 0, rnd = 0, issued = 0;
+            auto issue_w = [&]() {
+                uint8_t* st = ring + stg * a.stage_bytes;
+                uint64_t* fb = &full[stg];
+                const int row = seg_expert(sg) * a.N + tile * QMV_ROWS;
                 mbar_arrive_expect_tx(fb, stage_tx);
-                const int xb0 = c * a.KS * BITS / 8;
-                for (int j = 0; j < nb; ++j) tma_load_2d(st + j * QMV_BOX_BYTES, &tq, xb0 + 128 * j, row, fb);
-                tma_load_2d(st + nb * QMV_BOX_BYTES, &ts, c * (a.KS / 32), row, fb);
+                tma_load_2d(st, &tq, c * ksb / 8, row, fb);                              // 8-byte elements
+                tma_load_2d(st + QMV_ROWS * a.cpitch, &ts, c * (a.KS / 32), row, fb);  // fp16 elements
                 ++issued;
+                if (++c == a.nchunks) {
+                    c = 0;
+                    if (++tile == a.tilesN) { tile = 0; ++sg; }
+                }
+                if (++stg == a.nstage) { stg = 0; ++rnd; }
             };
             int xsegs = 0;
             bool ok = true;
-            auto issue_x = [&](int s) {   // activations of the next segment this CTA meets, double-buffered
+            auto issue_x = [&](int xs) {   // activations of the next segment this CTA meets, double-buffered
                 const int xb = xsegs & 1;
                 if (xsegs >= 2) ok = wait_parity(&xempty[xb], ((xsegs >> 1) - 1) & 1);
                 if (!ok) return;
-                const int cnt = seg_count(s);
+                const int cnt = seg_count(xs);
                 uint8_t* dst = xbuf + xb * a.xrows * a.xpitch;
                 mbar_arrive_expect_tx(&xfull[xb], (uint32_t)(cnt * a.K * 2));
                 for (int j = 0; j < cnt; ++j) {
-                    int tok = seg_slot(s, j);
+                    int tok = seg_slot(xs, j);
                     if constexpr (MODE == QMV_MOE) tok /= a.topk;
                     bulk_load(dst + j * a.xpitch, a.x + (size_t)tok * a.K, (uint32_t)(a.K * 2), &xfull[xb]);
                 }
                 ++xsegs;
             };
-            for (int it = 0; it < pre; ++it) issue_w(it);   // the weights do not depend on the previous grid
-            pdl_wait();                                     // the activations may
+            for (int i = 0; i < pre; ++i) issue_w();   // the weights do not depend on the previous grid
+            pdl_wait();                                // the activations may
+            // activations of the segments the prefetched stages belong to, in order
             int last_seg = -1;
-            for (int it = 0; it < pre && ok; it += a.nchunks) {
-                const int s = (w0 + it / a.nchunks) / a.tilesN;
-                if (s != last_seg) { issue_x(s); last_seg = s; }
+            {
+                int xsg = w0 / a.tilesN, xtile = w0 % a.tilesN;
+                for (int it = 0; it < pre && ok; it += a.nchunks) {
+                    if (xsg != last_seg) { issue_x(xsg); last_seg = xsg; }
+                    if (++xtile == a.tilesN) { xtile = 0; ++xsg; }
+                }
             }
             for (int it = pre; it < total_it && ok; ++it) {
-                const int s = (w0 + it / a.nchunks) / a.tilesN;
-                if (s != last_seg) { issue_x(s); last_seg = s; if (!ok) break; }
-                ok = wait_parity(&empty[it % a.nstage], ((it / a.nstage) - 1) & 1);
+                if (c == 0 && sg != last_seg) { issue_x(sg); last_seg = sg; if (!ok) break; }
+                ok = wait_parity(&empty[stg], (rnd - 1) & 1);
                 if (!ok) break;
-                issue_w(it);
+                issue_w();
             }
             // drain: every copy this CTA issued lands before the CTA may exit (bounded as well)
-            for (int it = max(0, issued - a.nstage); it < issued; ++it)
-                if (!wait_parity(&full[it % a.nstage], (it / a.nstage) & 1, DEV_ERR_DRAIN_TIMEOUT)) break;
+            {
+                int dstg = 0, drnd = 0;
+                for (int it = 0; it < issued; ++it) {
+                    if (it >= issued - a.nstage &&
+                        !wait_parity(&full[dstg], drnd & 1, DEV_ERR_DRAIN_TIMEOUT))
+                        break;
+                    if (++dstg == a.nstage) { dstg = 0; ++drnd; }
+                }
+            }
             for (int j = max(0, xsegs - 2); j < xsegs; ++j)
                 if (!wait_parity(&xfull[j & 1], (j >> 1) & 1, DEV_ERR_DRAIN_TIMEOUT)) break;
         }
         return;
     }
 
-    // ===================== consumers (warps 0..NW-1) =====================
+    // ===================== consumers (warps 0..NW-1, WG groups) =====================
+    const int grp = warp / WPG, wi = warp % WPG;
     const int g = lane >> 2, t = lane & 3;
-    const int gpw = (a.KS / 32) / QMV_NW;
-    const int G0 = warp * gpw, G1 = G0 + gpw;
+    const int GS = a.KS / 32;
+    const int G0 = wi * GS / WPG, G1w = (wi + 1) * GS / WPG;
+    const uint32_t cp = (uint32_t)a.cpitch, sp = (uint32_t)a.spitch;
+    const uint32_t ring_s = smem_u32(ring);
+    const uint32_t xbuf_s = smem_u32(xbuf);
+    const uint32_t c_row = g * cp;                                       // row g's codes inside a stage
+    const uint32_t s_row = (uint32_t)(QMV_ROWS * a.cpitch) + g * sp;     // row g's scales inside a stage
     OutT* y = reinterpret_cast<OutT*>(a.y);
-    pdl_wait();   // y may still be read or written by the previous grid
+    pdl_wait();   // x and y may still be written (or y read) by the previous grid
 
     int cur_seg = -1, segs_seen = 0, cnt = 0;
-    const uint8_t* xr = nullptr;
-    int it = 0, ntile = 0;
+    uint32_t xrow = 0;
     bool ok = true;
-    for (int w = w0; w < w1 && ok; ++w, ++ntile) {
-        const int s = w / a.tilesN, tile = w % a.tilesN;
-        if (s != cur_seg) {
-            if (cur_seg >= 0) {
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&xempty[(segs_seen - 1) & 1]);
+    // this group's tiles: tl = grp, grp + WG, ...; their first stage iteration is tl * nchunks
+    int sg = (w0 + grp) / a.tilesN, tile = (w0 + grp) % a.tilesN;
+    int stg = 0, rnd = 0;
+    {
+        const int it0 = grp * a.nchunks;   // the first iteration of this group (no division in the loop)
+        rnd = it0 / a.nstage;
+        stg = it0 - rnd * a.nstage;
+    }
+    int ntile = 0;   // tiles this group has done (reduction buffer parity / reducer rotation)
+    for (int tl = grp; tl < ntl && ok; tl += WG, ++ntile) {
+        if (sg != cur_seg) {
+            if constexpr (MODE == QMV_MOE) {
+                if (cur_seg >= 0) {
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&xempty[(segs_seen - 1) & 1]);
+                }
             }
-            cur_seg = s;
+            cur_seg = sg;
             const int xb = segs_seen & 1;
             ok = wait_parity(&xfull[xb], (segs_seen >> 1) & 1);
             ++segs_seen;
-            cnt = seg_count(s);
-            xr = g < cnt ? xbuf + xb * a.xrows * a.xpitch + g * a.xpitch : nullptr;
+            cnt = seg_count(sg);
+            xrow = xbuf_s + (uint32_t)(xb * a.xrows * a.xpitch + (g < cnt ? g : 0) * a.xpitch) + x_lane_off<F>(t);
             if (!ok) break;
         }
         float acc[4] = {0.f, 0.f, 0.f, 0.f};
-        for (int c = 0; c < a.nchunks; ++c, ++it) {
-            const int st = it % a.nstage;
-            if (!wait_parity(&full[st], (it / a.nstage) & 1)) { ok = false; break; }
-            consume_stage<F>(ring + st * a.stage_bytes, a.KS, G0, G1, c * a.KS, KG, xr, g, t, acc);
+        int kc = 0;
+        for (int c = 0; c < a.nchunks; ++c, kc += GS) {
+            if (!wait_parity(&full[stg], rnd & 1)) { ok = false; break; }
+            const uint32_t st = ring_s + (uint32_t)(stg * a.stage_bytes);
+            const int G1 = min(G1w, KG - kc);
+            consume_stage<F>(st + c_row, cp, st + s_row, sp, G0, G1, xrow + (uint32_t)(kc * 64), t, acc);
             __syncwarp();
-            if (lane == 0) mbar_arrive(&empty[st]);
+            if (lane == 0) mbar_arrive(&empty[stg]);
+            if (++stg == a.nstage) { stg = 0; ++rnd; }
         }
         if (!ok) break;
-        // cross-warp reduction of the tile (double-buffered, bounded mbarrier handshakes), then the write-back
-        const int tp = ntile & 1, use = ntile >> 1;
-        if (use > 0 && !wait_parity(&redfree[tp], (use - 1) & 1)) { ok = false; break; }
-        red[(tp * QMV_NW + warp) * 32 + lane] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+        // reduction over the group's warps (double-buffered, bounded mbarrier handshakes); the reducer rotates
+        const int tp = ntile & 1, use = ntile >> 1, reducer = ntile % WPG;
+        uint64_t* rfull = &redfull[grp * 2 + tp];
+        uint64_t* rfree = &redfree[grp * 2 + tp];
+        float4* rb = red + ((grp * 2 + tp) * WPG) * 32;
+        if (use > 0 && !wait_parity(rfree, (use - 1) & 1)) { ok = false; break; }
+        rb[wi * 32 + lane] = make_float4(acc[0], acc[1], acc[2], acc[3]);
         __syncwarp();
-        if (lane == 0) mbar_arrive(&redfull[tp]);
-        if (warp == 0) {
-            if (!wait_parity(&redfull[tp], use & 1)) { ok = false; break; }
-            float4 r = red[(tp * QMV_NW) * 32 + lane];
-#pragma unroll
-            for (int v = 1; v < QMV_NW; ++v) {
-                const float4 q = red[(tp * QMV_NW + v) * 32 + lane];
+        if (lane == 0) mbar_arrive(rfull);
+        if (wi == reducer) {
+            if (!wait_parity(rfull, use & 1)) { ok = false; break; }
+            float4 r = rb[lane];
+            for (int v = 1; v < WPG; ++v) {
+                const float4 q = rb[v * 32 + lane];
                 r.x += q.x; r.y += q.y; r.z += q.z; r.w += q.w;
             }
             __syncwarp();
-            if (lane == 0) mbar_arrive(&redfree[tp]);
+            if (lane == 0) mbar_arrive(rfree);
             const int n0 = tile * QMV_ROWS + g, n1 = n0 + 8;
             const float vals[4] = {r.x, r.y, r.z, r.w};
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
                 const int col = 2 * t + (q & 1);
                 const int n = (q < 2) ? n0 : n1;
-                if (col < cnt && n < a.N) y[(size_t)seg_slot(s, col) * a.N + n] = to_out<OutT>(vals[q]);
+                if (col < cnt && n < a.N) y[(size_t)seg_slot(sg, col) * a.N + n] = to_out<OutT>(vals[q]);
             }
         }
+        // next tile of this group: WG tiles further; its first iteration is (WG - 1) * nchunks stages further
+        tile += WG;
+        while (tile >= a.tilesN) { tile -= a.tilesN; ++sg; }
+        stg += (WG - 1) * a.nchunks;
+        while (stg >= a.nstage) { stg -= a.nstage; ++rnd; }
     }
 }
 

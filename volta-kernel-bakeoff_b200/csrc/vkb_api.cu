@@ -121,7 +121,6 @@ int get_tmap_2d(CUtensorMap* out, const void* ptr, uint64_t rows, uint64_t row_b
 // ---- decode / MoE planning ---------------------------------------------------------------------------------------
 
 static int fmt_bits(int fmt) { return fmt == VKB_FMT_Q4 ? 4 : fmt == VKB_FMT_Q8 ? 8 : 2; }
-static int ks_unit(int fmt) { return fmt == VKB_FMT_Q2 ? 512 : 256; }
 
 struct QmvPlan {
     QmvArgs a;
@@ -131,15 +130,17 @@ struct QmvPlan {
 
 static int round_up(int v, int m) { return (v + m - 1) / m * m; }
 
-// Stage: 16 rows x KS values, about 16 KB of codes; ring as deep as fits, preferring a footprint that lets a second
-// CTA (the next call, under PDL) share the SM.
+// Stage: 16 rows x KS values, up to 1.5 KB of codes per row (one TMA box each for codes and scales, rows padded so
+// the fragment reads are conflict free); ring as deep as fits, preferring a footprint that lets a second CTA (the
+// next call, under PDL) share the SM.
 static bool plan_qmv(int fmt, int N, int K, int xrows, int moe_slots, int E_local, const DeviceInfo& d, QmvPlan* p) {
-    const int bits = fmt_bits(fmt), unit = ks_unit(fmt);
-    const int ks_max = 8192 / bits;   // 1 KB of codes per row per stage
+    const int bits = fmt_bits(fmt), unit = QMV_KS_UNIT;
+    const int ks_max = 12288 / bits;   // 1.5 KB of codes per row per stage (the 8-byte box row limit is 2 KB)
     const int nchunks = (K + ks_max - 1) / ks_max;
     const int KS = round_up((K + nchunks - 1) / nchunks, unit);
-    const int nb = KS * bits / 8 / 128;
-    const int stage_bytes = round_up(nb * QMV_BOX_BYTES + KS, 1024);
+    const int cpitch = KS * bits / 8 + (fmt == VKB_FMT_Q8 ? 32 : 16);
+    const int spitch = KS / 16 + ((KS / 256) % 2 == 0 ? 16 : 32);   // pitch / 4 = 4 x odd: conflict-free rows
+    const int stage_bytes = round_up(QMV_ROWS * (cpitch + spitch), 128);
     const int xpitch = round_up(K * 2, 128) + 64;
     const int xbufs = moe_slots > 0 ? 2 : 1;
     const int xbytes = round_up(xbufs * xrows * xpitch, 16);
@@ -154,17 +155,23 @@ static bool plan_qmv(int fmt, int N, int K, int xrows, int moe_slots, int E_loca
         budget = pass == 0 ? pair_budget : solo_budget;
         nstage = 16;
         while (nstage >= 2 && nstage * stage_bytes + fixed_for(nstage) > budget) --nstage;
-        if (nstage >= 4 || (pass == 1 && nstage >= 2)) break;
+        if (nstage >= 3 || (pass == 1 && nstage >= 2)) break;
     }
     if (nstage < 2) return false;
     QmvArgs& a = p->a;
     a.N = N; a.K = K; a.KS = KS; a.nchunks = nchunks; a.nstage = nstage; a.stage_bytes = stage_bytes;
+    a.cpitch = cpitch; a.spitch = spitch;
     a.xpitch = xpitch; a.xrows = xrows; a.tilesN = (N + QMV_ROWS - 1) / QMV_ROWS;
     a.ring_off = 0;
     a.x_off = nstage * stage_bytes;
     a.red_off = a.x_off + xbytes;
     a.bar_off = a.red_off + redbytes;
     a.moe_off = a.bar_off + 8 * qmv_nbars(nstage);
+    // warp groups: as many tiles in flight as the ring allows (nstage >= wg * nchunks), one for MoE
+    a.wg = 1;
+    if (moe_slots == 0)
+        for (int wg = QMV_MAXWG; wg > 1; wg /= 2)
+            if (nstage >= wg * nchunks) { a.wg = wg; break; }
     p->smem = a.moe_off + moebytes + slack;
     return true;
 }
@@ -237,11 +244,11 @@ static int qmv_entry(const void* q, const void* s, const void* x, void* y, bool 
     if (fast && plan_qmv(F, N, K, xrows, slots, E_local, d, &p)) {
         constexpr int BITS = FmtTraits<F>::BITS;
         CUtensorMap tq, ts;
-        int r = get_tmap_2d(&tq, q, (uint64_t)rows, (uint64_t)K * BITS / 8, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, 128,
-                            QMV_ROWS, CU_TENSOR_MAP_SWIZZLE_128B);
+        int r = get_tmap_2d(&tq, q, (uint64_t)rows, (uint64_t)K * BITS / 8, CU_TENSOR_MAP_DATA_TYPE_UINT64, 8,
+                            (uint32_t)(p.a.cpitch / 8), QMV_ROWS, CU_TENSOR_MAP_SWIZZLE_NONE);
         if (r) return r;
         r = get_tmap_2d(&ts, s, (uint64_t)rows, (uint64_t)K / 16, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2,
-                        (uint32_t)(p.a.KS / 32), QMV_ROWS, CU_TENSOR_MAP_SWIZZLE_NONE);
+                        (uint32_t)(p.a.spitch / 2), QMV_ROWS, CU_TENSOR_MAP_SWIZZLE_NONE);
         if (r) return r;
         p.a.x = (const __half*)x;
         p.a.y = y;
