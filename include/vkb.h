@@ -21,7 +21,10 @@
  *     q, s and x; other shapes run a plain CUDA-core kernel with the same results.
  *   - Thread-safe: per-device one-time set-up is guarded; tensor-map caches are per host thread.
  *   - Launches use programmatic dependent launch (PDL) unless vkb_set_pdl(0): the weight stream of call i+1 overlaps
- *     the tail of call i; activations and outputs are still ordered after the previous kernel on the stream.
+ *     the tail of call i; activations and outputs are still ordered after the previous kernel on the stream. The
+ *     weights and scales are read BEFORE the preceding kernel in the stream has finished, so that kernel must not
+ *     write them (weights are normally static; after a kernel that repacks them, call vkb_set_pdl(0) for the next
+ *     call or put any other kernel in between).
  */
 #ifndef VKB_H
 #define VKB_H
@@ -73,6 +76,15 @@ int vkb_moe_q4(const void* qpool, const void* spool, const int32_t* idx, int T, 
                int E_local, int e0, int N, int K, vkb_stream_t stream);
 int vkb_moe(int fmt, const void* qpool, const void* spool, const int32_t* idx, int T, int topk, const void* x, void* y,
             int out_f32, int E_local, int e0, int N, int K, vkb_stream_t stream);
+
+/* ---- prompt GEMM on tcgen05: y[M][N] = x[M][K] . W[N][K]^T, any M >= 1 -----------------------------------------------
+ * Replaces tc_q4 / tc_q4_v2 (reference src/stage2.cuh:94-154, :226-229; src/stage4_tc.cuh:38-200): the weights are
+ * dequantised to fp16 exactly as the reference rounds them ((code - 8) * scale, one rounding) and multiplied on the
+ * 5th-generation tensor cores with fp32 accumulation. Needs K % 256 == 0, K <= 7680, 16-byte aligned q, s, x; any M
+ * and N (no tile-multiple requirement). fp16 output; _f32 writes fp32 (the reference's float* y). */
+int vkb_gemm_q4_tc(const void* q, const void* s, const void* x, void* y, int N, int K, int M, vkb_stream_t stream);
+int vkb_gemm_q4_tc_f32(const void* q, const void* s, const void* x, float* y, int N, int K, int M,
+                       vkb_stream_t stream);
 
 /* ---- status --------------------------------------------------------------------------------------------------------- */
 /* Human-readable text of a return code. */

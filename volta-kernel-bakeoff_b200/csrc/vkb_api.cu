@@ -11,6 +11,7 @@
 #include "../../include/vkb.h"
 #include "qmv.cuh"
 #include "qmv_simple.cuh"
+#include "tc_gemm.cuh"
 #include "vkb_internal.h"
 
 namespace vkb {
@@ -287,6 +288,86 @@ static int qmv_dispatch(int fmt, const void* q, const void* s, const void* x, vo
     }
 }
 
+// ---- prompt GEMM (tcgen05) --------------------------------------------------------------------------------------
+
+struct TcPlan {
+    TcArgs a;
+    int smem;
+    dim3 grid;
+};
+
+static bool plan_tc(int N, int K, int M, const DeviceInfo& d, TcPlan* p) {
+    TcArgs& a = p->a;
+    const int ntm = (M + 255) / 256;
+    int NT = round_up((M + ntm - 1) / ntm, 16);
+    if (NT < 16) NT = 16;
+    a.M = M; a.N = N; a.K = K; a.NT = NT;
+    int cols = 32;
+    while (cols < NT) cols *= 2;
+    a.tmem_cols = cols;
+    a.a_off = 0;
+    a.b_off = TC_BM * 128;                              // 16 KB A tile, 1024-aligned
+    a.p_off = round_up(a.b_off + NT * 128, 1024);       // packed codes after the 128B-swizzled B tile
+    a.stage_bytes = round_up(a.p_off + TC_BM * 32, 1024);
+    const int padh = ((K / 32) % 16 == 0) ? 8 : 16;     // scale row pitch / 4 = 4 x odd (2-way at most)
+    a.spitch = (K / 32 + padh) * 2;
+    const int sbytes = round_up(TC_BM * a.spitch, 1024);
+    const int fixed = sbytes + 8 * 32 + 1024;           // scales, barriers, alignment slack
+    int ns = 8;
+    while (ns >= 2 && ns * a.stage_bytes + fixed > d.smem_optin) --ns;
+    if (ns < 2) return false;
+    a.nstage = ns;
+    a.s_off = ns * a.stage_bytes;
+    a.bar_off = a.s_off + sbytes;
+    p->smem = a.bar_off + 8 * (3 * ns + 2) + 16 + 1024;
+    p->grid = dim3((unsigned)((N + TC_BM - 1) / TC_BM), (unsigned)ntm);
+    return true;
+}
+
+template <typename OutT>
+static int tc_entry(const void* q, const void* s, const void* x, void* y, int N, int K, int M, cudaStream_t st) {
+    if (!q || !s || !x || !y) return VKB_EINVAL;
+    if (N < 1 || M < 1 || K < 256) return VKB_EINVAL;
+    if (K % 256 != 0 || K / 32 + 16 > 256) return VKB_EUNSUPPORTED;
+    if (!aligned16(q) || !aligned16(s) || !aligned16(x)) return VKB_EUNSUPPORTED;
+    int dev = 0;
+    if (int r = current_device(&dev)) return r;
+    const DeviceInfo& d = device_info(dev);
+    if (d.cc_major < 10) return VKB_EUNSUPPORTED;
+    TcPlan p{};
+    if (!plan_tc(N, K, M, d, &p)) return VKB_EUNSUPPORTED;
+    p.a.y = y;
+    CUtensorMap tq, ts, tx;
+    int r = get_tmap_2d(&tq, q, (uint64_t)N, (uint64_t)K / 2, CU_TENSOR_MAP_DATA_TYPE_UINT64, 8, 4, TC_BM,
+                        CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (r) return r;
+    r = get_tmap_2d(&ts, s, (uint64_t)N, (uint64_t)K / 16, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2,
+                    (uint32_t)(p.a.spitch / 2), TC_BM, CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (r) return r;
+    r = get_tmap_2d(&tx, x, (uint64_t)M, (uint64_t)K * 2, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, TC_BK,
+                    (uint32_t)p.a.NT, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (r) return r;
+    auto kern = tc_q4_kernel<OutT>;
+    static std::once_flag once[kMaxDevices];
+    static cudaError_t attr_err[kMaxDevices];
+    std::call_once(once[dev], [&] {
+        attr_err[dev] = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, d.smem_optin);
+    });
+    if (attr_err[dev] != cudaSuccess) return -(int)attr_err[dev];
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = p.grid;
+    cfg.blockDim = dim3(TC_THREADS);
+    cfg.dynamicSmemBytes = p.smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl_enabled() && pdl_stream_ok(st) ? 1 : 0;
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, tq, ts, tx, p.a);
+    return e == cudaSuccess ? 0 : -(int)e;
+}
+
 }  // namespace vkb
 
 using namespace vkb;
@@ -324,6 +405,14 @@ int vkb_moe(int fmt, const void* qpool, const void* spool, const int32_t* idx, i
 int vkb_moe_q4(const void* qpool, const void* spool, const int32_t* idx, int T, int topk, const void* x, void* y,
                int E_local, int e0, int N, int K, vkb_stream_t stream) {
     return vkb_moe(VKB_FMT_Q4, qpool, spool, idx, T, topk, x, y, 0, E_local, e0, N, K, stream);
+}
+
+int vkb_gemm_q4_tc(const void* q, const void* s, const void* x, void* y, int N, int K, int M, vkb_stream_t stream) {
+    return tc_entry<__half>(q, s, x, y, N, K, M, (cudaStream_t)stream);
+}
+int vkb_gemm_q4_tc_f32(const void* q, const void* s, const void* x, float* y, int N, int K, int M,
+                       vkb_stream_t stream) {
+    return tc_entry<float>(q, s, x, y, N, K, M, (cudaStream_t)stream);
 }
 
 const char* vkb_strerror(int code) {
