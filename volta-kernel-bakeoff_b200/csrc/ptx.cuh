@@ -94,6 +94,35 @@ __device__ __forceinline__ bool wait_parity(uint64_t* bar, uint32_t parity, unsi
     }
 }
 
+// try_wait with a suspend-time hint: a thread whose phase is not complete sleeps until it completes (or the hint,
+// ns, elapses) instead of re-issuing the test, so a waiting role leaves its sub-partition's issue slots to others.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint32_t bar_addr, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(bar_addr), "r"(parity), "r"(100000u)
+        : "memory");
+    return ok != 0;
+}
+
+// wait_parity for roles that are not on the critical issue path (producers, the MMA thread, waiting consumers).
+__device__ __forceinline__ bool wait_parity_sleep(uint64_t* bar, uint32_t parity,
+                                                  unsigned err = DEV_ERR_WAIT_TIMEOUT) {
+    const uint32_t a = smem_u32(bar);
+    if (mbar_try_wait_sleep(a, parity)) return true;
+    const uint64_t t0 = globaltimer();
+    for (;;) {
+        if (mbar_try_wait_sleep(a, parity)) return true;
+        if (globaltimer() - t0 > VKB_WAIT_NS) {
+            raise_status(err);
+            return false;
+        }
+    }
+}
+
 // ---- TMA ------------------------------------------------------------------------------------------------------
 
 // 2-D tiled tensor load (no multicast) into this CTA's shared memory, completing bytes on bar.
@@ -112,8 +141,39 @@ __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t b
         : "memory");
 }
 
+// 3-D tiled tensor load (no multicast) into this CTA's shared memory, completing bytes on bar.
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, int x, int y, int z, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], [%2];"
+        ::"r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z)
+        : "memory");
+}
+
+// 2-D tiled tensor store shared -> global (bulk-group completion); elements outside the tensor are not written.
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, int x, int y, const void* src) {
+    asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];"
+                 ::"l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(src)), "r"(x), "r"(y)
+                 : "memory");
+}
+__device__ __forceinline__ void bulk_commit_group() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// Wait until at most N committed bulk groups of this thread still read their shared-memory source.
+template <int N> __device__ __forceinline__ void bulk_wait_group_read() {
+    asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+// Wait until at most N committed bulk groups of this thread are still in flight (writes performed).
+template <int N> __device__ __forceinline__ void bulk_wait_group() {
+    asm volatile("cp.async.bulk.wait_group %0;" ::"n"(N) : "memory");
+}
+
 __device__ __forceinline__ void prefetch_tmap(const CUtensorMap* map) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
+// One lane of a converged warp (elect.sync): the issuing lane for warp-uniform producer / MMA loops.
+__device__ __forceinline__ bool elect_one() {
+    uint32_t e;
+    asm volatile("{\n\t.reg .pred p;\n\telect.sync _|p, 0xffffffff;\n\tselp.u32 %0, 1, 0, p;\n\t}" : "=r"(e));
+    return e != 0;
 }
 
 // ---- programmatic dependent launch ------------------------------------------------------------------------------

@@ -119,6 +119,42 @@ int get_tmap_2d(CUtensorMap* out, const void* ptr, uint64_t rows, uint64_t row_b
     return 0;
 }
 
+// Activations x [M][K] fp16 as a 3-D tensor {64 k, M tokens, K/64 k-blocks} (strides 2K and 128 bytes), boxes of
+// {64, NT, XK} with 128-byte swizzle: one copy lands XK consecutive K-major UMMA B tiles of NT x 64. Cached per host
+// thread like get_tmap_2d.
+int get_tmap_x3d(CUtensorMap* out, const void* x, int M, int K, int NT, int XK) {
+    struct Key {
+        const void* p;
+        int M, K, NT, XK;
+        bool operator==(const Key& o) const { return p == o.p && M == o.M && K == o.K && NT == o.NT && XK == o.XK; }
+    };
+    struct Hash {
+        size_t operator()(const Key& k) const {
+            return std::hash<const void*>()(k.p) ^ ((size_t)k.M * 1000003u) ^ ((size_t)k.K << 20) ^
+                   ((size_t)k.NT << 40) ^ ((size_t)k.XK << 52);
+        }
+    };
+    thread_local std::unordered_map<Key, CUtensorMap, Hash> cache;
+    const Key key{x, M, K, NT, XK};
+    auto it = cache.find(key);
+    if (it != cache.end()) { *out = it->second; return 0; }
+    EncodeTiledFn enc = encode_fn();
+    if (!enc) return -(int)cudaErrorNotSupported;
+    cuuint64_t dims[3] = {64, (cuuint64_t)M, (cuuint64_t)(K / 64)};
+    cuuint64_t strides[2] = {(cuuint64_t)K * 2, 128};
+    cuuint32_t box[3] = {64, (cuuint32_t)NT, (cuuint32_t)XK};
+    cuuint32_t estr[3] = {1, 1, 1};
+    CUtensorMap m;
+    const CUresult r = enc(&m, CU_TENSOR_MAP_DATA_TYPE_UINT16, 3, const_cast<void*>(x), dims, strides, box, estr,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return -(int)cudaErrorInvalidValue;
+    if (cache.size() > 65536) cache.clear();
+    cache.emplace(key, m);
+    *out = m;
+    return 0;
+}
+
 // ---- decode / MoE planning ---------------------------------------------------------------------------------------
 
 static int fmt_bits(int fmt) { return fmt == VKB_FMT_Q4 ? 4 : fmt == VKB_FMT_Q8 ? 8 : 2; }
@@ -292,35 +328,60 @@ static int qmv_dispatch(int fmt, const void* q, const void* s, const void* x, vo
 
 struct TcPlan {
     TcArgs a;
+    int pk;     // K steps per packed chunk (kernel template argument)
     int smem;
     dim3 grid;
 };
 
-static bool plan_tc(int N, int K, int M, const DeviceInfo& d, TcPlan* p) {
+// Token tile NT (a multiple of 32, <= 256) chosen to minimise waves x per-tile time over the SMs (one CTA per SM);
+// ring depths sized for the latency each ring has to cover (the P ring: HBM, ~4.5k cycles; the X ring: L2; the A
+// ring: the MMA's completion), then shrunk to fit shared memory.
+static bool plan_tc(int N, int K, int M, int out_bytes, const DeviceInfo& d, TcPlan* p) {
     TcArgs& a = p->a;
-    const int ntm = (M + 255) / 256;
-    int NT = round_up((M + ntm - 1) / ntm, 16);
-    if (NT < 16) NT = 16;
-    a.M = M; a.N = N; a.K = K; a.NT = NT;
-    int cols = 32;
-    while (cols < NT) cols *= 2;
-    a.tmem_cols = cols;
-    a.a_off = 0;
-    a.b_off = TC_BM * 128;                              // 16 KB A tile, 1024-aligned
-    a.p_off = round_up(a.b_off + NT * 128, 1024);       // packed codes after the 128B-swizzled B tile
-    a.stage_bytes = round_up(a.p_off + TC_BM * 32, 1024);
-    const int padh = ((K / 32) % 16 == 0) ? 8 : 16;     // scale row pitch / 4 = 4 x odd (2-way at most)
-    a.spitch = (K / 32 + padh) * 2;
+    const int tiles_n = (N + TC_BM - 1) / TC_BM;
+    const int nk = K / TC_BK;
+    int NT = 0;
+    double best = 1e300;
+    const int nt_max = round_up(M, 32) < 256 ? round_up(M, 32) : 256;
+    for (int nt = nt_max; nt >= 32; nt -= 32) {
+        const long tiles = (long)tiles_n * ((M + nt - 1) / nt);
+        const long waves = (tiles + d.sm_count - 1) / d.sm_count;
+        const double step = nt * 2.0 > 160.0 ? nt * 2.0 : 160.0;   // cycles per K step: MMA or the dequant floor
+        const double t = (double)waves * (nk * step + 3000.0);
+        if (t < best * 0.999) { best = t; NT = nt; }
+    }
+    a.M = M; a.N = N; a.K = K; a.NT = NT; a.nk = nk;
+    p->pk = nk % 8 == 0 ? 8 : 4;   // K steps per packed chunk (K % 256 == 0 gives nk % 4 == 0)
+    const int pchunk = tc_pchunk(p->pk);
+    a.spitch = K / 16 + (((K / 256) % 2 == 0) ? 16 : 0);   // pitch / 16 odd: conflict-free 16-byte scale reads
     const int sbytes = round_up(TC_BM * a.spitch, 1024);
-    const int fixed = sbytes + 8 * 32 + 1024;           // scales, barriers, alignment slack
-    int ns = 8;
-    while (ns >= 2 && ns * a.stage_bytes + fixed > d.smem_optin) --ns;
-    if (ns < 2) return false;
-    a.nstage = ns;
-    a.s_off = ns * a.stage_bytes;
+    const int na = 2;   // TMEM: accumulators [0, NT <= 256), A ring of two 128-column slots from column 256
+    a.a_col0 = 256;
+    a.tmem_cols = 512;
+    // X stages of up to 32 KB (xk K steps per TMA box; two producer warps alternate stages, so nx is even), P
+    // chunks at least two; then deepen the P ring (HBM latency) and the X ring while shared memory lasts
+    int xk = 8;
+    while (xk > 1 && (xk * NT * 128 > 32768 || nk % xk != 0)) xk /= 2;
+    int nx = 4, np = 2;
+    auto bars_bytes = [&]() { return 8 * (2 * np + 2 * nx + 2 * na + 2) + 16; };
+    auto total = [&]() { return nx * xk * NT * 128 + np * pchunk + sbytes + bars_bytes() + 1024; };
+    if (total() > d.smem_optin) nx = 2;
+    if (total() > d.smem_optin) return false;
+    for (bool grew = true; grew;) {
+        grew = false;
+        if (np < 6) { ++np; if (total() <= d.smem_optin) grew = true; else --np; }
+        if (nx < 6) { nx += 2; if (total() <= d.smem_optin) grew = true; else nx -= 2; }
+    }
+    a.xk = xk;
+    a.x_stage = xk * NT * 128;
+    if (2 * TC_NDQ * TC_EPI_BOX * TC_EPI_BOX * out_bytes > nx * a.x_stage + np * pchunk) return false;   // staging
+    a.na = na; a.nx = nx; a.np = np;
+    a.x_off = 0;
+    a.p_off = nx * a.x_stage;
+    a.s_off = a.p_off + np * pchunk;
     a.bar_off = a.s_off + sbytes;
-    p->smem = a.bar_off + 8 * (3 * ns + 2) + 16 + 1024;
-    p->grid = dim3((unsigned)((N + TC_BM - 1) / TC_BM), (unsigned)ntm);
+    p->smem = total();
+    p->grid = dim3((unsigned)tiles_n, (unsigned)((M + NT - 1) / NT));
     return true;
 }
 
@@ -328,30 +389,42 @@ template <typename OutT>
 static int tc_entry(const void* q, const void* s, const void* x, void* y, int N, int K, int M, cudaStream_t st) {
     if (!q || !s || !x || !y) return VKB_EINVAL;
     if (N < 1 || M < 1 || K < 256) return VKB_EINVAL;
-    if (K % 256 != 0 || K / 32 + 16 > 256) return VKB_EUNSUPPORTED;
+    if (K % 256 != 0 || K > 7680) return VKB_EUNSUPPORTED;
     if (!aligned16(q) || !aligned16(s) || !aligned16(x)) return VKB_EUNSUPPORTED;
     int dev = 0;
     if (int r = current_device(&dev)) return r;
     const DeviceInfo& d = device_info(dev);
     if (d.cc_major < 10) return VKB_EUNSUPPORTED;
     TcPlan p{};
-    if (!plan_tc(N, K, M, d, &p)) return VKB_EUNSUPPORTED;
+    if (!plan_tc(N, K, M, (int)sizeof(OutT), d, &p)) return VKB_EUNSUPPORTED;
     p.a.y = y;
-    CUtensorMap tq, ts, tx;
-    int r = get_tmap_2d(&tq, q, (uint64_t)N, (uint64_t)K / 2, CU_TENSOR_MAP_DATA_TYPE_UINT64, 8, 4, TC_BM,
-                        CU_TENSOR_MAP_SWIZZLE_NONE);
+    p.a.tma_store = aligned16(y) && ((size_t)N * sizeof(OutT)) % 16 == 0;
+    CUtensorMap tq, ts, tx, ty;
+    int r = get_tmap_2d(&tq, q, (uint64_t)N, (uint64_t)K / 2, CU_TENSOR_MAP_DATA_TYPE_UINT64, 8,
+                        (uint32_t)tc_ppitch(p.pk) / 8, TC_BM, CU_TENSOR_MAP_SWIZZLE_NONE);
     if (r) return r;
     r = get_tmap_2d(&ts, s, (uint64_t)N, (uint64_t)K / 16, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2,
                     (uint32_t)(p.a.spitch / 2), TC_BM, CU_TENSOR_MAP_SWIZZLE_NONE);
     if (r) return r;
-    r = get_tmap_2d(&tx, x, (uint64_t)M, (uint64_t)K * 2, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, TC_BK,
-                    (uint32_t)p.a.NT, CU_TENSOR_MAP_SWIZZLE_128B);
+    r = get_tmap_x3d(&tx, x, M, K, p.a.NT, p.a.xk);
     if (r) return r;
-    auto kern = tc_q4_kernel<OutT>;
+    if (p.a.tma_store) {
+        r = get_tmap_2d(&ty, y, (uint64_t)M, (uint64_t)N * sizeof(OutT),
+                        sizeof(OutT) == 4 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_UINT16,
+                        (uint32_t)sizeof(OutT), TC_EPI_BOX, TC_EPI_BOX, CU_TENSOR_MAP_SWIZZLE_NONE);
+        if (r) return r;
+    } else {
+        ty = tq;   // unused by the kernel
+    }
+    auto kern = p.pk == 8 ? tc_q4_kernel<OutT, 8> : tc_q4_kernel<OutT, 4>;
     static std::once_flag once[kMaxDevices];
     static cudaError_t attr_err[kMaxDevices];
     std::call_once(once[dev], [&] {
-        attr_err[dev] = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, d.smem_optin);
+        attr_err[dev] = cudaFuncSetAttribute(tc_q4_kernel<OutT, 8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             d.smem_optin);
+        if (attr_err[dev] == cudaSuccess)
+            attr_err[dev] = cudaFuncSetAttribute(tc_q4_kernel<OutT, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                 d.smem_optin);
     });
     if (attr_err[dev] != cudaSuccess) return -(int)attr_err[dev];
     cudaLaunchConfig_t cfg{};
@@ -364,7 +437,7 @@ static int tc_entry(const void* q, const void* s, const void* x, void* y, int N,
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl_enabled() && pdl_stream_ok(st) ? 1 : 0;
-    const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, tq, ts, tx, p.a);
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, tq, ts, tx, ty, p.a);
     return e == cudaSuccess ? 0 : -(int)e;
 }
 
