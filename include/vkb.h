@@ -86,6 +86,35 @@ int vkb_gemm_q4_tc(const void* q, const void* s, const void* x, void* y, int N, 
 int vkb_gemm_q4_tc_f32(const void* q, const void* s, const void* x, float* y, int N, int K, int M,
                        vkb_stream_t stream);
 
+/* ---- multi-GPU: one process (and one rank) per GPU ---------------------------------------------------------------------
+ * No counterpart in the reference, which runs on one GPU: these shard the MoE (by experts) and the prompt GEMM (by
+ * weight rows) over the GPUs of one node. A communicator wraps one NCCL rank on the device that is current at vkb_comm_init. Collective entry points must be
+ * called by every rank, in the same order, with equal shapes and counts; they return an error instead of leaving a
+ * peer waiting when a local launch fails after the argument checks. */
+typedef struct vkb_comm vkb_comm_t;
+#define VKB_UNIQUE_ID_BYTES 128
+/* Rank 0 creates the id; the caller distributes the 128 bytes to every rank (any host channel). */
+int vkb_comm_unique_id(void* id);
+int vkb_comm_init(vkb_comm_t** comm, int rank, int nranks, const void* id);
+int vkb_comm_destroy(vkb_comm_t* comm);
+int vkb_comm_rank(const vkb_comm_t* comm);
+int vkb_comm_size(const vkb_comm_t* comm);
+/* MoE, expert parallel: this rank holds experts [e0, e0 + E_local) (qpool / spool as in vkb_moe_q4); idx and x are
+ * the full batch on every rank. After the call every rank's y [T][topk][N] holds every slot, bit-identical to one GPU
+ * (each rank writes its slots and zeros elsewhere; an in-place ncclAllReduce sums the ranks). */
+int vkb_moe_q4_ep(vkb_comm_t* comm, const void* qpool, const void* spool, const int32_t* idx, int T, int topk,
+                  const void* x, void* y, int E_local, int e0, int N, int K, vkb_stream_t stream);
+int vkb_moe_ep(vkb_comm_t* comm, int fmt, const void* qpool, const void* spool, const int32_t* idx, int T, int topk,
+               const void* x, void* y, int out_f32, int E_local, int e0, int N, int K, vkb_stream_t stream);
+/* Prompt GEMM, row split: this rank holds weight rows [r N/G, (r+1) N/G) (q_local, s_local in the vkb_gemm_q4_tc
+ * layout, N/G rows); x [M][K] on every rank. After the call every rank's y [M][N] is the full product. work: device
+ * memory of vkb_gemm_rowsplit_work_bytes(M, N, out_f32) bytes (caller-owned). N must be divisible by the rank count. */
+size_t vkb_gemm_rowsplit_work_bytes(int M, int N, int out_f32);
+int vkb_gemm_q4_tc_rowsplit(vkb_comm_t* comm, const void* q_local, const void* s_local, const void* x, void* y,
+                            void* work, int N, int K, int M, vkb_stream_t stream);
+int vkb_gemm_q4_tc_rowsplit_f32(vkb_comm_t* comm, const void* q_local, const void* s_local, const void* x, float* y,
+                                void* work, int N, int K, int M, vkb_stream_t stream);
+
 /* ---- status --------------------------------------------------------------------------------------------------------- */
 /* Human-readable text of a return code. */
 const char* vkb_strerror(int code);

@@ -1,0 +1,183 @@
+// libvkb.so, multi-GPU: the communicator (one NCCL rank per GPU, one process per GPU) and the two sharded paths.
+//
+//   MoE, expert parallel: rank r holds experts [e0, e0 + E_local) and runs the one-launch MoE kernel over the full
+//   index list, writing its own slots and zeros into every other slot; one in-place ncclAllReduce(sum) combines the
+//   ranks. Each slot has exactly one non-zero contributor, so the sum is exact and equal to the one-GPU result.
+//
+//   Prompt GEMM, row split: rank r holds weight rows [r N/G, (r+1) N/G). The tcgen05 kernel writes its [M][N/G] slice
+//   into block r of a [G][M][N/G] workspace, an in-place ncclAllGather fills the other blocks, and a permute kernel
+//   writes y [M][N] (y[m][g N/G + n] = work[g][m][n]).
+//
+// Every rank takes the same collective steps in the same order: argument checks depend only on values that are equal
+// on all ranks (shapes, counts), and once they pass, the collective runs even if the local launch failed, so that no
+// rank is left waiting; the call then returns the first error.
+#include <cuda_runtime.h>
+#include <nccl.h>
+
+#include <cstdint>
+#include <cstring>
+#include <new>
+
+#include "../../include/vkb.h"
+#include "ptx.cuh"
+#include "vkb_internal.h"
+
+struct vkb_comm {
+    ncclComm_t nc;
+    int rank, size, dev;
+};
+
+namespace vkb {
+
+VKB_STATUS_ACCESSOR(status_take_comm)
+
+static int nccl_rc(ncclResult_t r) { return r == ncclSuccess ? 0 : -(VKB_NCCL_BASE + (int)r); }
+
+// y[m][g * nl + n] = work[g][m][n], 16 bytes per thread step when rows allow it.
+template <typename T>
+__global__ void __launch_bounds__(256) gather_permute_kernel(const T* __restrict__ work, T* __restrict__ y, int M, int nl,
+                                                             int G, int vec) {
+    pdl_wait();
+    constexpr int V = 16 / sizeof(T);
+    const long long total = (long long)G * M * nl;
+    const long long step = (long long)gridDim.x * blockDim.x * (vec ? V : 1);
+    for (long long i = ((long long)blockIdx.x * blockDim.x + threadIdx.x) * (vec ? V : 1); i < total; i += step) {
+        const long long g = i / ((long long)M * nl), rem = i - g * M * nl;
+        const long long m = rem / nl, n = rem - m * nl;
+        T* dst = y + m * (long long)G * nl + g * nl + n;
+        if (vec)
+            *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(work + i);
+        else
+            *dst = work[i];
+    }
+}
+
+template <typename T>
+static int launch_permute(const void* work, void* y, int M, int nl, int G, cudaStream_t st) {
+    const long long total = (long long)G * M * nl;
+    // 16-byte copies need 16-byte aligned buffers and rows that are whole vectors
+    const int vec = (nl % (16 / (int)sizeof(T))) == 0 && (reinterpret_cast<uintptr_t>(work) & 15u) == 0 &&
+                    (reinterpret_cast<uintptr_t>(y) & 15u) == 0;
+    const long long per = vec ? 16 / (long long)sizeof(T) : 1;
+    long long blocks = (total / per + 255) / 256;
+    if (blocks > 4096) blocks = 4096;
+    if (blocks < 1) blocks = 1;
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3((unsigned)blocks);
+    cfg.blockDim = dim3(256);
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl_enabled() && pdl_stream_ok(st) ? 1 : 0;
+    const cudaError_t e =
+        cudaLaunchKernelEx(&cfg, gather_permute_kernel<T>, (const T*)work, (T*)y, M, nl, G, vec);
+    return e == cudaSuccess ? 0 : -(int)e;
+}
+
+static int rowsplit(vkb_comm_t* c, const void* q, const void* s, const void* x, void* y, void* work, bool f32, int N,
+                    int K, int M, cudaStream_t st) {
+    if (!c) return VKB_ENOCOMM;
+    if (!q || !s || !x || !y || !work) return VKB_EINVAL;
+    // shape checks (equal on every rank): a failure here returns before any rank reaches the collective
+    if (N < 1 || M < 1 || K < 256) return VKB_EINVAL;
+    if (N % c->size != 0 || K % 256 != 0 || K > 7680) return VKB_EUNSUPPORTED;
+    const int nl = N / c->size;
+    const size_t esz = f32 ? 4 : 2;
+    const size_t chunk = (size_t)M * nl;                    // elements per rank
+    uint8_t* mine = static_cast<uint8_t*>(work) + (size_t)c->rank * chunk * esz;
+    // a local refusal past this point (e.g. an unaligned pointer on one rank) still joins the collective
+    int rc = tc_dispatch(q, s, x, mine, f32, nl, K, M, st);
+    const int rc_nccl = nccl_rc(ncclAllGather(mine, work, chunk, f32 ? ncclFloat : ncclHalf, c->nc, st));
+    if (rc == 0) rc = rc_nccl;
+    const int rc_p = f32 ? launch_permute<float>(work, y, M, nl, c->size, st)
+                         : launch_permute<__half>(work, y, M, nl, c->size, st);
+    return rc != 0 ? rc : rc_p;
+}
+
+static int moe_ep(vkb_comm_t* c, int fmt, const void* qpool, const void* spool, const int32_t* idx, int T, int topk,
+                  const void* x, void* y, bool f32, int E_local, int e0, int N, int K, cudaStream_t st) {
+    if (!c) return VKB_ENOCOMM;
+    if (!idx || !y) return VKB_EINVAL;
+    // the kernel's checks are shape checks (equal on every rank; unaligned buffers take the general kernel, not a
+    // refusal), so a refusal here happens on every rank before any reaches the collective
+    int rc = qmv_dispatch(fmt, qpool, spool, x, y, f32, idx, N, K, T, topk, E_local, e0, 1, st);
+    if (rc > 0) return rc;
+    const size_t count = (size_t)T * topk * N;
+    const int rc_nccl = nccl_rc(ncclAllReduce(y, y, count, f32 ? ncclFloat : ncclHalf, ncclSum, c->nc, st));
+    return rc != 0 ? rc : rc_nccl;
+}
+
+}  // namespace vkb
+
+using namespace vkb;
+
+extern "C" {
+
+int vkb_comm_unique_id(void* id) {
+    if (!id) return VKB_EINVAL;
+    ncclUniqueId u;
+    const int rc = nccl_rc(ncclGetUniqueId(&u));
+    if (rc) return rc;
+    static_assert(sizeof(ncclUniqueId) == VKB_UNIQUE_ID_BYTES, "NCCL unique id size");
+    memcpy(id, &u, sizeof(u));
+    return 0;
+}
+
+int vkb_comm_init(vkb_comm_t** comm, int rank, int nranks, const void* id) {
+    if (!comm || !id) return VKB_EINVAL;
+    *comm = nullptr;
+    if (nranks < 1 || rank < 0 || rank >= nranks) return VKB_EINVAL;
+    int dev = 0;
+    if (int r = current_device(&dev)) return r;
+    ncclUniqueId u;
+    memcpy(&u, id, sizeof(u));
+    ncclComm_t nc = nullptr;
+    const int rc = nccl_rc(ncclCommInitRank(&nc, nranks, u, rank));
+    if (rc) return rc;
+    vkb_comm* c = new (std::nothrow) vkb_comm{nc, rank, nranks, dev};
+    if (!c) {
+        ncclCommDestroy(nc);
+        return VKB_EINVAL;
+    }
+    *comm = c;
+    return 0;
+}
+
+int vkb_comm_destroy(vkb_comm_t* comm) {
+    if (!comm) return 0;
+    const int rc = nccl_rc(ncclCommDestroy(comm->nc));
+    delete comm;
+    return rc;
+}
+
+int vkb_comm_rank(const vkb_comm_t* comm) { return comm ? comm->rank : -1; }
+int vkb_comm_size(const vkb_comm_t* comm) { return comm ? comm->size : -1; }
+
+int vkb_moe_ep(vkb_comm_t* comm, int fmt, const void* qpool, const void* spool, const int32_t* idx, int T, int topk,
+               const void* x, void* y, int out_f32, int E_local, int e0, int N, int K, vkb_stream_t stream) {
+    return moe_ep(comm, fmt, qpool, spool, idx, T, topk, x, y, out_f32 != 0, E_local, e0, N, K, (cudaStream_t)stream);
+}
+
+int vkb_moe_q4_ep(vkb_comm_t* comm, const void* qpool, const void* spool, const int32_t* idx, int T, int topk,
+                  const void* x, void* y, int E_local, int e0, int N, int K, vkb_stream_t stream) {
+    return moe_ep(comm, VKB_FMT_Q4, qpool, spool, idx, T, topk, x, y, false, E_local, e0, N, K, (cudaStream_t)stream);
+}
+
+size_t vkb_gemm_rowsplit_work_bytes(int M, int N, int out_f32) {
+    if (M < 1 || N < 1) return 0;
+    return (size_t)M * N * (out_f32 ? 4 : 2);
+}
+
+int vkb_gemm_q4_tc_rowsplit(vkb_comm_t* comm, const void* q_local, const void* s_local, const void* x, void* y,
+                            void* work, int N, int K, int M, vkb_stream_t stream) {
+    return rowsplit(comm, q_local, s_local, x, y, work, false, N, K, M, (cudaStream_t)stream);
+}
+
+int vkb_gemm_q4_tc_rowsplit_f32(vkb_comm_t* comm, const void* q_local, const void* s_local, const void* x, float* y,
+                                void* work, int N, int K, int M, vkb_stream_t stream) {
+    return rowsplit(comm, q_local, s_local, x, y, work, true, N, K, M, (cudaStream_t)stream);
+}
+
+}  // extern "C"

@@ -54,6 +54,7 @@ struct QmvArgs {
     int T;                   // dense: tokens (M); MoE: tokens
     int topk;                // MoE: slots per token
     int E_local, e0;         // MoE: experts held in this pool, id of the first one
+    int zero_foreign;        // MoE: write zeros into the slots of experts outside the pool (expert-parallel combine)
     int KS, nchunks;         // stage width in k values, stages per row tile
     int cpitch, spitch;      // shared bytes per row of a stage: codes (KS*bits/8 + pad), scales (KS/16 + 16)
     int nstage;              // ring depth
@@ -454,6 +455,16 @@ qmv_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUten
     const uint32_t s_row = (uint32_t)(QMV_ROWS * a.cpitch) + g * sp;     // row g's scales inside a stage
     OutT* y = reinterpret_cast<OutT*>(a.y);
     pdl_wait();   // x and y may still be written (or y read) by the previous grid
+    if constexpr (MODE == QMV_MOE) {
+        if (a.zero_foreign) {   // another rank computes these slots; the combine adds this rank's zeros to them
+            const int nslots = a.T * a.topk;
+            for (int i = blockIdx.x; i < nslots; i += gridDim.x) {
+                const int e = __ldg(a.idx + i) - a.e0;
+                if (e >= 0 && e < a.E_local) continue;
+                for (int n = threadIdx.x; n < a.N; n += QMV_NW * 32) y[(size_t)i * a.N + n] = to_out<OutT>(0.f);
+            }
+        }
+    }
 
     int cur_seg = -1, segs_seen = 0, cnt = 0;
     uint32_t xrow = 0;

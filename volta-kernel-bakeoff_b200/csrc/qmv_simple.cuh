@@ -26,7 +26,7 @@ template <int F, typename OutT>
 __global__ void __launch_bounds__(256) qmv_simple_kernel(const void* __restrict__ q, const __half* __restrict__ s,
                                                          const __half* __restrict__ x, OutT* __restrict__ y,
                                                          const int32_t* __restrict__ idx, int N, int K, int M,
-                                                         int topk, int E_local, int e0) {
+                                                         int topk, int E_local, int e0, int zero_foreign) {
     pdl_wait();
     const int lane = threadIdx.x & 31;
     const int row = (int)((blockIdx.x * (size_t)blockDim.x + threadIdx.x) >> 5);
@@ -36,7 +36,10 @@ __global__ void __launch_bounds__(256) qmv_simple_kernel(const void* __restrict_
     if (idx != nullptr) {
         slot = blockIdx.y;
         const int e = __ldg(idx + slot) - e0;
-        if (e < 0 || e >= E_local) return;
+        if (e < 0 || e >= E_local) {   // another rank's expert: zero for the expert-parallel combine, or untouched
+            if (zero_foreign && lane == 0) y[(size_t)slot * N + row] = to_out<OutT>(0.f);
+            return;
+        }
         wrow = (size_t)e * N + row;
         ntok = 1;
         tok0 = slot / topk;

@@ -19,7 +19,7 @@ namespace vkb {
 VKB_STATUS_ACCESSOR(status_take_qmv)
 
 StatusList status_accessors() {
-    static const StatusTake list[] = {status_take_qmv};
+    static const StatusTake list[] = {status_take_qmv, status_take_comm};
     return {list, list + sizeof(list) / sizeof(list[0])};
 }
 
@@ -49,7 +49,7 @@ int current_device(int* dev) {
 thread_local int t_pdl = -1;
 // PDL is not used on the legacy NULL stream, whose implicit synchronisation with every other stream does not mix
 // with programmatic serialisation; any created stream (or the per-thread default stream) gets it.
-static bool pdl_stream_ok(cudaStream_t st) { return st != nullptr && st != cudaStreamLegacy; }
+bool pdl_stream_ok(cudaStream_t st) { return st != nullptr && st != cudaStreamLegacy; }
 bool pdl_enabled() {
     if (t_pdl < 0) {
         const char* e = getenv("VKB_PDL");
@@ -240,7 +240,7 @@ static int launch_qmv(const QmvPlan& p, const CUtensorMap& tq, const CUtensorMap
 
 template <int F, typename OutT>
 static int launch_simple(const void* q, const void* s, const void* x, void* y, const int32_t* idx, int N, int K,
-                         int M, int topk, int E_local, int e0, int slots, cudaStream_t st) {
+                         int M, int topk, int E_local, int e0, int zero_foreign, int slots, cudaStream_t st) {
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3((unsigned)((N + 7) / 8), (unsigned)(idx ? slots : 1));
     cfg.blockDim = dim3(256);
@@ -251,7 +251,8 @@ static int launch_simple(const void* q, const void* s, const void* x, void* y, c
     cfg.attrs = attr;
     cfg.numAttrs = pdl_enabled() && pdl_stream_ok(st) ? 1 : 0;
     const cudaError_t e = cudaLaunchKernelEx(&cfg, qmv_simple_kernel<F, OutT>, q, (const __half*)s,
-                                             (const __half*)x, (OutT*)y, idx, N, K, M, topk, E_local, e0);
+                                             (const __half*)x, (OutT*)y, idx, N, K, M, topk, E_local, e0,
+                                             zero_foreign);
     return e == cudaSuccess ? 0 : -(int)e;
 }
 
@@ -260,7 +261,7 @@ static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 
 // Common body of the dense and MoE entry points.
 template <int F>
 static int qmv_entry(const void* q, const void* s, const void* x, void* y, bool f32, const int32_t* idx, int N, int K,
-                     int M, int topk, int E_local, int e0, cudaStream_t st) {
+                     int M, int topk, int E_local, int e0, int zero_foreign, cudaStream_t st) {
     const bool moe = idx != nullptr;
     if (!q || !s || !x || !y) return VKB_EINVAL;
     if (N < 1 || K < 32 || M < 1) return VKB_EINVAL;
@@ -294,6 +295,7 @@ static int qmv_entry(const void* q, const void* s, const void* x, void* y, bool 
         p.a.topk = topk;
         p.a.E_local = E_local;
         p.a.e0 = e0;
+        p.a.zero_foreign = zero_foreign;
         int grid;
         if (moe) {
             grid = d.sm_count;
@@ -310,16 +312,16 @@ static int qmv_entry(const void* q, const void* s, const void* x, void* y, bool 
     if (F != FMT_Q8 && (reinterpret_cast<uintptr_t>(q) & 3u)) return VKB_EUNSUPPORTED;
     if ((reinterpret_cast<uintptr_t>(s) | reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(y)) & 1u)
         return VKB_EUNSUPPORTED;
-    return f32 ? launch_simple<F, float>(q, s, x, y, idx, N, K, M, topk, E_local, e0, slots, st)
-               : launch_simple<F, __half>(q, s, x, y, idx, N, K, M, topk, E_local, e0, slots, st);
+    return f32 ? launch_simple<F, float>(q, s, x, y, idx, N, K, M, topk, E_local, e0, zero_foreign, slots, st)
+               : launch_simple<F, __half>(q, s, x, y, idx, N, K, M, topk, E_local, e0, zero_foreign, slots, st);
 }
 
-static int qmv_dispatch(int fmt, const void* q, const void* s, const void* x, void* y, bool f32, const int32_t* idx,
-                        int N, int K, int M, int topk, int E_local, int e0, cudaStream_t st) {
+int qmv_dispatch(int fmt, const void* q, const void* s, const void* x, void* y, bool f32, const int32_t* idx, int N,
+                 int K, int M, int topk, int E_local, int e0, int zero_foreign, cudaStream_t st) {
     switch (fmt) {
-        case VKB_FMT_Q4: return qmv_entry<FMT_Q4>(q, s, x, y, f32, idx, N, K, M, topk, E_local, e0, st);
-        case VKB_FMT_Q8: return qmv_entry<FMT_Q8>(q, s, x, y, f32, idx, N, K, M, topk, E_local, e0, st);
-        case VKB_FMT_Q2: return qmv_entry<FMT_Q2>(q, s, x, y, f32, idx, N, K, M, topk, E_local, e0, st);
+        case VKB_FMT_Q4: return qmv_entry<FMT_Q4>(q, s, x, y, f32, idx, N, K, M, topk, E_local, e0, zero_foreign, st);
+        case VKB_FMT_Q8: return qmv_entry<FMT_Q8>(q, s, x, y, f32, idx, N, K, M, topk, E_local, e0, zero_foreign, st);
+        case VKB_FMT_Q2: return qmv_entry<FMT_Q2>(q, s, x, y, f32, idx, N, K, M, topk, E_local, e0, zero_foreign, st);
         default: return VKB_EUNSUPPORTED;
     }
 }
@@ -441,6 +443,10 @@ static int tc_entry(const void* q, const void* s, const void* x, void* y, int N,
     return e == cudaSuccess ? 0 : -(int)e;
 }
 
+int tc_dispatch(const void* q, const void* s, const void* x, void* y, bool f32, int N, int K, int M, cudaStream_t st) {
+    return f32 ? tc_entry<float>(q, s, x, y, N, K, M, st) : tc_entry<__half>(q, s, x, y, N, K, M, st);
+}
+
 }  // namespace vkb
 
 using namespace vkb;
@@ -449,7 +455,7 @@ extern "C" {
 
 int vkb_gemv(int fmt, const void* q, const void* s, const void* x, void* y, int out_f32, int N, int K, int M,
              vkb_stream_t stream) {
-    return qmv_dispatch(fmt, q, s, x, y, out_f32 != 0, nullptr, N, K, M, 0, 0, 0, (cudaStream_t)stream);
+    return qmv_dispatch(fmt, q, s, x, y, out_f32 != 0, nullptr, N, K, M, 0, 0, 0, 0, (cudaStream_t)stream);
 }
 int vkb_gemv_q4(const void* q, const void* s, const void* x, void* y, int N, int K, int M, vkb_stream_t stream) {
     return vkb_gemv(VKB_FMT_Q4, q, s, x, y, 0, N, K, M, stream);
@@ -473,7 +479,8 @@ int vkb_gemv_q2_f32(const void* q, const void* s, const void* x, float* y, int N
 int vkb_moe(int fmt, const void* qpool, const void* spool, const int32_t* idx, int T, int topk, const void* x,
             void* y, int out_f32, int E_local, int e0, int N, int K, vkb_stream_t stream) {
     if (!idx) return VKB_EINVAL;
-    return qmv_dispatch(fmt, qpool, spool, x, y, out_f32 != 0, idx, N, K, T, topk, E_local, e0, (cudaStream_t)stream);
+    return qmv_dispatch(fmt, qpool, spool, x, y, out_f32 != 0, idx, N, K, T, topk, E_local, e0, 0,
+                        (cudaStream_t)stream);
 }
 int vkb_moe_q4(const void* qpool, const void* spool, const int32_t* idx, int T, int topk, const void* x, void* y,
                int E_local, int e0, int N, int K, vkb_stream_t stream) {

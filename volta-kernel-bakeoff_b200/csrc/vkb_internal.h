@@ -26,9 +26,17 @@ bool pdl_enabled();
 int get_tmap_2d(CUtensorMap* out, const void* ptr, uint64_t rows, uint64_t row_bytes, CUtensorMapDataType dtype,
                 uint32_t elem_bytes, uint32_t box0, uint32_t box1, CUtensorMapSwizzle swz);
 
+// The decode / MoE entry (formats VKB_FMT_*; idx == nullptr: dense) and the prompt GEMM entry, shared with the
+// multi-GPU entry points. Same return codes as the C ABI.
+int qmv_dispatch(int fmt, const void* q, const void* s, const void* x, void* y, bool f32, const int32_t* idx, int N,
+                 int K, int M, int topk, int E_local, int e0, int zero_foreign, cudaStream_t st);
+int tc_dispatch(const void* q, const void* s, const void* x, void* y, bool f32, int N, int K, int M, cudaStream_t st);
+bool pdl_stream_ok(cudaStream_t st);
+
 // Host accessors of the per-translation-unit device status words (read and clear, OR into *bits).
 using StatusTake = int (*)(unsigned*);
 int status_take_qmv(unsigned* bits);
+int status_take_comm(unsigned* bits);
 struct StatusList {
     const StatusTake* b;
     const StatusTake* e;

@@ -81,13 +81,16 @@ def _register_optional(L) -> None:
     opt = {
         "vkb_gemm_q4_tc": ([vp, vp, vp, vp, i, i, i, vp], i),
         "vkb_gemm_q4_tc_f32": ([vp, vp, vp, vp, i, i, i, vp], i),
-        "vkb_dequant_q4": ([vp, vp, vp, i, i, vp], i),
-        "vkb_comm_init": ([i, i, vp, vp], i),
-        "vkb_comm_destroy": ([vp], i),
         "vkb_comm_unique_id": ([vp], i),
-        "vkb_comm_unique_id_bytes": ([], i),
-        "vkb_moe_q4_ep": ([vp, vp, vp, vp, i, i, vp, vp, i, i, i, vp], i),
-        "vkb_gemm_q4_tc_rowsplit": ([vp, vp, vp, vp, vp, i, i, i, vp, vp], i),
+        "vkb_comm_init": ([ctypes.POINTER(vp), i, i, vp], i),
+        "vkb_comm_destroy": ([vp], i),
+        "vkb_comm_rank": ([vp], i),
+        "vkb_comm_size": ([vp], i),
+        "vkb_moe_q4_ep": ([vp, vp, vp, vp, i, i, vp, vp, i, i, i, i, vp], i),
+        "vkb_moe_ep": ([vp, i, vp, vp, vp, i, i, vp, vp, i, i, i, i, i, vp], i),
+        "vkb_gemm_rowsplit_work_bytes": ([i, i, i], ctypes.c_size_t),
+        "vkb_gemm_q4_tc_rowsplit": ([vp, vp, vp, vp, vp, vp, i, i, i, vp], i),
+        "vkb_gemm_q4_tc_rowsplit_f32": ([vp, vp, vp, vp, vp, vp, i, i, i, vp], i),
     }
     for name, (args, res) in opt.items():
         if hasattr(L, name):
@@ -207,6 +210,19 @@ def moe(fmt: int, qpool, spool, idx, x, y=None, E_local: int | None = None, e0: 
     rc = lib().vkb_moe(fmt, _ptr(qpool), _ptr(spool), _ptr(idx), T, topk, _ptr(x), _ptr(y), int(out_f32),
                        E if E_local is None else E_local, e0, N, K, _stream(stream))
     check(rc, "vkb_moe")
+    return y
+
+
+def gemm_tc(q, s, x, y=None, out_f32: bool = False, stream=None):
+    """Prompt GEMM on tcgen05 (Q4): y[M][N] = x[M][K] . W[N][K]^T for any M. q: packed Q4 codes, s: fp16 [N][K/32],
+    x: fp16 [M][K]. Returns y (fp16, or fp32 with out_f32)."""
+    torch = _torch()
+    M, K = x.shape
+    N = s.shape[0]
+    if y is None:
+        y = torch.empty((M, N), dtype=torch.float32 if out_f32 else torch.float16, device=x.device)
+    fn = lib().vkb_gemm_q4_tc_f32 if out_f32 else lib().vkb_gemm_q4_tc
+    check(fn(_ptr(q), _ptr(s), _ptr(x), _ptr(y), N, K, M, _stream(stream)), "vkb_gemm_q4_tc")
     return y
 
 
