@@ -95,6 +95,8 @@ typedef struct vkb_comm vkb_comm_t;
 #define VKB_UNIQUE_ID_BYTES 128
 /* Rank 0 creates the id; the caller distributes the 128 bytes to every rank (any host channel). */
 int vkb_comm_unique_id(void* id);
+/* Collective over the ranks: creates the NCCL communicator and runs warm-up collectives (4 MiB per rank, a temporary
+ * device buffer), so that NCCL's lazily created connection buffers exist before the first vkb call. */
 int vkb_comm_init(vkb_comm_t** comm, int rank, int nranks, const void* id);
 int vkb_comm_destroy(vkb_comm_t* comm);
 int vkb_comm_rank(const vkb_comm_t* comm);
@@ -114,6 +116,13 @@ int vkb_gemm_q4_tc_rowsplit(vkb_comm_t* comm, const void* q_local, const void* s
                             void* work, int N, int K, int M, vkb_stream_t stream);
 int vkb_gemm_q4_tc_rowsplit_f32(vkb_comm_t* comm, const void* q_local, const void* s_local, const void* x, float* y,
                                 void* work, int N, int K, int M, vkb_stream_t stream);
+/* The same (fp16 y) with no workspace argument and no allocation: the workspace is a static device array of the
+ * library, 16 MiB per device, looked up once per device. No counterpart in the reference. M * N * 2 must not exceed
+ * VKB_ROWSPLIT_NOALLOC_MAX_BYTES (VKB_EUNSUPPORTED otherwise, nothing launched). Calls that overlap in time on one
+ * device (other streams, host threads or communicators) share the array and race: serialise them. */
+#define VKB_ROWSPLIT_NOALLOC_MAX_BYTES (16u << 20)
+int vkb_gemm_q4_tc_rowsplit_noalloc(vkb_comm_t* comm, const void* q_local, const void* s_local, const void* x, void* y,
+                                    int N, int K, int M, vkb_stream_t stream);
 
 /* ---- status --------------------------------------------------------------------------------------------------------- */
 /* Human-readable text of a return code. */

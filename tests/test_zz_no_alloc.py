@@ -1,0 +1,76 @@
+"""vkb_gemm_q4_tc_rowsplit_noalloc: the row-split prompt GEMM with its workspace in the library's static device array
+(no allocation on the call path). On one GPU with a one-rank communicator: two calls in a row (different shapes, then
+the first again) against vkb_gemm_q4_tc_rowsplit with a caller-owned workspace and against vkb_gemm_q4_tc -- bit for
+bit -- and a shape past the array's size refused with nothing written. This file is collected last on purpose: it
+must pass after every other test as well as alone."""
+import ctypes
+
+import numpy as np
+import pytest
+
+import vkb
+from oracle import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+MAX_BYTES = 16 << 20
+
+
+@pytest.fixture(scope="module")
+def comm(cuda):
+    from vkb import dist as D
+    c = D.Comm(0, 1, D.Comm.unique_id())
+    yield c
+    c.close()
+
+
+def _weights(rng, N, K, dev):
+    codes = rng.integers(-8, 8, size=(N, K)).astype(np.int8)
+    scales = rng.uniform(0.004, 0.02, size=(N, K // 32)).astype(np.float16).view(np.uint16)
+    return vkb.to_device_packed(O.pack(O.FMT_Q4, codes), dev), vkb.to_device_f16(scales, dev), codes, scales
+
+
+def _noalloc(comm, q, s, x, y, N, K, M):
+    return vkb.lib().vkb_gemm_q4_tc_rowsplit_noalloc(comm._h, vkb._ptr(q), vkb._ptr(s), vkb._ptr(x), vkb._ptr(y),
+                                                     N, K, M, vkb._stream())
+
+
+def test_two_calls_in_a_row_match(comm, cuda):
+    import torch
+    rng = np.random.default_rng(77)
+    cases = [(1024, 2048, 64), (2048, 2560, 512), (1024, 2048, 64)]
+    made = {}
+    for N, K, M in cases:
+        if (N, K, M) not in made:
+            q, s, codes, scales = _weights(rng, N, K, cuda)
+            x_np = rng.uniform(-1, 1, size=(M, K)).astype(np.float16).view(np.uint16)
+            made[(N, K, M)] = (q, s, vkb.to_device_f16(x_np, cuda), codes, scales, x_np)
+    outs = []
+    for N, K, M in cases:                      # back to back on one stream, no synchronisation in between
+        q, s, x, *_ = made[(N, K, M)]
+        y = torch.full((M, N), float("nan"), dtype=torch.float16, device=cuda)
+        assert _noalloc(comm, q, s, x, y, N, K, M) == 0
+        outs.append(y)
+    torch.cuda.synchronize()
+    for (N, K, M), y in zip(cases, outs):
+        q, s, x, codes, scales, x_np = made[(N, K, M)]
+        y_ws = comm.gemm_rowsplit(q, s, x, N)          # caller-owned workspace
+        y_one = vkb.gemm_tc(q, s, x)                   # single-GPU entry point
+        torch.cuda.synchronize()
+        assert torch.equal(y, y_ws) and torch.equal(y, y_one), (N, K, M)
+        ref, mag = O.ref_value(codes, scales, x_np), O.ref_scale(codes, scales, x_np)
+        assert O.check_error(y.float().cpu().numpy().astype(np.float64), ref, mag)[0] <= O.TOL_FP16
+    assert vkb.device_status() == 0
+
+
+def test_too_large_is_refused(comm, cuda):
+    import torch
+    N, K, M = 8192, 2048, 1025                          # M * N * 2 > 16 MiB
+    assert M * N * 2 > MAX_BYTES
+    q = torch.zeros(N * K // 2, dtype=torch.uint8, device=cuda)
+    s = torch.zeros(N * K // 32, dtype=torch.float16, device=cuda)
+    x = torch.zeros((M, K), dtype=torch.float16, device=cuda)
+    y = torch.full((M, N), 7.0, dtype=torch.float16, device=cuda)
+    assert _noalloc(comm, q, s, x, y, N, K, M) == vkb.EUNSUPPORTED
+    torch.cuda.synchronize()
+    assert bool((y == 7.0).all())

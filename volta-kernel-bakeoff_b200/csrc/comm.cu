@@ -16,6 +16,7 @@
 
 #include <cstdint>
 #include <cstring>
+#include <mutex>
 #include <new>
 
 #include "../../include/vkb.h"
@@ -109,6 +110,24 @@ static int moe_ep(vkb_comm_t* c, int fmt, const void* qpool, const void* spool, 
     return rc != 0 ? rc : rc_nccl;
 }
 
+// Workspace of the allocation-free row-split entry point: a file-scope device array (no cudaMalloc anywhere on that
+// path). Its size bounds M * N * 2 bytes. Every byte is written before it is read (block r by this rank's kernel, the
+// others by the all-gather), so nothing has to be cleared between calls; calls that overlap in time (two streams,
+// two host threads, or two communicators in one process on the same device) share it and race.
+constexpr size_t kRowsplitScratchBytes = (size_t)16 << 20;
+static __device__ __align__(256) uint8_t g_rowsplit_scratch[kRowsplitScratchBytes];
+
+// Device address of the array on device `dev`, looked up once per device (the symbol is per device context).
+static int rowsplit_scratch(int dev, void** out) {
+    static std::once_flag once[kMaxDevices];
+    static void* addr[kMaxDevices];
+    static cudaError_t err[kMaxDevices];
+    std::call_once(once[dev], [dev] { err[dev] = cudaGetSymbolAddress(&addr[dev], g_rowsplit_scratch); });
+    if (err[dev] != cudaSuccess) return -(int)err[dev];
+    *out = addr[dev];
+    return 0;
+}
+
 }  // namespace vkb
 
 using namespace vkb;
@@ -141,6 +160,25 @@ int vkb_comm_init(vkb_comm_t** comm, int rank, int nranks, const void* id) {
         ncclCommDestroy(nc);
         return VKB_EINVAL;
     }
+    // Warm-up collectives of the kinds and sizes the entry points issue: NCCL sets up connection buffers on a
+    // communicator's first use of an algorithm, so this happens here (set-up) rather than inside a later call.
+    const size_t per = (size_t)4 << 20;   // bytes per rank
+    void* tmp = nullptr;
+    cudaError_t e = cudaMalloc(&tmp, per * nranks);
+    int wrc = e == cudaSuccess ? 0 : -(int)e;
+    if (wrc == 0) {
+        const size_t n = per / 2;
+        wrc = nccl_rc(ncclAllGather(static_cast<uint8_t*>(tmp) + (size_t)rank * per, tmp, n, ncclHalf, nc, nullptr));
+        if (wrc == 0) wrc = nccl_rc(ncclAllReduce(tmp, tmp, n, ncclHalf, ncclSum, nc, nullptr));
+        e = cudaStreamSynchronize(nullptr);
+        if (wrc == 0 && e != cudaSuccess) wrc = -(int)e;
+        cudaFree(tmp);
+    }
+    if (wrc != 0) {
+        ncclCommDestroy(nc);
+        delete c;
+        return wrc;
+    }
     *comm = c;
     return 0;
 }
@@ -172,6 +210,18 @@ size_t vkb_gemm_rowsplit_work_bytes(int M, int N, int out_f32) {
 
 int vkb_gemm_q4_tc_rowsplit(vkb_comm_t* comm, const void* q_local, const void* s_local, const void* x, void* y,
                             void* work, int N, int K, int M, vkb_stream_t stream) {
+    return rowsplit(comm, q_local, s_local, x, y, work, false, N, K, M, (cudaStream_t)stream);
+}
+
+int vkb_gemm_q4_tc_rowsplit_noalloc(vkb_comm_t* comm, const void* q_local, const void* s_local, const void* x, void* y,
+                                    int N, int K, int M, vkb_stream_t stream) {
+    if (!comm) return VKB_ENOCOMM;
+    if (N < 1 || M < 1) return VKB_EINVAL;
+    if ((size_t)M * (size_t)N * 2 > kRowsplitScratchBytes) return VKB_EUNSUPPORTED;   // equal on every rank
+    int dev = 0;
+    if (int r = current_device(&dev)) return r;
+    void* work = nullptr;
+    if (int r = rowsplit_scratch(dev, &work)) return r;
     return rowsplit(comm, q_local, s_local, x, y, work, false, N, K, M, (cudaStream_t)stream);
 }
 

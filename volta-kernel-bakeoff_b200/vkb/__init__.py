@@ -91,6 +91,7 @@ def _register_optional(L) -> None:
         "vkb_gemm_rowsplit_work_bytes": ([i, i, i], ctypes.c_size_t),
         "vkb_gemm_q4_tc_rowsplit": ([vp, vp, vp, vp, vp, vp, i, i, i, vp], i),
         "vkb_gemm_q4_tc_rowsplit_f32": ([vp, vp, vp, vp, vp, vp, i, i, i, vp], i),
+        "vkb_gemm_q4_tc_rowsplit_noalloc": ([vp, vp, vp, vp, vp, i, i, i, vp], i),
     }
     for name, (args, res) in opt.items():
         if hasattr(L, name):
