@@ -17,6 +17,10 @@ median), including configs[0] (Q4_0 8192x2048, 1 token).
 Multi-GPU: the dense GEMV does not shard (replicas only): every rank runs the whole step on its own GPU; value sums the
 ranks' bytes over the slowest rank's time (weak scaling).
 
+Extra fields of the same JSON line: "prompt_gemm" (configs[4]: the tcgen05 Q4 prompt GEMM at 64 and 512 tokens against
+cuBLAS bf16 on the same GPU), "moe" (configs[2]/[3] one-launch MoE, µs per call), and with N > 1 GPUs "sharded": the
+expert-parallel MoE and the row-split prompt GEMM across the ranks (max over ranks).
+
 The reference arm (--impl reference) times the reference's own CPU path, ref_value (src/bakeoff.cu:221-227, compiled
 from the reference source into oracle/_ref/ by oracle/Makefile), on all host cores over a bounded sample of each
 step's outputs, scaled to the full step.
@@ -161,6 +165,144 @@ def host_cases(for_cpu: bool = True):
                 x = vkb.to_f16_bits(vkb.synth_normal(1 + M, (M, K), 1.0))
                 cases.append(dict(fname=fname, fmt=fmt, bw=bw, N=N, K=K, M=M, codes=codes, scales=scales, x=x))
     return cases
+
+
+# ---- extra sections: prompt GEMM, MoE, sharded paths -------------------------------------------------------------
+
+PROMPT_SHAPES = [(12288, 2560), (8192, 2048)]          # configs[4]
+PROMPT_TOKENS = [64, 512]
+MOE_CASES = [  # configs[2] and configs[3]: (name, experts, top-k, N, K, token counts)
+    ("qwen36_gate_up_128x512x2048_top8", 128, 8, 512, 2048, [1, 8, 64]),
+    ("qwen36_down_128x2048x512_top8", 128, 8, 2048, 512, [1, 8, 64]),
+    ("flashnext_gate_up_160x640x2560_top10", 160, 10, 640, 2560, [1, 8]),
+]
+
+
+def _median_us(torch, stream, run, calls: int = 50, reps: int = 5, graph: bool = True) -> float:
+    """The reference's time_us: median over reps of `calls` back-to-back calls (run(i) issues call i), captured in one
+    CUDA graph when `graph` (no host launch cost in the number), else launched directly."""
+    for i in range(3):
+        run(i)
+    torch.cuda.synchronize()
+    g = None
+    if graph:
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            for i in range(calls):
+                run(i)
+        g.replay()
+    ts = []
+    for r in range(reps):
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        if g is not None:
+            g.replay()
+        else:
+            for i in range(calls):
+                run(r * calls + i)
+        b.record(stream)
+        b.synchronize()
+        ts.append(a.elapsed_time(b) * 1000.0 / calls)
+    del g
+    return sorted(ts)[len(ts) // 2]
+
+
+def _max_over_ranks(torch, dist, dev, v: float) -> float:
+    if dist is None:
+        return v
+    t = torch.tensor([v], dtype=torch.float64, device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def _copies(nbytes: int, L2: int) -> int:
+    return max(2, math.ceil(4 * L2 / max(1, nbytes)))
+
+
+def prompt_section(torch, vkb, dev, stream, L2, peaks):
+    """configs[4] on one GPU: the tcgen05 prompt GEMM against cuBLAS bf16 (torch.matmul, bf16 in and out) at the same
+    shapes, weights cycled over >= 4x L2 for both."""
+    out = {}
+    for N, K in PROMPT_SHAPES:
+        codes, scales = vkb.quantize(0, vkb.synth_normal(0, (N, K), 0.02))
+        q0 = vkb.to_device_packed(vkb.pack(0, codes), dev)
+        s0 = vkb.to_device_f16(scales, dev)
+        nq = _copies(q0.numel() + 2 * s0.numel(), L2)
+        ql, sl = [q0] + [q0.clone() for _ in range(nq - 1)], [s0] + [s0.clone() for _ in range(nq - 1)]
+        wb = torch.randn(N, K, device=dev, dtype=torch.bfloat16) * 0.02
+        nb = _copies(wb.numel() * 2, L2)
+        wl = [wb] + [wb.clone() for _ in range(nb - 1)]
+        for M in PROMPT_TOKENS:
+            x = vkb.to_device_f16(vkb.to_f16_bits(vkb.synth_normal(5, (M, K), 1.0)), dev)
+            xb = x.to(torch.bfloat16)
+            y = torch.empty((M, N), dtype=torch.float16, device=dev)
+            yb = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
+            us = _median_us(torch, stream, lambda i: vkb.gemm_tc(ql[i % nq], sl[i % nq], x, y=y))
+            us_b = _median_us(torch, stream, lambda i: torch.matmul(xb, wl[i % nb].t(), out=yb))
+            fl = 2.0 * M * N * K
+            out[f"q4_{N}x{K}_m{M}"] = {
+                "us": round(us, 2), "tflops": round(fl / us / 1e6, 1), "cublas_bf16_us": round(us_b, 2),
+                "cublas_bf16_tflops": round(fl / us_b / 1e6, 1), "time_vs_cublas_bf16": round(us_b / us, 3),
+                "frac_of_bf16_peak": round(fl / us / 1e6 / float(peaks.get("bf16_tflops", 1590.0)), 3)}
+        del ql, sl, wl
+    return out
+
+
+def moe_section(torch, vkb, dev, stream, L2, comm=None, rank=0, world=1):
+    import numpy as np
+    """configs[2]/[3]: one-launch MoE over a device index list, T tokens x k distinct experts. With a communicator,
+    the experts are split over the ranks (vkb_moe_ep: own slots + zeros, in-place all-reduce)."""
+    from vkb import dist as D
+    out = {}
+    for name, E, k, N, K, Ts in MOE_CASES:
+        e0, el = D.expert_range(E, world, rank) if comm is not None else (0, E)
+        codes, scales = vkb.quantize(0, vkb.synth_normal(7, (el * N, K), 0.02))
+        q0 = vkb.to_device_packed(vkb.pack(0, codes), dev).view(el, N, -1)
+        s0 = vkb.to_device_f16(scales, dev).view(el, N, K // 32)
+        per_expert = N * K * 0.5625
+        n = _copies(int(el * per_expert), L2)
+        ql, sl = [q0] + [q0.clone() for _ in range(n - 1)], [s0] + [s0.clone() for _ in range(n - 1)]
+        for T in Ts:
+            idx_np = vkb.synth_topk(11 + T, T, E, k)
+            idx = torch.from_numpy(idx_np).to(dev)
+            x = vkb.to_device_f16(vkb.to_f16_bits(vkb.synth_normal(13, (T, K), 1.0)), dev)
+            y = torch.empty((T, k, N), dtype=torch.float16, device=dev)
+            if comm is None:
+                us = _median_us(torch, stream, lambda i: vkb.moe(0, ql[i % n], sl[i % n], idx, x, y=y))
+            else:
+                us = _median_us(torch, stream, lambda i: comm.moe_ep(ql[i % n], sl[i % n], idx, x, E_local=el,
+                                                                      e0=e0, y=y), graph=False)
+            U = len(np.unique(idx_np))
+            nbytes = U * per_expert + idx_np.nbytes + T * K * 2 + T * k * N * 2
+            out[f"{name}_t{T}"] = {"us": round(us, 2), "distinct_experts": U,
+                                   "GBps": round(nbytes / us / 1e3, 1) if comm is None else None}
+        del ql, sl
+    return out
+
+
+def rowsplit_section(torch, vkb, dev, stream, L2, comm, rank, world):
+    """configs[4] with the weight rows split over the ranks (vkb_gemm_q4_tc_rowsplit: local tcgen05 GEMM, in-place
+    all-gather, permute)."""
+    from vkb import dist as D
+    out = {}
+    for N, K in PROMPT_SHAPES:
+        n0, nl = D.row_range(N, world, rank)
+        codes, scales = vkb.quantize(0, vkb.synth_normal(0, (N, K), 0.02)[n0:n0 + nl])
+        q0 = vkb.to_device_packed(vkb.pack(0, codes), dev)
+        s0 = vkb.to_device_f16(scales, dev)
+        nq = _copies(q0.numel() + 2 * s0.numel(), L2)
+        ql, sl = [q0] + [q0.clone() for _ in range(nq - 1)], [s0] + [s0.clone() for _ in range(nq - 1)]
+        for M in PROMPT_TOKENS:
+            x = vkb.to_device_f16(vkb.to_f16_bits(vkb.synth_normal(5, (M, K), 1.0)), dev)
+            y = torch.empty((M, N), dtype=torch.float16, device=dev)
+            work = torch.empty(vkb.lib().vkb_gemm_rowsplit_work_bytes(M, N, 0), dtype=torch.uint8, device=dev)
+            us = _median_us(torch, stream, lambda i: comm.gemm_rowsplit(ql[i % nq], sl[i % nq], x, N, y=y, work=work),
+                            graph=False)
+            out[f"q4_{N}x{K}_m{M}"] = {"us": round(us, 2), "tflops": round(2.0 * M * N * K / us / 1e6, 1),
+                                       "allgather_bytes": M * N * 2}
+        del ql, sl
+    return out
 
 
 # ---- our arm ---------------------------------------------------------------------------------------------------------
@@ -328,14 +470,31 @@ def run_ours(args, rank: int, world: int, local_rank: int, dist):
         dist.all_reduce(te, op=dist.ReduceOp.MAX)
     e2e_value = sbytes * e2e_steps * world / float(te.item()) / 1e9
 
-    if rank != 0:
-        return None
-
     peaks = {}
     try:
         peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
     except (OSError, ValueError):
         pass
+
+    # prompt GEMM and MoE on this GPU (every rank runs them: replicas), then the sharded paths when world > 1
+    prompt = prompt_section(torch, vkb, dev, stream, L2, peaks)
+    moe1 = moe_section(torch, vkb, dev, stream, L2)
+    sharded = None
+    if dist is not None:
+        from vkb import dist as D
+        comm = D.Comm.from_torch()
+        moe_ep = moe_section(torch, vkb, dev, stream, L2, comm, rank, world)
+        rows = rowsplit_section(torch, vkb, dev, stream, L2, comm, rank, world)
+        for d in (moe_ep, rows):
+            for v in d.values():
+                v["us"] = round(_max_over_ranks(torch, dist, dev, v["us"]), 2)
+        torch.cuda.synchronize()
+        comm.close()
+        sharded = {"gpus": world, "moe_expert_parallel": moe_ep, "prompt_row_split": rows,
+                   "timing": "median of 5 x 50 calls, device events, max over ranks; no CUDA graph (NCCL inside)"}
+
+    if rank != 0:
+        return None
     peak = float(peaks.get("hbm_gbs", 6650.0))
     traffic = None
     tf = os.path.join(ROOT, "profiles", "qmv_dram_traffic.json")
@@ -385,6 +544,9 @@ def run_ours(args, rank: int, world: int, local_rank: int, dist):
         "clocks": clocks,
         "cases_us": table,
         "headline": headline,
+        "prompt_gemm": prompt,
+        "moe": moe1,
+        "sharded": sharded,
     }
 
 
