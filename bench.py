@@ -178,16 +178,18 @@ MOE_CASES = [  # configs[2] and configs[3]: (name, experts, top-k, N, K, token c
 ]
 
 
-def _median_us(torch, stream, run, calls: int = 50, reps: int = 5, graph: bool = True) -> float:
+def _median_us(torch, stream, run, calls: int = 50, reps: int = 5, graph: bool = True, vkb_graph: bool = True) -> float:
     """The reference's time_us: median over reps of `calls` back-to-back calls (run(i) issues call i), captured in one
-    CUDA graph when `graph` (no host launch cost in the number), else launched directly."""
+    CUDA graph when `graph` (no host launch cost in the number; vkb calls through the library's own graph helpers,
+    torch calls through torch.cuda.graph), else launched directly."""
+    import vkb
     for i in range(3):
         run(i)
     torch.cuda.synchronize()
     g = None
     if graph:
-        g = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(g, stream=stream):
+        g = vkb.Graph(stream) if vkb_graph else torch.cuda.CUDAGraph()
+        with (g if vkb_graph else torch.cuda.graph(g, stream=stream)):
             for i in range(calls):
                 run(i)
         g.replay()
@@ -239,7 +241,7 @@ def prompt_section(torch, vkb, dev, stream, L2, peaks):
             y = torch.empty((M, N), dtype=torch.float16, device=dev)
             yb = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
             us = _median_us(torch, stream, lambda i: vkb.gemm_tc(ql[i % nq], sl[i % nq], x, y=y))
-            us_b = _median_us(torch, stream, lambda i: torch.matmul(xb, wl[i % nb].t(), out=yb))
+            us_b = _median_us(torch, stream, lambda i: torch.matmul(xb, wl[i % nb].t(), out=yb), vkb_graph=False)
             fl = 2.0 * M * N * K
             out[f"q4_{N}x{K}_m{M}"] = {
                 "us": round(us, 2), "tflops": round(fl / us / 1e6, 1), "cublas_bf16_us": round(us_b, 2),
@@ -355,9 +357,9 @@ def run_ours(args, rank: int, world: int, local_rank: int, dist):
         raise RuntimeError("device-side timeout during warm-up")
 
     graphs = []
-    for j in range(ngraph):
-        g = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(g, stream=stream):
+    for j in range(ngraph):   # the library's graph helpers (vkb_graph_*): one launch per step, nothing else replayed
+        g = vkb.Graph(stream)
+        with g:
             launch_step(j)
         graphs.append(g)
 
@@ -392,8 +394,8 @@ def run_ours(args, rank: int, world: int, local_rank: int, dist):
     # per-case µs/call, the reference's time_us: 5 batches of 50 back-to-back calls, median (graph of 50 calls)
     table = {}
     def time_case(fmt, q_list, s_list, x, y, n):
-        g = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(g, stream=stream):
+        g = vkb.Graph(stream)
+        with g:
             for i in range(50):
                 vkb.gemv(fmt, q_list[i % n], s_list[i % n], x, y=y)
         for _ in range(2):
@@ -530,7 +532,8 @@ def run_ours(args, rank: int, world: int, local_rank: int, dist):
             "tables": [f"{n}x{k}" for n, k in SHAPES], "tokens": TOKENS, "formats": [f[0] for f in FORMATS],
             "parallelism": f"replicas x{world}" if world > 1 else "1 GPU",
             "l2": "inputs larger than L2: every call reads a different copy; each table's copies cycle >= 4x L2",
-            "launch": "one CUDA graph per step (48 vkb_gemv calls, programmatic dependent launch between them)",
+            "launch": "one CUDA graph per step (48 vkb_gemv calls captured with vkb_graph_begin/end, programmatic "
+                      "dependent launch between them)",
             "step_bytes": sbytes,
         },
         "roofline": {"bound": "hbm", "achieved": round(per_gpu, 1), "peak": peak, "unit": "GB/s",

@@ -124,6 +124,16 @@ int vkb_gemm_q4_tc_rowsplit_f32(vkb_comm_t* comm, const void* q_local, const voi
 int vkb_gemm_q4_tc_rowsplit_noalloc(vkb_comm_t* comm, const void* q_local, const void* s_local, const void* x, void* y,
                                     int N, int K, int M, vkb_stream_t stream);
 
+/* ---- CUDA graphs of vkb calls ---------------------------------------------------------------------------------------
+ * Capture a sequence of calls on a stream into one executable graph (a decode step: many short GEMVs) and replay it
+ * with one launch; programmatic dependent launch edges between the captured kernels are kept. No counterpart in the
+ * reference. begin: start capturing `stream` (thread-local mode); end: stop, instantiate, return the executable graph
+ * handle; launch: replay on any stream; destroy: release. Return codes as above. */
+int vkb_graph_begin(vkb_stream_t stream);
+int vkb_graph_end(vkb_stream_t stream, void** graph_exec);
+int vkb_graph_launch(void* graph_exec, vkb_stream_t stream);
+int vkb_graph_destroy(void* graph_exec);
+
 /* ---- status --------------------------------------------------------------------------------------------------------- */
 /* Human-readable text of a return code. */
 const char* vkb_strerror(int code);

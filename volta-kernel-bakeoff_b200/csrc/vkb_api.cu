@@ -495,6 +495,37 @@ int vkb_gemm_q4_tc_f32(const void* q, const void* s, const void* x, float* y, in
     return tc_entry<float>(q, s, x, y, N, K, M, (cudaStream_t)stream);
 }
 
+int vkb_graph_begin(vkb_stream_t stream) {
+    const cudaError_t e = cudaStreamBeginCapture((cudaStream_t)stream, cudaStreamCaptureModeThreadLocal);
+    return e == cudaSuccess ? 0 : -(int)e;
+}
+
+int vkb_graph_end(vkb_stream_t stream, void** graph_exec) {
+    if (!graph_exec) return VKB_EINVAL;
+    *graph_exec = nullptr;
+    cudaGraph_t g = nullptr;
+    cudaError_t e = cudaStreamEndCapture((cudaStream_t)stream, &g);
+    if (e != cudaSuccess) return -(int)e;
+    cudaGraphExec_t ge = nullptr;
+    e = cudaGraphInstantiate(&ge, g, 0);
+    cudaGraphDestroy(g);
+    if (e != cudaSuccess) return -(int)e;
+    *graph_exec = ge;
+    return 0;
+}
+
+int vkb_graph_launch(void* graph_exec, vkb_stream_t stream) {
+    if (!graph_exec) return VKB_EINVAL;
+    const cudaError_t e = cudaGraphLaunch((cudaGraphExec_t)graph_exec, (cudaStream_t)stream);
+    return e == cudaSuccess ? 0 : -(int)e;
+}
+
+int vkb_graph_destroy(void* graph_exec) {
+    if (!graph_exec) return 0;
+    const cudaError_t e = cudaGraphExecDestroy((cudaGraphExec_t)graph_exec);
+    return e == cudaSuccess ? 0 : -(int)e;
+}
+
 const char* vkb_strerror(int code) {
     switch (code) {
         case VKB_OK: return "ok";

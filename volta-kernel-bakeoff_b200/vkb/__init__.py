@@ -92,6 +92,10 @@ def _register_optional(L) -> None:
         "vkb_gemm_q4_tc_rowsplit": ([vp, vp, vp, vp, vp, vp, i, i, i, vp], i),
         "vkb_gemm_q4_tc_rowsplit_f32": ([vp, vp, vp, vp, vp, vp, i, i, i, vp], i),
         "vkb_gemm_q4_tc_rowsplit_noalloc": ([vp, vp, vp, vp, vp, i, i, i, vp], i),
+        "vkb_graph_begin": ([vp], i),
+        "vkb_graph_end": ([vp, ctypes.POINTER(vp)], i),
+        "vkb_graph_launch": ([vp, vp], i),
+        "vkb_graph_destroy": ([vp], i),
     }
     for name, (args, res) in opt.items():
         if hasattr(L, name):
@@ -225,6 +229,38 @@ def gemm_tc(q, s, x, y=None, out_f32: bool = False, stream=None):
     fn = lib().vkb_gemm_q4_tc_f32 if out_f32 else lib().vkb_gemm_q4_tc
     check(fn(_ptr(q), _ptr(s), _ptr(x), _ptr(y), N, K, M, _stream(stream)), "vkb_gemm_q4_tc")
     return y
+
+
+class Graph:
+    """A CUDA graph of vkb calls captured on a stream through the C ABI (vkb_graph_*): replay() launches them all at
+    once. Used like torch.cuda.graph, without torch's per-replay generator bookkeeping."""
+
+    def __init__(self, stream=None):
+        self.stream = stream
+        self._h = ctypes.c_void_p()
+
+    def __enter__(self):
+        check(lib().vkb_graph_begin(_stream(self.stream)), "vkb_graph_begin")
+        return self
+
+    def __exit__(self, exc_type, exc, tb):
+        h = ctypes.c_void_p()
+        rc = lib().vkb_graph_end(_stream(self.stream), ctypes.byref(h))
+        if exc_type is None:
+            check(rc, "vkb_graph_end")
+            self._h = h
+        return False
+
+    def replay(self, stream=None):
+        check(lib().vkb_graph_launch(self._h, _stream(stream if stream is not None else self.stream)),
+              "vkb_graph_launch")
+
+    def __del__(self):
+        try:
+            if self._h:
+                lib().vkb_graph_destroy(self._h)
+        except Exception:
+            pass
 
 
 def to_device_packed(packed: np.ndarray, device="cuda"):
