@@ -226,6 +226,16 @@ tc_q4_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUt
         mbar_init(sfull, 1);
         mbar_init(accum, 1);
         fence_mbar_init();
+        // the weights do not depend on the previous grid: the scales and the first chunks start now, before the TMEM
+        // allocation and the block-wide barrier (the thread that initialised the barriers issues them)
+        prefetch_tmap(&tq);
+        prefetch_tmap(&ts);
+        mbar_arrive_expect_tx(sfull, (uint32_t)(TC_BM * a.spitch));
+        tma_load_2d(sm + a.s_off, &ts, 0, row0, sfull);
+        for (int c = 0; c < min(nch, a.np); ++c) {
+            mbar_arrive_expect_tx(&pfull[c], (uint32_t)PCHUNK);
+            tma_load_2d(sm + a.p_off + c * PCHUNK, &tq, c * PK * 4, row0, &pfull[c]);   // PK x 4 x 8 B of codes
+        }
     }
     if (warp == 1) tmem_alloc(tmem_slot, (uint32_t)a.tmem_cols);
     tc_fence_before();
@@ -238,16 +248,10 @@ tc_q4_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUt
     // tcgen05 / TMA issue path expects; `ok` stays warp-uniform.
     if (warp == 0) {
         // ===================== P ring producer (weights: no dependence on the previous grid) =====================
-        if (elect_one()) {
-            prefetch_tmap(&tq);
-            prefetch_tmap(&ts);
-            mbar_arrive_expect_tx(sfull, (uint32_t)(TC_BM * a.spitch));
-            tma_load_2d(sm + a.s_off, &ts, 0, row0, sfull);
-        }
-        __syncwarp();
-        int b = 0, rnd = 0;
-        for (int c = 0; c < nch; ++c) {
-            if (rnd > 0) ok = __all_sync(0xffffffffu, wait_parity_sleep(&pempty[b], (rnd - 1) & 1));
+        // chunks 0 .. np-1 and the scales were issued at barrier set-up; refill the ring from chunk np on
+        int b = 0, rnd = 1;
+        for (int c = a.np; c < nch; ++c) {
+            ok = __all_sync(0xffffffffu, wait_parity_sleep(&pempty[b], (rnd - 1) & 1));
             if (!ok) break;
             if (elect_one()) {
                 mbar_arrive_expect_tx(&pfull[b], (uint32_t)PCHUNK);
@@ -284,42 +288,75 @@ tc_q4_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUt
             if (!wait_parity_sleep(&xfull[xs % a.nx], (xs / a.nx) & 1, DEV_ERR_DRAIN_TIMEOUT)) break;
     } else if (warp == 1) {
         // ===================== MMA issuer =====================
+        // per slot: wait for its A (TMEM) and the X stages its 4 K steps read, then 16 UMMAs (4 per K step), one A
+        // handshake per slot. When the X ring holds at least two slots of K steps, all of a slot's X waits come first
+        // and the 16 UMMAs issue back to back; otherwise (large token tiles, shallow X ring) the waits interleave
+        // with the K steps, so that each X stage is released as soon as its own MMAs complete.
         const uint32_t idesc = umma_idesc_f16(a.NT);
         const uint32_t xtile = (uint32_t)a.NT * 128;
         const int nslots = nk / TC_SLOT;
+        const bool hoist = a.nx * a.xk >= 2 * TC_SLOT;
         int ab = 0, arnd = 0, xb = 0, xrnd = 0, xj = 0;
         for (int sl = 0; sl < nslots && ok; ++sl) {
             ok = __all_sync(0xffffffffu, wait_parity_sleep(&afull[ab], arnd & 1));
             if (!ok) break;
             tc_fence_after();
             const uint32_t ta = tmem + (uint32_t)(a.a_col0 + ab * TC_SLOT * TC_ACOLS);
+            if (hoist) {
+                uint32_t sb[TC_SLOT];
+                int rel[TC_SLOT];   // X stage to release after K step j (-1: none)
 #pragma unroll
-            for (int j = 0; j < TC_SLOT; ++j) {
-                if (xj == 0) {
-                    ok = __all_sync(0xffffffffu, wait_parity_sleep(&xfull[xb], xrnd & 1));
-                    if (!ok) break;
+                for (int j = 0; j < TC_SLOT; ++j) {
+                    if (xj == 0 && ok) ok = __all_sync(0xffffffffu, wait_parity_sleep(&xfull[xb], xrnd & 1));
+                    sb[j] = smem_u32(sm + a.x_off + xb * a.x_stage) + xj * xtile;
+                    rel[j] = xj + 1 == a.xk ? xb : -1;
+                    if (++xj == a.xk) {
+                        xj = 0;
+                        if (++xb == a.nx) { xb = 0; ++xrnd; }
+                    }
                 }
-                const int it = sl * TC_SLOT + j;
-                const uint32_t sb = smem_u32(sm + a.x_off + xb * a.x_stage) + xj * xtile;
-                const bool last_x = xj + 1 == a.xk;
+                if (!ok) break;
                 if (elect_one()) {
 #pragma unroll
-                    for (int kk = 0; kk < TC_BK / 16; ++kk)   // 16 k: 8 TMEM columns of A, 32 bytes of the B row
-                        umma_f16_ts(tmem, ta + (uint32_t)(j * TC_ACOLS + 8 * kk), umma_desc_sw128(sb + 32 * kk), idesc,
-                                    (it | kk) != 0);
-                    if (last_x) umma_commit(&xempty[xb]);   // the stage's last K step: free it after these MMAs
+                    for (int j = 0; j < TC_SLOT; ++j) {
+                        const int it = sl * TC_SLOT + j;
+#pragma unroll
+                        for (int kk = 0; kk < TC_BK / 16; ++kk)   // 16 k: 8 TMEM columns of A, 32 bytes of the B row
+                            umma_f16_ts(tmem, ta + (uint32_t)(j * TC_ACOLS + 8 * kk), umma_desc_sw128(sb[j] + 32 * kk),
+                                        idesc, (it | kk) != 0);
+                        if (rel[j] >= 0) umma_commit(&xempty[rel[j]]);   // free the stage once these MMAs complete
+                    }
+                    umma_commit(&aempty[ab]);
                 }
                 __syncwarp();
-                if (last_x) {
-                    xj = 0;
-                    if (++xb == a.nx) { xb = 0; ++xrnd; }
-                } else {
-                    ++xj;
+            } else {
+#pragma unroll
+                for (int j = 0; j < TC_SLOT; ++j) {
+                    if (xj == 0) {
+                        ok = __all_sync(0xffffffffu, wait_parity_sleep(&xfull[xb], xrnd & 1));
+                        if (!ok) break;
+                    }
+                    const int it = sl * TC_SLOT + j;
+                    const uint32_t sb = smem_u32(sm + a.x_off + xb * a.x_stage) + xj * xtile;
+                    const bool last_x = xj + 1 == a.xk;
+                    if (elect_one()) {
+#pragma unroll
+                        for (int kk = 0; kk < TC_BK / 16; ++kk)
+                            umma_f16_ts(tmem, ta + (uint32_t)(j * TC_ACOLS + 8 * kk), umma_desc_sw128(sb + 32 * kk),
+                                        idesc, (it | kk) != 0);
+                        if (last_x) umma_commit(&xempty[xb]);
+                        if (j == TC_SLOT - 1) umma_commit(&aempty[ab]);
+                    }
+                    __syncwarp();
+                    if (last_x) {
+                        xj = 0;
+                        if (++xb == a.nx) { xb = 0; ++xrnd; }
+                    } else {
+                        ++xj;
+                    }
                 }
+                if (!ok) break;
             }
-            if (!ok) break;
-            if (elect_one()) umma_commit(&aempty[ab]);
-            __syncwarp();
             if (++ab == a.na) { ab = 0; ++arnd; }
         }
         if (elect_one()) umma_commit(accum);   // arrives when every MMA issued above has completed
@@ -379,56 +416,58 @@ tc_q4_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUt
                 if (lane == 0) mbar_arrive(&afull[ab]);
             }
         }
-        // epilogue: warp reads TMEM lanes 32*(warp % 4).. (weight rows); the two warps of a lane quarter take
-        // alternate 32-token chunks
-        pdl_wait();   // y may still be read or written by the previous grid
-        if (ok && wait_parity_sleep(accum, 0)) {
-            tc_fence_after();
-            const int q = qtr, half = grp;
-            const uint32_t tq_addr = tmem + ((uint32_t)(32 * q) << 16);
-            if (a.tma_store) {
-                // per-warp staging (2 buffers of 32 tokens x 32 rows) in the idle X/P rings: every load has landed
-                // and been consumed before the last MMA completed
-                OutT* stg = reinterpret_cast<OutT*>(sm) + (size_t)dw * 2 * TC_EPI_BOX * TC_EPI_BOX;
-                auto put = [&](uint32_t (&v)[32], int c, int nb) {
-                    OutT* sb = stg + nb * TC_EPI_BOX * TC_EPI_BOX;
-                    if (lane == 0) bulk_wait_group_read<1>();   // the store that last used this buffer has read it
-                    __syncwarp();
-#pragma unroll
-                    for (int j = 0; j < 32; ++j) sb[j * TC_EPI_BOX + lane] = tc_out<OutT>(__uint_as_float(v[j]));
-                    fence_proxy_async_smem();
-                    __syncwarp();
-                    if (lane == 0) {
-                        tma_store_2d(&ty, row0 + 32 * q, tok0 + c, sb);   // clipped at N and M by the tensor map
-                        bulk_commit_group();
-                    }
-                };
-                // two TMEM loads in flight: the next chunk loads while this one is converted and stored
-                uint32_t va[32], vb[32];
-                int c = 32 * half;
-                if (c < a.NT) tmem_ld32_async(tq_addr + (uint32_t)c, va);
-                for (; c < a.NT; c += 128) {
-                    tmem_wait_ld(va);
-                    if (c + 64 < a.NT) tmem_ld32_async(tq_addr + (uint32_t)(c + 64), vb);
-                    put(va, c, 0);
-                    if (c + 64 >= a.NT) break;
-                    tmem_wait_ld(vb);
-                    if (c + 128 < a.NT) tmem_ld32_async(tq_addr + (uint32_t)(c + 128), va);
-                    put(vb, c + 64, 1);
-                }
-                if (lane == 0) bulk_wait_group<0>();
+    }
+    // ===================== epilogue: all twelve warps =====================
+    // warp w reads TMEM lanes 32 (w % 4).. (weight rows); the three warps of a lane quarter (w % 4 equal) take every
+    // third 32-token chunk. Producers and the MMA warp join once their own loads have landed / MMAs are issued.
+    pdl_wait();   // y may still be read or written by the previous grid
+    if (ok && wait_parity_sleep(accum, 0)) {
+        tc_fence_after();
+        const int q = warp & 3, third = warp >> 2;
+        constexpr int STEP = 3 * 32;
+        const uint32_t tq_addr = tmem + ((uint32_t)(32 * q) << 16);
+        if (a.tma_store) {
+            // per-warp staging (2 buffers of 32 tokens x 32 rows) in the idle X/P rings: every load has landed and
+            // been consumed before the last MMA completed
+            OutT* stg = reinterpret_cast<OutT*>(sm) + (size_t)warp * 2 * TC_EPI_BOX * TC_EPI_BOX;
+            auto put = [&](uint32_t (&v)[32], int c, int nb) {
+                OutT* sb = stg + nb * TC_EPI_BOX * TC_EPI_BOX;
+                if (lane == 0) bulk_wait_group_read<1>();   // the store that last used this buffer has read it
                 __syncwarp();
-            } else {
-                const int n = row0 + 32 * q + lane;
-                OutT* y = reinterpret_cast<OutT*>(a.y);
-                for (int c = 32 * half; c < a.NT; c += 64) {
-                    uint32_t v[32];
-                    tmem_ld32(tq_addr + (uint32_t)c, v);
 #pragma unroll
-                    for (int j = 0; j < 32; ++j) {
-                        const int m = tok0 + c + j;
-                        if (m < a.M && n < a.N) y[(size_t)m * a.N + n] = tc_out<OutT>(__uint_as_float(v[j]));
-                    }
+                for (int j = 0; j < 32; ++j) sb[j * TC_EPI_BOX + lane] = tc_out<OutT>(__uint_as_float(v[j]));
+                fence_proxy_async_smem();
+                __syncwarp();
+                if (lane == 0) {
+                    tma_store_2d(&ty, row0 + 32 * q, tok0 + c, sb);   // clipped at N and M by the tensor map
+                    bulk_commit_group();
+                }
+            };
+            // two TMEM loads in flight: the next chunk loads while this one is converted and stored
+            uint32_t va[32], vb[32];
+            int c = 32 * third;
+            if (c < a.NT) tmem_ld32_async(tq_addr + (uint32_t)c, va);
+            for (; c < a.NT; c += 2 * STEP) {
+                tmem_wait_ld(va);
+                if (c + STEP < a.NT) tmem_ld32_async(tq_addr + (uint32_t)(c + STEP), vb);
+                put(va, c, 0);
+                if (c + STEP >= a.NT) break;
+                tmem_wait_ld(vb);
+                if (c + 2 * STEP < a.NT) tmem_ld32_async(tq_addr + (uint32_t)(c + 2 * STEP), va);
+                put(vb, c + STEP, 1);
+            }
+            if (lane == 0) bulk_wait_group<0>();
+            __syncwarp();
+        } else {
+            const int n = row0 + 32 * q + lane;
+            OutT* y = reinterpret_cast<OutT*>(a.y);
+            for (int c = 32 * third; c < a.NT; c += STEP) {
+                uint32_t v[32];
+                tmem_ld32(tq_addr + (uint32_t)c, v);
+#pragma unroll
+                for (int j = 0; j < 32; ++j) {
+                    const int m = tok0 + c + j;
+                    if (m < a.M && n < a.N) y[(size_t)m * a.N + n] = tc_out<OutT>(__uint_as_float(v[j]));
                 }
             }
         }

@@ -376,7 +376,8 @@ static bool plan_tc(int N, int K, int M, int out_bytes, const DeviceInfo& d, TcP
     }
     a.xk = xk;
     a.x_stage = xk * NT * 128;
-    if (2 * TC_NDQ * TC_EPI_BOX * TC_EPI_BOX * out_bytes > nx * a.x_stage + np * pchunk) return false;   // staging
+    if (2 * (TC_THREADS / 32) * TC_EPI_BOX * TC_EPI_BOX * out_bytes > nx * a.x_stage + np * pchunk)
+        return false;   // epilogue staging (two buffers per warp) fits in the X and P rings
     a.na = na; a.nx = nx; a.np = np;
     a.x_off = 0;
     a.p_off = nx * a.x_stage;
