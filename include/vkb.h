@@ -80,7 +80,7 @@ int vkb_moe(int fmt, const void* qpool, const void* spool, const int32_t* idx, i
 /* ---- prompt GEMM on tcgen05: y[M][N] = x[M][K] . W[N][K]^T, any M >= 1 -----------------------------------------------
  * Replaces tc_q4 / tc_q4_v2 (reference src/stage2.cuh:94-154, :226-229; src/stage4_tc.cuh:38-200): the weights are
  * dequantised to fp16 exactly as the reference rounds them ((code - 8) * scale, one rounding) and multiplied on the
- * 5th-generation tensor cores with fp32 accumulation. Needs K % 256 == 0, K <= 7680, 16-byte aligned q, s, x; any M
+ * 5th-generation tensor cores with fp32 accumulation. Needs K % 256 == 0 and 16-byte aligned q, s, x; any M
  * and N (no tile-multiple requirement). fp16 output; _f32 writes fp32 (the reference's float* y). */
 int vkb_gemm_q4_tc(const void* q, const void* s, const void* x, void* y, int N, int K, int M, vkb_stream_t stream);
 int vkb_gemm_q4_tc_f32(const void* q, const void* s, const void* x, float* y, int N, int K, int M,

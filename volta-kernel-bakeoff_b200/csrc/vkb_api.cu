@@ -335,9 +335,11 @@ struct TcPlan {
     dim3 grid;
 };
 
-// Token tile NT (a multiple of 32, <= 256) chosen to minimise waves x per-tile time over the SMs (one CTA per SM);
-// ring depths sized for the latency each ring has to cover (the P ring: HBM, ~4.5k cycles; the X ring: L2; the A
-// ring: the MMA's completion), then shrunk to fit shared memory.
+// Token tile NT (a multiple of 32, <= 256): the persistent grid (one CTA per SM) walks ceil(tiles / grid) tiles per
+// CTA; a K step costs 4 UMMAs of (32 + 0.41 NT) cycles (measured, A in TMEM) or the dequantisation floor, and a
+// single-buffered accumulator (NT > 128) exposes the epilogue once per extra tile. Ring depths: X stages of up to
+// 32 KB (an even count: two producers), P chunks of 8 K steps when they fit (else 4), both deepened while shared
+// memory lasts.
 static bool plan_tc(int N, int K, int M, int out_bytes, const DeviceInfo& d, TcPlan* p) {
     TcArgs& a = p->a;
     const int tiles_n = (N + TC_BM - 1) / TC_BM;
@@ -345,54 +347,61 @@ static bool plan_tc(int N, int K, int M, int out_bytes, const DeviceInfo& d, TcP
     int NT = 0;
     double best = 1e300;
     const int nt_max = round_up(M, 32) < 256 ? round_up(M, 32) : 256;
+    static const int nt_force = getenv("VKB_TC_NT") ? atoi(getenv("VKB_TC_NT")) : 0;   // tuning override
     for (int nt = nt_max; nt >= 32; nt -= 32) {
+        if (nt_force > 0 && nt != nt_force && nt_force <= nt_max) continue;
         const long tiles = (long)tiles_n * ((M + nt - 1) / nt);
-        const long waves = (tiles + d.sm_count - 1) / d.sm_count;
-        const double step = nt * 2.0 > 160.0 ? nt * 2.0 : 160.0;   // cycles per K step: MMA or the dequant floor
-        const double t = (double)waves * (nk * step + 3000.0);
+        const long grid = tiles < d.sm_count ? tiles : d.sm_count;
+        const long per_cta = (tiles + grid - 1) / grid;
+        const double umma = 4.0 * (32.0 + 0.41 * nt);
+        const double step = umma > 180.0 ? umma : 180.0;
+        const double epi = nt <= 128 ? 0.0 : 1500.0 + 10.0 * nt;
+        const double t = (double)per_cta * nk * step + (double)(per_cta - 1) * epi + 6000.0;
         if (t < best * 0.999) { best = t; NT = nt; }
     }
     a.M = M; a.N = N; a.K = K; a.NT = NT; a.nk = nk;
-    p->pk = nk % 8 == 0 ? 8 : 4;   // K steps per packed chunk (K % 256 == 0 gives nk % 4 == 0)
-    const int pchunk = tc_pchunk(p->pk);
-    a.spitch = K / 16 + (((K / 256) % 2 == 0) ? 16 : 0);   // pitch / 16 odd: conflict-free 16-byte scale reads
-    const int sbytes = round_up(TC_BM * a.spitch, 1024);
-    const int na = 2;   // TMEM: accumulators [0, NT <= 256), A ring of two 128-column slots from column 256
+    a.tiles_n = tiles_n;
+    a.tiles = tiles_n * ((M + NT - 1) / NT);
+    a.na = 2;
+    a.nacc = NT <= 128 ? 2 : 1;   // TMEM: accumulators at columns 0 / 128, A ring of two 128-column slots from 256
     a.a_col0 = 256;
     a.tmem_cols = 512;
-    // X stages of up to 32 KB (xk K steps per TMA box; two producer warps alternate stages, so nx is even), P
-    // chunks at least two; then deepen the P ring (HBM latency) and the X ring while shared memory lasts
     int xk = 8;
     while (xk > 1 && (xk * NT * 128 > 32768 || nk % xk != 0)) xk /= 2;
-    int nx = 4, np = 2;
-    auto bars_bytes = [&]() { return 8 * (2 * np + 2 * nx + 2 * na + 2) + 16; };
-    auto total = [&]() { return nx * xk * NT * 128 + np * pchunk + sbytes + bars_bytes() + 1024; };
-    if (total() > d.smem_optin) nx = 2;
-    if (total() > d.smem_optin) return false;
-    for (bool grew = true; grew;) {
-        grew = false;
-        if (np < 6) { ++np; if (total() <= d.smem_optin) grew = true; else --np; }
-        if (nx < 6) { nx += 2; if (total() <= d.smem_optin) grew = true; else nx -= 2; }
+    (void)out_bytes;
+    for (int pk : {8, 4}) {
+        if (nk % pk != 0) continue;
+        const int pchunk = tc_pchunk(pk);
+        int nx = 4, np = 2;   // four X stages first: the activations are the fast-consumed stream
+        auto bars_bytes = [&]() { return 8 * (2 * np + 2 * nx + 2 * a.na + 2 * a.nacc) + 16; };
+        auto total = [&]() { return nx * xk * NT * 128 + np * pchunk + bars_bytes() + 1024; };
+        if (total() > d.smem_optin) nx = 2;
+        if (total() > d.smem_optin) continue;
+        for (bool grew = true; grew;) {
+            grew = false;
+            if (np < 6) { ++np; if (total() <= d.smem_optin) grew = true; else --np; }
+            if (nx < 6) { nx += 2; if (total() <= d.smem_optin) grew = true; else nx -= 2; }
+        }
+        p->pk = pk;
+        a.xk = xk;
+        a.x_stage = xk * NT * 128;
+        a.nx = nx;
+        a.np = np;
+        a.x_off = 0;
+        a.p_off = nx * a.x_stage;
+        a.bar_off = a.p_off + np * pchunk;
+        p->smem = total();
+        p->grid = dim3((unsigned)(a.tiles < d.sm_count ? a.tiles : d.sm_count));
+        return true;
     }
-    a.xk = xk;
-    a.x_stage = xk * NT * 128;
-    if (2 * (TC_THREADS / 32) * TC_EPI_BOX * TC_EPI_BOX * out_bytes > nx * a.x_stage + np * pchunk)
-        return false;   // epilogue staging (two buffers per warp) fits in the X and P rings
-    a.na = na; a.nx = nx; a.np = np;
-    a.x_off = 0;
-    a.p_off = nx * a.x_stage;
-    a.s_off = a.p_off + np * pchunk;
-    a.bar_off = a.s_off + sbytes;
-    p->smem = total();
-    p->grid = dim3((unsigned)tiles_n, (unsigned)((M + NT - 1) / NT));
-    return true;
+    return false;
 }
 
 template <typename OutT>
 static int tc_entry(const void* q, const void* s, const void* x, void* y, int N, int K, int M, cudaStream_t st) {
     if (!q || !s || !x || !y) return VKB_EINVAL;
     if (N < 1 || M < 1 || K < 256) return VKB_EINVAL;
-    if (K % 256 != 0 || K > 7680) return VKB_EUNSUPPORTED;
+    if (K % 256 != 0) return VKB_EUNSUPPORTED;
     if (!aligned16(q) || !aligned16(s) || !aligned16(x)) return VKB_EUNSUPPORTED;
     int dev = 0;
     if (int r = current_device(&dev)) return r;
@@ -401,24 +410,15 @@ static int tc_entry(const void* q, const void* s, const void* x, void* y, int N,
     TcPlan p{};
     if (!plan_tc(N, K, M, (int)sizeof(OutT), d, &p)) return VKB_EUNSUPPORTED;
     p.a.y = y;
-    p.a.tma_store = aligned16(y) && ((size_t)N * sizeof(OutT)) % 16 == 0;
-    CUtensorMap tq, ts, tx, ty;
+    CUtensorMap tq, ts, tx;
     int r = get_tmap_2d(&tq, q, (uint64_t)N, (uint64_t)K / 2, CU_TENSOR_MAP_DATA_TYPE_UINT64, 8,
                         (uint32_t)tc_ppitch(p.pk) / 8, TC_BM, CU_TENSOR_MAP_SWIZZLE_NONE);
     if (r) return r;
-    r = get_tmap_2d(&ts, s, (uint64_t)N, (uint64_t)K / 16, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2,
-                    (uint32_t)(p.a.spitch / 2), TC_BM, CU_TENSOR_MAP_SWIZZLE_NONE);
+    r = get_tmap_2d(&ts, s, (uint64_t)N, (uint64_t)K / 16, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, TC_SPITCH / 2, TC_BM,
+                    CU_TENSOR_MAP_SWIZZLE_NONE);
     if (r) return r;
     r = get_tmap_x3d(&tx, x, M, K, p.a.NT, p.a.xk);
     if (r) return r;
-    if (p.a.tma_store) {
-        r = get_tmap_2d(&ty, y, (uint64_t)M, (uint64_t)N * sizeof(OutT),
-                        sizeof(OutT) == 4 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_UINT16,
-                        (uint32_t)sizeof(OutT), TC_EPI_BOX, TC_EPI_BOX, CU_TENSOR_MAP_SWIZZLE_NONE);
-        if (r) return r;
-    } else {
-        ty = tq;   // unused by the kernel
-    }
     auto kern = p.pk == 8 ? tc_q4_kernel<OutT, 8> : tc_q4_kernel<OutT, 4>;
     static std::once_flag once[kMaxDevices];
     static cudaError_t attr_err[kMaxDevices];
@@ -440,7 +440,7 @@ static int tc_entry(const void* q, const void* s, const void* x, void* y, int N,
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl_enabled() && pdl_stream_ok(st) ? 1 : 0;
-    const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, tq, ts, tx, ty, p.a);
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, tq, ts, tx, p.a);
     return e == cudaSuccess ? 0 : -(int)e;
 }
 
