@@ -466,9 +466,32 @@ qmv_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUten
         }
     }
 
-    int cur_seg = -1, segs_seen = 0, cnt = 0;
+    // Activation segments of this CTA, in order: j = sg - first_seg. Every warp enters (waits xfull) and leaves (arrives
+    // xempty) every segment exactly once and in order -- also the ones it has no tile in -- so that an arrival is
+    // never counted towards an earlier use of the same double buffer.
+    const int first_seg = w0 / a.tilesN;
+    const int last_seg = ntl > 0 ? (w1 - 1) / a.tilesN : first_seg - 1;
+    int jn = 0;            // next segment to enter
+    bool held = false;     // holding segment jn - 1
+    int cnt = 0;
     uint32_t xrow = 0;
     bool ok = true;
+    auto leave = [&]() {
+        if (held) {
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&xempty[(jn - 1) & 1]);
+            held = false;
+        }
+    };
+    auto enter_upto = [&](int j_target) -> bool {   // hold segment j_target, passing through the ones before it
+        while (jn <= j_target) {
+            leave();
+            if (!wait_parity(&xfull[jn & 1], (jn >> 1) & 1)) return false;
+            held = true;
+            ++jn;
+        }
+        return true;
+    };
     // this group's tiles: tl = grp, grp + WG, ...; their first stage iteration is tl * nchunks
     int sg = (w0 + grp) / a.tilesN, tile = (w0 + grp) % a.tilesN;
     int stg = 0, rnd = 0;
@@ -479,20 +502,11 @@ qmv_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUten
     }
     int ntile = 0;   // tiles this group has done (reduction buffer parity / reducer rotation)
     for (int tl = grp; tl < ntl && ok; tl += WG, ++ntile) {
-        if (sg != cur_seg) {
-            if constexpr (MODE == QMV_MOE) {
-                if (cur_seg >= 0) {
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(&xempty[(segs_seen - 1) & 1]);
-                }
-            }
-            cur_seg = sg;
-            const int xb = segs_seen & 1;
-            ok = wait_parity(&xfull[xb], (segs_seen >> 1) & 1);
-            ++segs_seen;
+        if (sg - first_seg != jn - 1 || !held) {
+            if (!enter_upto(sg - first_seg)) { ok = false; break; }
+            const int xb = (jn - 1) & 1;
             cnt = seg_count(sg);
             xrow = xbuf_s + (uint32_t)(xb * a.xrows * a.xpitch + (g < cnt ? g : 0) * a.xpitch) + x_lane_off<F>(t);
-            if (!ok) break;
         }
         float acc[4] = {0.f, 0.f, 0.f, 0.f};
         int kc = 0;
@@ -539,6 +553,9 @@ qmv_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUten
         stg += (WG - 1) * a.nchunks;
         while (stg >= a.nstage) { stg -= a.nstage; ++rnd; }
     }
+    // release the rest of the CTA's segments (also those this group had no tile in)
+    if (ok) ok = enter_upto(last_seg - first_seg);
+    leave();
 }
 
 }  // namespace vkb

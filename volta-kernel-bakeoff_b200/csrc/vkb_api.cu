@@ -204,11 +204,12 @@ static bool plan_qmv(int fmt, int N, int K, int xrows, int moe_slots, int E_loca
     a.red_off = a.x_off + xbytes;
     a.bar_off = a.red_off + redbytes;
     a.moe_off = a.bar_off + 8 * qmv_nbars(nstage);
-    // warp groups: as many tiles in flight as the ring allows (nstage >= wg * nchunks), one for MoE
+    // warp groups: as many tiles in flight as the ring allows (nstage >= wg * nchunks); MoE too (every warp passes
+    // through every activation segment of its CTA in order, also those it has no tile in)
     a.wg = 1;
-    if (moe_slots == 0)
-        for (int wg = QMV_MAXWG; wg > 1; wg /= 2)
-            if (nstage >= wg * nchunks) { a.wg = wg; break; }
+    for (int wg = QMV_MAXWG; wg > 1; wg /= 2)
+        if (nstage >= wg * nchunks) { a.wg = wg; break; }
+    (void)moe_slots;
     p->smem = a.moe_off + moebytes + slack;
     return true;
 }
@@ -242,7 +243,6 @@ template <int F, typename OutT>
 static int launch_simple(const void* q, const void* s, const void* x, void* y, const int32_t* idx, int N, int K,
                          int M, int topk, int E_local, int e0, int zero_foreign, int slots, cudaStream_t st) {
     cudaLaunchConfig_t cfg{};
-    cfg.gridDim = dim3((unsigned)((N + 7) / 8), (unsigned)(idx ? slots : 1));
     cfg.blockDim = dim3(256);
     cfg.stream = st;
     cudaLaunchAttribute attr[1];
@@ -250,9 +250,28 @@ static int launch_simple(const void* q, const void* s, const void* x, void* y, c
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl_enabled() && pdl_stream_ok(st) ? 1 : 0;
-    const cudaError_t e = cudaLaunchKernelEx(&cfg, qmv_simple_kernel<F, OutT>, q, (const __half*)s,
-                                             (const __half*)x, (OutT*)y, idx, N, K, M, topk, E_local, e0,
-                                             zero_foreign);
+    cudaError_t e;
+    if (idx == nullptr) {
+        cfg.gridDim = dim3((unsigned)((N + 7) / 8), 1);
+        e = cudaLaunchKernelEx(&cfg, qmv_simple_kernel<F, OutT>, q, (const __half*)s, (const __half*)x, (OutT*)y, idx,
+                               N, K, M, topk, E_local, e0, zero_foreign);
+    } else {
+        // the slot list of one expert in dynamic shared memory (slots x 4 bytes; the entry point caps slots at 32767)
+        static std::once_flag once[kMaxDevices];
+        static cudaError_t attr_err[kMaxDevices];
+        int dev = 0;
+        if (int r = current_device(&dev)) return r;
+        std::call_once(once[dev], [&] {
+            attr_err[dev] = cudaFuncSetAttribute(qmv_simple_moe_kernel<F, OutT>,
+                                                 cudaFuncAttributeMaxDynamicSharedMemorySize, 4 * 32767 + 16);
+        });
+        if (attr_err[dev] != cudaSuccess) return -(int)attr_err[dev];
+        cfg.gridDim = dim3((unsigned)((N + QMV_SIMPLE_MOE_ROWS - 1) / QMV_SIMPLE_MOE_ROWS),
+                           (unsigned)(E_local + (zero_foreign ? 1 : 0)));
+        cfg.dynamicSmemBytes = (size_t)slots * 4;
+        e = cudaLaunchKernelEx(&cfg, qmv_simple_moe_kernel<F, OutT>, q, (const __half*)s, (const __half*)x, (OutT*)y,
+                               idx, N, K, M, topk, E_local, e0, zero_foreign);
+    }
     return e == cudaSuccess ? 0 : -(int)e;
 }
 
