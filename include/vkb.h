@@ -116,6 +116,17 @@ int vkb_gemm_q4_tc_rowsplit(vkb_comm_t* comm, const void* q_local, const void* s
                             void* work, int N, int K, int M, vkb_stream_t stream);
 int vkb_gemm_q4_tc_rowsplit_f32(vkb_comm_t* comm, const void* q_local, const void* s_local, const void* x, float* y,
                                 void* work, int N, int K, int M, vkb_stream_t stream);
+/* Symmetric device buffers for the fused (peer-store) calls: collective, the same `bytes` on every rank; each rank's
+ * buffer is mapped into every peer (CUDA IPC, exchanged over the communicator). Freed by vkb_comm_free (collective)
+ * or vkb_comm_destroy. At most 8 ranks. */
+int vkb_comm_alloc(vkb_comm_t* comm, size_t bytes, void** ptr);
+int vkb_comm_free(vkb_comm_t* comm, void* ptr);
+/* Row split with the all-gather fused into the GEMM: the tcgen05 epilogue stores this rank's columns of y straight
+ * into every rank's copy of y_sym (a vkb_comm_alloc buffer of >= M x N fp16) over NVLink, ordered by per-call epochs
+ * (a rank is written only after it started the call; the call's kernel ends when every rank's part has arrived).
+ * Same operands and result as vkb_gemm_q4_tc_rowsplit, no workspace, no NCCL call. */
+int vkb_gemm_q4_tc_rowsplit_p2p(vkb_comm_t* comm, const void* q_local, const void* s_local, const void* x, void* y_sym,
+                                int N, int K, int M, vkb_stream_t stream);
 /* The same (fp16 y) with no workspace argument and no allocation: the workspace is a static device array of the
  * library, 16 MiB per device, looked up once per device. No counterpart in the reference. M * N * 2 must not exceed
  * VKB_ROWSPLIT_NOALLOC_MAX_BYTES (VKB_EUNSUPPORTED otherwise, nothing launched). Calls that overlap in time on one

@@ -73,6 +73,28 @@ def _rank_main(rank, world, port, q):
                 ref, mag = O.ref_value(codes, scales, x_np), O.ref_scale(codes, scales, x_np)
                 err = O.check_error(y_rs.float().cpu().numpy().astype(np.float64), ref, mag)[0]
                 out.append((f"rowsplit N{N} K{K} M{M} f32={f32}", same, err, O.TOL_FP16))
+        # ---- row split with the all-gather fused into the epilogue (peer stores into a symmetric buffer) ----
+        for (N, K, M) in [(1024, 2048, 64), (2048, 2560, 512), (512, 768, 65)]:
+            codes = rng.integers(-8, 8, size=(N, K)).astype(np.int8)
+            scales = rng.uniform(0.004, 0.02, size=(N, K // 32)).astype(np.float16).view(np.uint16)
+            qfull = vkb.to_device_packed(O.pack(O.FMT_Q4, codes), dev)
+            sfull = vkb.to_device_f16(scales, dev)
+            n0, nl = D.row_range(N, world, rank)
+            qloc, sloc = qfull[n0:n0 + nl].contiguous(), sfull[n0:n0 + nl].contiguous()
+            xs = [vkb.to_device_f16(rng.uniform(-1, 1, size=(M, K)).astype(np.float16).view(np.uint16), dev)
+                  for _ in range(3)]
+            ysym = comm.alloc((M, N), torch.float16)
+            yv = ysym.tensor()
+            snaps = []
+            for x in xs:   # three calls in a row on one stream; each result copied out before the next call
+                comm.gemm_rowsplit_p2p(qloc, sloc, x, N, ysym)
+                snaps.append(yv.clone())
+            torch.cuda.synchronize()
+            for i, x in enumerate(xs):
+                y_one = vkb.gemm_tc(qfull, sfull, x)
+                torch.cuda.synchronize()
+                out.append((f"rowsplit_p2p N{N} K{K} M{M} call{i}", bool(torch.equal(y_one, snaps[i])), 0.0, 1.0))
+            ysym.free()
         status = vkb.device_status()
         comm.close()
         dist.barrier()

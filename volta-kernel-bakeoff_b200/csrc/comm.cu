@@ -19,13 +19,26 @@
 #include <mutex>
 #include <new>
 
+#include <vector>
+
 #include "../../include/vkb.h"
+#include "p2p.cuh"
 #include "ptx.cuh"
 #include "vkb_internal.h"
+
+// A symmetric buffer: the same size on every rank, this rank's allocation plus every peer's mapped by CUDA IPC; the
+// data is followed by the flags block of the peer-store protocol (p2p.cuh).
+struct SymBuf {
+    void* base;
+    size_t data_bytes;
+    void* peer[vkb::P2P_MAX_RANKS];
+    uint32_t epoch;
+};
 
 struct vkb_comm {
     ncclComm_t nc;
     int rank, size, dev;
+    std::vector<SymBuf> sym;
 };
 
 namespace vkb {
@@ -128,6 +141,24 @@ static int rowsplit_scratch(int dev, void** out) {
     return 0;
 }
 
+static SymBuf* find_sym(vkb_comm_t* c, const void* p, size_t need) {
+    for (auto& b : c->sym)
+        if (b.base == p && b.data_bytes >= need) return &b;
+    return nullptr;
+}
+
+static int sym_free_one(vkb_comm_t* c, SymBuf& b) {
+    int rc = 0;
+    for (int r = 0; r < c->size; ++r)
+        if (r != c->rank && b.peer[r]) {
+            const cudaError_t e = cudaIpcCloseMemHandle(b.peer[r]);
+            if (e != cudaSuccess && rc == 0) rc = -(int)e;
+        }
+    const cudaError_t e = cudaFree(b.base);
+    if (e != cudaSuccess && rc == 0) rc = -(int)e;
+    return rc;
+}
+
 }  // namespace vkb
 
 using namespace vkb;
@@ -185,9 +216,86 @@ int vkb_comm_init(vkb_comm_t** comm, int rank, int nranks, const void* id) {
 
 int vkb_comm_destroy(vkb_comm_t* comm) {
     if (!comm) return 0;
-    const int rc = nccl_rc(ncclCommDestroy(comm->nc));
+    int rc = 0;
+    for (auto& b : comm->sym) {
+        const int r = sym_free_one(comm, b);
+        if (r && !rc) rc = r;
+    }
+    const int r = nccl_rc(ncclCommDestroy(comm->nc));
     delete comm;
-    return rc;
+    return rc ? rc : r;
+}
+
+int vkb_comm_alloc(vkb_comm_t* comm, size_t bytes, void** ptr) {
+    if (!comm || !ptr || bytes == 0) return VKB_EINVAL;
+    *ptr = nullptr;
+    if (comm->size > P2P_MAX_RANKS) return VKB_EUNSUPPORTED;
+    SymBuf b{};
+    b.data_bytes = (bytes + 255) / 256 * 256;
+    cudaError_t e = cudaMalloc(&b.base, b.data_bytes + P2P_FLAG_WORDS * 4);
+    if (e != cudaSuccess) return -(int)e;
+    e = cudaMemset(b.base, 0, b.data_bytes + P2P_FLAG_WORDS * 4);
+    cudaIpcMemHandle_t h;
+    if (e == cudaSuccess) e = cudaIpcGetMemHandle(&h, b.base);
+    // every rank's handle to every rank, through the communicator
+    void* dh = nullptr;
+    if (e == cudaSuccess) e = cudaMalloc(&dh, sizeof(h) * comm->size);
+    int rc = e == cudaSuccess ? 0 : -(int)e;
+    std::vector<cudaIpcMemHandle_t> all(comm->size);
+    if (rc == 0) {
+        e = cudaMemcpy(static_cast<uint8_t*>(dh) + comm->rank * sizeof(h), &h, sizeof(h), cudaMemcpyHostToDevice);
+        rc = e == cudaSuccess ? 0 : -(int)e;
+    }
+    // the collective runs on every rank that reached this point with valid arguments
+    if (dh) {
+        const int rn = nccl_rc(ncclAllGather(static_cast<uint8_t*>(dh) + comm->rank * sizeof(h), dh, sizeof(h),
+                                             ncclUint8, comm->nc, nullptr));
+        if (!rc) rc = rn;
+        e = cudaStreamSynchronize(nullptr);
+        if (!rc && e != cudaSuccess) rc = -(int)e;
+        if (!rc) {
+            e = cudaMemcpy(all.data(), dh, sizeof(h) * comm->size, cudaMemcpyDeviceToHost);
+            if (e != cudaSuccess) rc = -(int)e;
+        }
+        cudaFree(dh);
+    }
+    for (int r = 0; r < comm->size && rc == 0; ++r) {
+        if (r == comm->rank) { b.peer[r] = b.base; continue; }
+        e = cudaIpcOpenMemHandle(&b.peer[r], all[r], cudaIpcMemLazyEnablePeerAccess);
+        if (e != cudaSuccess) rc = -(int)e;
+    }
+    if (rc) {
+        for (int r = 0; r < comm->size; ++r)
+            if (r != comm->rank && b.peer[r]) cudaIpcCloseMemHandle(b.peer[r]);
+        if (b.base) cudaFree(b.base);
+        return rc;
+    }
+    comm->sym.push_back(b);
+    *ptr = b.base;
+    return 0;
+}
+
+int vkb_comm_free(vkb_comm_t* comm, void* ptr) {
+    if (!comm || !ptr) return VKB_EINVAL;
+    for (size_t i = 0; i < comm->sym.size(); ++i)
+        if (comm->sym[i].base == ptr) {
+            // nobody may still store into this rank's copy: every rank has finished with the buffer before the
+            // mappings go away
+            cudaError_t e = cudaDeviceSynchronize();
+            int rc = e == cudaSuccess ? 0 : -(int)e;
+            void* tmp = nullptr;
+            if (cudaMalloc(&tmp, 4) == cudaSuccess) {
+                const int rn = nccl_rc(ncclAllReduce(tmp, tmp, 1, ncclInt32, ncclSum, comm->nc, nullptr));
+                if (!rc) rc = rn;
+                e = cudaStreamSynchronize(nullptr);
+                if (!rc && e != cudaSuccess) rc = -(int)e;
+                cudaFree(tmp);
+            }
+            const int rf = sym_free_one(comm, comm->sym[i]);
+            comm->sym.erase(comm->sym.begin() + (long)i);
+            return rc ? rc : rf;
+        }
+    return VKB_EINVAL;
 }
 
 int vkb_comm_rank(const vkb_comm_t* comm) { return comm ? comm->rank : -1; }
@@ -223,6 +331,27 @@ int vkb_gemm_q4_tc_rowsplit_noalloc(vkb_comm_t* comm, const void* q_local, const
     void* work = nullptr;
     if (int r = rowsplit_scratch(dev, &work)) return r;
     return rowsplit(comm, q_local, s_local, x, y, work, false, N, K, M, (cudaStream_t)stream);
+}
+
+int vkb_gemm_q4_tc_rowsplit_p2p(vkb_comm_t* comm, const void* q_local, const void* s_local, const void* x, void* y_sym,
+                                int N, int K, int M, vkb_stream_t stream) {
+    if (!comm) return VKB_ENOCOMM;
+    if (!q_local || !s_local || !x || !y_sym) return VKB_EINVAL;
+    if (N < 1 || M < 1 || K < 256) return VKB_EINVAL;
+    if (N % comm->size != 0 || K % 256 != 0 || comm->size > P2P_MAX_RANKS) return VKB_EUNSUPPORTED;
+    SymBuf* b = find_sym(comm, y_sym, (size_t)M * N * 2);
+    if (!b) return VKB_EINVAL;   // y must come from vkb_comm_alloc and hold M x N fp16
+    P2PArgs pp{};
+    for (int r = 0; r < comm->size; ++r) {
+        pp.peer_base[r] = b->peer[r];
+        pp.peer_flags[r] = reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(b->peer[r]) + b->data_bytes);
+    }
+    pp.rank = comm->rank;
+    pp.size = comm->size;
+    pp.epoch = ++b->epoch;
+    const int nl = N / comm->size;
+    TcOut out{N, comm->rank * nl, &pp};
+    return tc_dispatch(q_local, s_local, x, y_sym, false, nl, K, M, (cudaStream_t)stream, &out);
 }
 
 int vkb_gemm_q4_tc_rowsplit_f32(vkb_comm_t* comm, const void* q_local, const void* s_local, const void* x, float* y,

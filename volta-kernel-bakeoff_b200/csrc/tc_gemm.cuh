@@ -32,6 +32,7 @@
 // No cluster multicast anywhere: the kernel also serves the row-split multi-GPU calls.
 #pragma once
 
+#include "p2p.cuh"
 #include "ptx.cuh"
 
 namespace vkb {
@@ -53,7 +54,7 @@ __host__ __device__ constexpr int tc_ppitch(int pk) { return 32 * pk + 16; }
 __host__ __device__ constexpr int tc_pchunk(int pk) { return TC_BM * (tc_ppitch(pk) + TC_SPITCH); }
 
 struct TcArgs {
-    void* y;            // [M][N]
+    void* y;            // [M][ldy], this call's columns from ycol0
     int M, N, K;
     int NT;             // tokens per tile (multiple of 32, <= 256)
     int nk;             // K steps per tile (K / 64)
@@ -66,6 +67,9 @@ struct TcArgs {
     int x_stage;        // bytes of one X stage (xk x NT x 128)
     int x_off, p_off, bar_off;   // shared-memory region offsets (1024-aligned)
     int tmem_cols;
+    int ldy, ycol0;     // output row stride and first column (row split: the full y, this rank's columns)
+    int p2p;            // 1: also store into every peer's copy of y (pp.peer_base) and run the epoch protocol
+    P2PArgs pp;
 };
 
 // ---- tcgen05 wrappers ----------------------------------------------------------------------------------------------
@@ -464,6 +468,11 @@ tc_q4_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUt
         const int q = warp & 3;
         const int sub = epi ? 0 : 1 + ((warp - TC_WDQ0) >> 2);   // participant index within the lane quarter
         pdl_wait();   // y may still be read or written by the previous grid
+        if (a.p2p) {   // this rank's copy may now be written; wait until every peer's may be
+            if (blockIdx.x == 0 && warp == TC_WEPI0 && lane == 0) p2p_post_ready(a.pp);
+            if (lane == 0 && !p2p_wait_ready(a.pp)) ok = false;
+            ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+        }
         OutT* y = reinterpret_cast<OutT*>(a.y);
         for (int i = epi ? 0 : ntl - 1; i < ntl && ok; ++i) {
             const int acc = i % a.nacc, t = tile_of(i), row0 = row0_of(t), tok0 = tok0_of(t);
@@ -477,11 +486,21 @@ tc_q4_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUt
             const int step = 32 * parts;
             auto put = [&](const uint32_t (&v)[32], int c) {
                 if (n >= a.N) return;
-                OutT* yp = y + (size_t)(tok0 + c) * a.N + n;
+                const size_t off = (size_t)(tok0 + c) * a.ldy + a.ycol0 + n;
                 const int lim = a.M - (tok0 + c);
+                if (!a.p2p) {
+                    OutT* yp = y + off;
 #pragma unroll
-                for (int j = 0; j < 32; ++j, yp += a.N)
-                    if (j < lim) *yp = tc_out<OutT>(__uint_as_float(v[j]));
+                    for (int j = 0; j < 32; ++j, yp += a.ldy)
+                        if (j < lim) *yp = tc_out<OutT>(__uint_as_float(v[j]));
+                } else {   // every rank's copy, this rank's included (peer stores go over NVLink)
+                    for (int r = 0; r < a.pp.size; ++r) {
+                        OutT* yp = reinterpret_cast<OutT*>(a.pp.peer_base[r]) + off;
+#pragma unroll 8
+                        for (int j = 0; j < 32; ++j, yp += a.ldy)
+                            if (j < lim) *yp = tc_out<OutT>(__uint_as_float(v[j]));
+                    }
+                }
             };
             uint32_t va[32], vb[32];
             int c = 32 * sub;
@@ -502,6 +521,7 @@ tc_q4_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUt
                 if (lane == 0) mbar_arrive(&accempty[acc]);
             }
         }
+        if (a.p2p) fence_acq_rel_sys();   // this thread's peer stores before the CTA's completion count
     }
     // teardown: every MMA has completed (the epilogue waited on each accumulator) before TMEM is released
     if (warp == 1 && !ok && ntl > 0) wait_parity_sleep(&accfull[(ntl - 1) % a.nacc], ((ntl - 1) / a.nacc) & 1,
@@ -512,6 +532,7 @@ tc_q4_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUt
         tc_fence_after();
         tmem_dealloc(tmem, (uint32_t)a.tmem_cols);
     }
+    if (a.p2p && threadIdx.x == 0) p2p_finish(a.pp);   // every store of this CTA is done (the barrier above)
 }
 
 }  // namespace vkb

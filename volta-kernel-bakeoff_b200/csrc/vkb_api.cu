@@ -417,7 +417,8 @@ static bool plan_tc(int N, int K, int M, int out_bytes, const DeviceInfo& d, TcP
 }
 
 template <typename OutT>
-static int tc_entry(const void* q, const void* s, const void* x, void* y, int N, int K, int M, cudaStream_t st) {
+static int tc_entry(const void* q, const void* s, const void* x, void* y, int N, int K, int M, cudaStream_t st,
+                    const TcOut* out = nullptr) {
     if (!q || !s || !x || !y) return VKB_EINVAL;
     if (N < 1 || M < 1 || K < 256) return VKB_EINVAL;
     if (K % 256 != 0) return VKB_EUNSUPPORTED;
@@ -429,6 +430,10 @@ static int tc_entry(const void* q, const void* s, const void* x, void* y, int N,
     TcPlan p{};
     if (!plan_tc(N, K, M, (int)sizeof(OutT), d, &p)) return VKB_EUNSUPPORTED;
     p.a.y = y;
+    p.a.ldy = out ? out->ldy : N;
+    p.a.ycol0 = out ? out->col0 : 0;
+    p.a.p2p = out && out->p2p ? 1 : 0;
+    if (p.a.p2p) p.a.pp = *out->p2p;
     CUtensorMap tq, ts, tx;
     int r = get_tmap_2d(&tq, q, (uint64_t)N, (uint64_t)K / 2, CU_TENSOR_MAP_DATA_TYPE_UINT64, 8,
                         (uint32_t)tc_ppitch(p.pk) / 8, TC_BM, CU_TENSOR_MAP_SWIZZLE_NONE);
@@ -463,8 +468,9 @@ static int tc_entry(const void* q, const void* s, const void* x, void* y, int N,
     return e == cudaSuccess ? 0 : -(int)e;
 }
 
-int tc_dispatch(const void* q, const void* s, const void* x, void* y, bool f32, int N, int K, int M, cudaStream_t st) {
-    return f32 ? tc_entry<float>(q, s, x, y, N, K, M, st) : tc_entry<__half>(q, s, x, y, N, K, M, st);
+int tc_dispatch(const void* q, const void* s, const void* x, void* y, bool f32, int N, int K, int M, cudaStream_t st,
+                const TcOut* out) {
+    return f32 ? tc_entry<float>(q, s, x, y, N, K, M, st, out) : tc_entry<__half>(q, s, x, y, N, K, M, st, out);
 }
 
 }  // namespace vkb

@@ -105,6 +105,23 @@ class Comm:
         check(rc, "vkb_moe_ep")
         return y
 
+    def alloc(self, shape, dtype):
+        """A symmetric tensor (collective: same shape on every rank): this rank's buffer, mapped into every peer, for
+        the fused peer-store calls. Freed with free()."""
+        import torch
+        nbytes = int(np.prod(shape)) * torch.tensor([], dtype=dtype).element_size()
+        p = ctypes.c_void_p()
+        check(lib().vkb_comm_alloc(self._h, nbytes, ctypes.byref(p)), "vkb_comm_alloc")
+        return SymTensor(self, p, shape, dtype)
+
+    def gemm_rowsplit_p2p(self, q_local, s_local, x, N: int, y_sym: "SymTensor", stream=None):
+        """Row-split prompt GEMM with the all-gather fused into the epilogue (peer stores over NVLink): y_sym (from
+        alloc, [M][N] fp16) holds the full product on every rank after the call."""
+        M, K = x.shape
+        check(lib().vkb_gemm_q4_tc_rowsplit_p2p(self._h, _ptr(q_local), _ptr(s_local), _ptr(x), y_sym.ptr, N, K, M,
+                                                 _stream(stream)), "vkb_gemm_q4_tc_rowsplit_p2p")
+        return y_sym
+
     def gemm_rowsplit(self, q_local, s_local, x, N: int, y=None, work=None, out_f32: bool = False, stream=None):
         """Row-split prompt GEMM: q_local / s_local hold this rank's N/G weight rows. Returns y [M][N] on every
         rank."""
@@ -120,3 +137,24 @@ class Comm:
         check(fn(self._h, _ptr(q_local), _ptr(s_local), _ptr(x), _ptr(y), _ptr(work), N, K, M, _stream(stream)),
               "vkb_gemm_q4_tc_rowsplit")
         return y
+
+
+class SymTensor:
+    """A symmetric device buffer of a communicator, viewed as a torch tensor (tensor())."""
+
+    def __init__(self, comm: Comm, ptr: ctypes.c_void_p, shape, dtype):
+        self.comm, self.ptr, self.shape, self.dtype = comm, ptr, tuple(shape), dtype
+
+    def tensor(self):
+        """A torch view of the buffer (no copy; valid until free())."""
+        import torch
+        n = int(np.prod(self.shape))
+        esz = torch.tensor([], dtype=self.dtype).element_size()
+        iface = {"shape": (n * esz,), "typestr": "|u1", "data": (self.ptr.value, False), "version": 3}
+        holder = type("_CudaArray", (), {"__cuda_array_interface__": iface})()
+        return torch.as_tensor(holder, device="cuda").view(self.dtype).view(self.shape)
+
+    def free(self):
+        if self.ptr:
+            check(lib().vkb_comm_free(self.comm._h, self.ptr), "vkb_comm_free")
+            self.ptr = ctypes.c_void_p()
