@@ -270,15 +270,23 @@ def moe_section(torch, vkb, dev, stream, L2, comm=None, rank=0, world=1):
             idx = torch.from_numpy(idx_np).to(dev)
             x = vkb.to_device_f16(vkb.to_f16_bits(vkb.synth_normal(13, (T, K), 1.0)), dev)
             y = torch.empty((T, k, N), dtype=torch.float16, device=dev)
+            us_p2p = None
             if comm is None:
                 us = _median_us(torch, stream, lambda i: vkb.moe(0, ql[i % n], sl[i % n], idx, x, y=y))
             else:
                 us = _median_us(torch, stream, lambda i: comm.moe_ep(ql[i % n], sl[i % n], idx, x, E_local=el,
                                                                       e0=e0, y=y), graph=False)
+                ysym = comm.alloc((T, k, N), torch.float16)
+                us_p2p = _median_us(torch, stream, lambda i: comm.moe_ep_p2p(ql[i % n], sl[i % n], idx, x, E_local=el,
+                                                                              e0=e0, y_sym=ysym))
+                torch.cuda.synchronize()
+                ysym.free()
             U = len(np.unique(idx_np))
             nbytes = U * per_expert + idx_np.nbytes + T * K * 2 + T * k * N * 2
             out[f"{name}_t{T}"] = {"us": round(us, 2), "distinct_experts": U,
                                    "GBps": round(nbytes / us / 1e3, 1) if comm is None else None}
+            if us_p2p is not None:
+                out[f"{name}_t{T}"]["us_p2p"] = round(us_p2p, 2)
         del ql, sl
     return out
 
@@ -301,7 +309,11 @@ def rowsplit_section(torch, vkb, dev, stream, L2, comm, rank, world):
             work = torch.empty(vkb.lib().vkb_gemm_rowsplit_work_bytes(M, N, 0), dtype=torch.uint8, device=dev)
             us = _median_us(torch, stream, lambda i: comm.gemm_rowsplit(ql[i % nq], sl[i % nq], x, N, y=y, work=work),
                             graph=False)
-            out[f"q4_{N}x{K}_m{M}"] = {"us": round(us, 2), "tflops": round(2.0 * M * N * K / us / 1e6, 1),
+            ysym = comm.alloc((M, N), torch.float16)
+            us_p2p = _median_us(torch, stream, lambda i: comm.gemm_rowsplit_p2p(ql[i % nq], sl[i % nq], x, N, ysym))
+            torch.cuda.synchronize()
+            ysym.free()
+            out[f"q4_{N}x{K}_m{M}"] = {"us": us, "us_p2p": us_p2p, "flop": 2.0 * M * N * K,
                                        "allgather_bytes": M * N * 2}
         del ql, sl
     return out
@@ -489,11 +501,18 @@ def run_ours(args, rank: int, world: int, local_rank: int, dist):
         rows = rowsplit_section(torch, vkb, dev, stream, L2, comm, rank, world)
         for d in (moe_ep, rows):
             for v in d.values():
-                v["us"] = round(_max_over_ranks(torch, dist, dev, v["us"]), 2)
+                for key in ("us", "us_p2p"):
+                    if key in v:
+                        v[key] = round(_max_over_ranks(torch, dist, dev, v[key]), 2)
+                if "flop" in v:   # throughput of the max-over-ranks time
+                    fl = v.pop("flop")
+                    v["tflops"] = round(fl / v["us"] / 1e6, 1)
+                    v["tflops_p2p"] = round(fl / v["us_p2p"] / 1e6, 1)
         torch.cuda.synchronize()
         comm.close()
         sharded = {"gpus": world, "moe_expert_parallel": moe_ep, "prompt_row_split": rows,
-                   "timing": "median of 5 x 50 calls, device events, max over ranks; no CUDA graph (NCCL inside)"}
+                   "timing": "median of 5 x 50 calls, device events, max over ranks; us: NCCL combine, launched directly; "
+                             "us_p2p: combine fused into the kernel (peer stores), the 50 calls in one CUDA graph"}
 
     if rank != 0:
         return None

@@ -116,24 +116,38 @@ int vkb_gemm_q4_tc_rowsplit(vkb_comm_t* comm, const void* q_local, const void* s
                             void* work, int N, int K, int M, vkb_stream_t stream);
 int vkb_gemm_q4_tc_rowsplit_f32(vkb_comm_t* comm, const void* q_local, const void* s_local, const void* x, float* y,
                                 void* work, int N, int K, int M, vkb_stream_t stream);
-/* Symmetric device buffers for the fused (peer-store) calls: collective, the same `bytes` on every rank; each rank's
- * buffer is mapped into every peer (CUDA IPC, exchanged over the communicator). Freed by vkb_comm_free (collective)
- * or vkb_comm_destroy. At most 8 ranks. */
-int vkb_comm_alloc(vkb_comm_t* comm, size_t bytes, void** ptr);
-int vkb_comm_free(vkb_comm_t* comm, void* ptr);
-/* Row split with the all-gather fused into the GEMM: the tcgen05 epilogue stores this rank's columns of y straight
- * into every rank's copy of y_sym (a vkb_comm_alloc buffer of >= M x N fp16) over NVLink, ordered by per-call epochs
- * (a rank is written only after it started the call; the call's kernel ends when every rank's part has arrived).
- * Same operands and result as vkb_gemm_q4_tc_rowsplit, no workspace, no NCCL call. */
-int vkb_gemm_q4_tc_rowsplit_p2p(vkb_comm_t* comm, const void* q_local, const void* s_local, const void* x, void* y_sym,
-                                int N, int K, int M, vkb_stream_t stream);
-/* The same (fp16 y) with no workspace argument and no allocation: the workspace is a static device array of the
- * library, 16 MiB per device, looked up once per device. No counterpart in the reference. M * N * 2 must not exceed
- * VKB_ROWSPLIT_NOALLOC_MAX_BYTES (VKB_EUNSUPPORTED otherwise, nothing launched). Calls that overlap in time on one
- * device (other streams, host threads or communicators) share the array and race: serialise them. */
+/* vkb_gemm_q4_tc_rowsplit (fp16 y) with no workspace argument and no allocation: the workspace is a static device
+ * array of the library, 16 MiB per device, looked up once per device. No counterpart in the reference. M * N * 2 must
+ * not exceed VKB_ROWSPLIT_NOALLOC_MAX_BYTES (VKB_EUNSUPPORTED otherwise, nothing launched). Calls that overlap in time
+ * on one device (other streams, host threads or communicators) share the array and race: serialise them. */
 #define VKB_ROWSPLIT_NOALLOC_MAX_BYTES (16u << 20)
 int vkb_gemm_q4_tc_rowsplit_noalloc(vkb_comm_t* comm, const void* q_local, const void* s_local, const void* x, void* y,
                                     int N, int K, int M, vkb_stream_t stream);
+
+/* ---- multi-GPU, fused: the exchange inside the kernel (peer stores over NVLink, no NCCL call) --------------------
+ * Symmetric device buffers: collective, the same `bytes` on every rank; each rank's buffer is mapped into every peer
+ * (CUDA IPC, exchanged over the communicator) and followed by a 17 KiB flags block. Freed by vkb_comm_free
+ * (collective) or vkb_comm_destroy. At most 8 ranks.
+ * The fused calls below write every rank's copy of a symmetric y. Every rank makes the same fused calls on a buffer in
+ * the same order; each call is numbered by an epoch kept in the buffer's flags (device memory, so the calls may be
+ * captured in a CUDA graph and replayed): a rank's copy is written only after that rank started the call, and each
+ * rank's kernel ends only when every rank's part has arrived. A call refused on one rank only (an argument error
+ * there) leaves the other ranks' kernels waiting until their bounded waits give up: their calls end with the
+ * peer-timeout bit (4) in vkb_device_status instead of a result. */
+int vkb_comm_alloc(vkb_comm_t* comm, size_t bytes, void** ptr);
+int vkb_comm_free(vkb_comm_t* comm, void* ptr);
+/* Row split with the all-gather fused into the GEMM: the tcgen05 epilogue stores this rank's columns of y straight
+ * into every rank's copy of y_sym (>= M x N fp16). Same operands and result as vkb_gemm_q4_tc_rowsplit. */
+int vkb_gemm_q4_tc_rowsplit_p2p(vkb_comm_t* comm, const void* q_local, const void* s_local, const void* x, void* y_sym,
+                                int N, int K, int M, vkb_stream_t stream);
+/* Expert-parallel MoE with the combine fused into the GEMV: each rank's kernel stores the slots of its own experts
+ * straight into every rank's copy of y_sym (>= T*topk x N outputs); no zero slots, no all-reduce. Same operands and
+ * result as vkb_moe_ep for every slot whose expert some rank holds (slots of an expert that no rank holds are not
+ * written). Needs the pipelined kernel's shapes and alignment (K % 256 == 0, 16-byte aligned pools and x):
+ * VKB_EUNSUPPORTED otherwise. */
+int vkb_moe_ep_p2p(vkb_comm_t* comm, int fmt, const void* qpool, const void* spool, const int32_t* idx, int T,
+                   int topk, const void* x, void* y_sym, int out_f32, int E_local, int e0, int N, int K,
+                   vkb_stream_t stream);
 
 /* ---- CUDA graphs of vkb calls ---------------------------------------------------------------------------------------
  * Capture a sequence of calls on a stream into one executable graph (a decode step: many short GEMVs) and replay it

@@ -1,7 +1,9 @@
-"""Multi-GPU parity (2+ GPUs, one process per GPU): the expert-parallel MoE (vkb_moe_ep) and the row-split prompt
-GEMM (vkb_gemm_q4_tc_rowsplit) against the one-GPU calls on the same inputs -- bit-identical, since every slot / row is
-computed by the same kernel code and the combines only add zeros or move blocks -- and against the oracle. Skipped
-with fewer than two GPUs."""
+"""Multi-GPU parity (2+ GPUs, one process per GPU): the expert-parallel MoE (vkb_moe_ep, and vkb_moe_ep_p2p with
+the combine fused into the kernel) and the row-split prompt GEMM (vkb_gemm_q4_tc_rowsplit, and
+vkb_gemm_q4_tc_rowsplit_p2p with the all-gather fused into the epilogue, called directly and replayed from a CUDA
+graph) against the one-GPU calls on the same inputs -- bit-identical, since every slot / row is computed by the same
+kernel code and the combines only add zeros or move values -- and against the oracle. Skipped with fewer than two
+GPUs."""
 import datetime
 import os
 import socket
@@ -16,6 +18,13 @@ def _free_port():
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
         return s.getsockname()[1]
+
+
+def _raw_u32(torch, ptr: int, nbytes: int):
+    """uint32 words of device memory at ptr (a view, no copy)."""
+    iface = {"shape": (nbytes,), "typestr": "|u1", "data": (ptr, False), "version": 3}
+    holder = type("_CudaArray", (), {"__cuda_array_interface__": iface})()
+    return torch.as_tensor(holder, device="cuda").view(torch.int32)
 
 
 def _rank_main(rank, world, port, q):
@@ -95,6 +104,58 @@ def _rank_main(rank, world, port, q):
                 torch.cuda.synchronize()
                 out.append((f"rowsplit_p2p N{N} K{K} M{M} call{i}", bool(torch.equal(y_one, snaps[i])), 0.0, 1.0))
             ysym.free()
+            # the same call captured once in a CUDA graph and replayed: the epochs live in device memory, so every
+            # replay is a new call (the buffer's per-CTA epoch words, after the 256-byte aligned data, count the replays)
+            if (N, K, M) == (1024, 2048, 64):
+                ysym = comm.alloc((M, N), torch.float16)
+                yv = ysym.tensor()
+                xg = torch.empty_like(xs[0])
+                stream = torch.cuda.current_stream()
+                g = vkb.Graph(stream)
+                with g:
+                    comm.gemm_rowsplit_p2p(qloc, sloc, xg, N, ysym)
+                snaps = []
+                for x in xs:
+                    xg.copy_(x)
+                    g.replay()
+                    snaps.append(yv.clone())
+                torch.cuda.synchronize()
+                del g
+                data_bytes = (M * N * 2 + 255) // 256 * 256
+                flags = _raw_u32(torch, ysym.ptr.value, data_bytes + 4352 * 4)[data_bytes // 4:]
+                # EPOCH[cta] words (after READY and DONE, 8 ranks x 256 CTAs each): CTA 0 completed every replay
+                out.append(("rowsplit_p2p graph epochs", int(flags[4096].item()) == len(xs), 0.0, 1.0))
+                for i, x in enumerate(xs):
+                    y_one = vkb.gemm_tc(qfull, sfull, x)
+                    torch.cuda.synchronize()
+                    out.append((f"rowsplit_p2p graph replay{i}", bool(torch.equal(y_one, snaps[i])), 0.0, 1.0))
+                ysym.free()
+        # ---- expert-parallel MoE with the combine fused into the kernel (peer stores) ----
+        for (E, N, K, T, k) in [(16, 512, 2048, 1, 4), (16, 512, 2048, 33, 4), (8, 1024, 1024, 8, 2)]:
+            codes = rng.integers(-8, 8, size=(E, N, K)).astype(np.int8)
+            scales = rng.uniform(0.004, 0.02, size=(E, N, K // 32)).astype(np.float16).view(np.uint16)
+            qfull = vkb.to_device_packed(O.pack(O.FMT_Q4, codes.reshape(E * N, K)), dev).view(E, N, -1)
+            sfull = vkb.to_device_f16(scales, dev)
+            e0, el = D.expert_range(E, world, rank)
+            qloc, sloc = qfull[e0:e0 + el].contiguous(), sfull[e0:e0 + el].contiguous()
+            for f32 in (False, True):
+                ysym = comm.alloc((T, k, N), torch.float32 if f32 else torch.float16)
+                yv = ysym.tensor()
+                for call in range(2):
+                    idx_np = np.stack([rng.permutation(E)[:k] for _ in range(T)]).astype(np.int32)
+                    idx = torch.from_numpy(idx_np).to(dev)
+                    x = vkb.to_device_f16(rng.uniform(-1, 1, size=(T, K)).astype(np.float16).view(np.uint16), dev)
+                    yv.fill_(float("nan"))   # a slot nobody writes stays NaN and fails the comparison
+                    torch.cuda.synchronize()
+                    dist.barrier()           # no peer stores into this copy before the fill is done
+                    comm.moe_ep_p2p(qloc, sloc, idx, x, E_local=el, e0=e0, y_sym=ysym)
+                    torch.cuda.synchronize()
+                    y_one = vkb.moe(O.FMT_Q4, qfull, sfull, idx, x, out_f32=f32)
+                    torch.cuda.synchronize()
+                    out.append((f"moe_p2p E{E} N{N} K{K} T{T} k{k} f32={f32} call{call}",
+                                bool(torch.equal(y_one, yv)), 0.0, 1.0))
+                    dist.barrier()           # every rank compared before the next call's fill
+                ysym.free()
         status = vkb.device_status()
         comm.close()
         dist.barrier()

@@ -32,7 +32,6 @@ struct SymBuf {
     void* base;
     size_t data_bytes;
     void* peer[vkb::P2P_MAX_RANKS];
-    uint32_t epoch;
 };
 
 struct vkb_comm {
@@ -147,6 +146,18 @@ static SymBuf* find_sym(vkb_comm_t* c, const void* p, size_t need) {
     return nullptr;
 }
 
+// The kernels' view of a symmetric buffer: every rank's copy and its flags block.
+static P2PArgs p2p_args(const vkb_comm_t* c, const SymBuf& b) {
+    P2PArgs pp{};
+    for (int r = 0; r < c->size; ++r) {
+        pp.peer_base[r] = b.peer[r];
+        pp.peer_flags[r] = reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(b.peer[r]) + b.data_bytes);
+    }
+    pp.rank = c->rank;
+    pp.size = c->size;
+    return pp;
+}
+
 static int sym_free_one(vkb_comm_t* c, SymBuf& b) {
     int rc = 0;
     for (int r = 0; r < c->size; ++r)
@@ -232,9 +243,9 @@ int vkb_comm_alloc(vkb_comm_t* comm, size_t bytes, void** ptr) {
     if (comm->size > P2P_MAX_RANKS) return VKB_EUNSUPPORTED;
     SymBuf b{};
     b.data_bytes = (bytes + 255) / 256 * 256;
-    cudaError_t e = cudaMalloc(&b.base, b.data_bytes + P2P_FLAG_WORDS * 4);
+    cudaError_t e = cudaMalloc(&b.base, b.data_bytes + P2P_FLAG_BYTES);
     if (e != cudaSuccess) return -(int)e;
-    e = cudaMemset(b.base, 0, b.data_bytes + P2P_FLAG_WORDS * 4);
+    e = cudaMemset(b.base, 0, b.data_bytes + P2P_FLAG_BYTES);
     cudaIpcMemHandle_t h;
     if (e == cudaSuccess) e = cudaIpcGetMemHandle(&h, b.base);
     // every rank's handle to every rank, through the communicator
@@ -311,6 +322,19 @@ int vkb_moe_q4_ep(vkb_comm_t* comm, const void* qpool, const void* spool, const 
     return moe_ep(comm, VKB_FMT_Q4, qpool, spool, idx, T, topk, x, y, false, E_local, e0, N, K, (cudaStream_t)stream);
 }
 
+int vkb_moe_ep_p2p(vkb_comm_t* comm, int fmt, const void* qpool, const void* spool, const int32_t* idx, int T,
+                   int topk, const void* x, void* y_sym, int out_f32, int E_local, int e0, int N, int K,
+                   vkb_stream_t stream) {
+    if (!comm) return VKB_ENOCOMM;
+    if (!idx || !y_sym || T < 1 || topk < 1 || N < 1) return VKB_EINVAL;
+    if (comm->size > P2P_MAX_RANKS) return VKB_EUNSUPPORTED;
+    SymBuf* b = find_sym(comm, y_sym, (size_t)T * topk * N * (out_f32 ? 4 : 2));
+    if (!b) return VKB_EINVAL;   // y must come from vkb_comm_alloc and hold T*topk x N outputs
+    const P2PArgs pp = p2p_args(comm, *b);
+    return qmv_dispatch(fmt, qpool, spool, x, y_sym, out_f32 != 0, idx, N, K, T, topk, E_local, e0, 0,
+                        (cudaStream_t)stream, &pp);
+}
+
 size_t vkb_gemm_rowsplit_work_bytes(int M, int N, int out_f32) {
     if (M < 1 || N < 1) return 0;
     return (size_t)M * N * (out_f32 ? 4 : 2);
@@ -341,14 +365,7 @@ int vkb_gemm_q4_tc_rowsplit_p2p(vkb_comm_t* comm, const void* q_local, const voi
     if (N % comm->size != 0 || K % 256 != 0 || comm->size > P2P_MAX_RANKS) return VKB_EUNSUPPORTED;
     SymBuf* b = find_sym(comm, y_sym, (size_t)M * N * 2);
     if (!b) return VKB_EINVAL;   // y must come from vkb_comm_alloc and hold M x N fp16
-    P2PArgs pp{};
-    for (int r = 0; r < comm->size; ++r) {
-        pp.peer_base[r] = b->peer[r];
-        pp.peer_flags[r] = reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(b->peer[r]) + b->data_bytes);
-    }
-    pp.rank = comm->rank;
-    pp.size = comm->size;
-    pp.epoch = ++b->epoch;
+    const P2PArgs pp = p2p_args(comm, *b);
     const int nl = N / comm->size;
     TcOut out{N, comm->rank * nl, &pp};
     return tc_dispatch(q_local, s_local, x, y_sym, false, nl, K, M, (cudaStream_t)stream, &out);

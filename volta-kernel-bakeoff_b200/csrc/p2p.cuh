@@ -1,18 +1,34 @@
 // Peer-memory (NVLink) output exchange for the fused multi-GPU kernels: each rank's kernel stores its part of the
 // output straight into every rank's copy of a symmetric buffer (same size and layout on every rank, mapped into
-// every peer by CUDA IPC), ordered by per-call epochs in a flags block that follows the data in the buffer:
+// every peer by CUDA IPC), ordered by per-call epochs in a flags block that follows the data in the buffer.
 //
-//   flags[P2P_READY + p] = e   rank p has started call e on its stream (its earlier work, which may still read
-//                              this buffer, is done), so call e may write into rank p's buffer
-//   flags[P2P_DONE + p]  = e   every store of rank p's call e into this buffer is visible
-//   flags[P2P_COUNT]           this rank's count of CTAs that finished call e (local)
+// The protocol is per CTA: every rank launches the same grid for a call (the calls have equal shapes on every rank,
+// and the grid depends only on the shape and the device's SM count), and CTA b of one rank pairs with CTA b of every
+// other rank. Flags of the block (32-bit words):
 //
-// Protocol of call e (all waits bounded by time; a timeout raises DEV_ERR_PEER_TIMEOUT and gives up):
-//   1. after griddepcontrol.wait, one thread posts READY[rank] = e into every peer's flags (release, system scope);
-//   2. before its first remote store a warp waits until READY[p] >= e for every peer p in its own flags (acquire);
-//   3. every CTA: fence.acq_rel.sys, then an atomic count; the last CTA posts DONE[rank] = e into every peer and
-//      waits until DONE[p] >= e for every p, so the call's kernel ends only when the whole output is in place.
-// Epochs only grow (the host numbers the calls of a buffer from 1), so the flags never need resetting.
+//   READY[p][b] = e   CTA b of rank p has started call e (rank p's earlier work, which may still read this buffer,
+//                     is complete), so call e may write into rank p's buffer
+//   DONE[p][b]  = e   every store of CTA b of rank p for call e into this buffer is visible
+//   EPOCH[b]          the last call that CTA b completed on this rank (local)
+//
+// The kernels store their results into this rank's copy as on one GPU; as soon as a region (a tile) is complete,
+// the warps that wrote it push it to every peer with wide vector copies (p2p_push), overlapping the copies with the
+// CTA's next tiles. NVLink moves large writes far faster than the scattered 2-byte stores of an epilogue.
+//
+// Call e on rank r, CTA b (all waits bounded by time; a timeout raises DEV_ERR_PEER_TIMEOUT and gives up):
+//   1. after griddepcontrol.wait: e = EPOCH[b] + 1; post READY[r][b] = e into every peer (relaxed system-scope
+//      store: it orders nothing but the end of this rank's earlier kernels, which the grid dependency already did);
+//   2. before its first push a warp waits until READY[p][b] >= e for every peer p (in this rank's flags);
+//   3. after a barrier that follows all of the CTA's stores: one thread's fence.acq_rel.sys (cumulative: it releases
+//      the stores of every thread ordered before it by the barrier), then DONE[r][b] = e into every peer (relaxed),
+//      then it waits (acquire) until DONE[p][b] >= e for every peer p, and stores EPOCH[b] = e.
+// The kernel ends when all its CTAs have, i.e. when every CTA of every peer has delivered its part. One system-scope
+// fence per CTA is the only one on the critical path (a system fence costs microseconds on B200; acquire loads and
+// relaxed stores cost only the link latency).
+//
+// The epochs live in device memory, so a call captured in a CUDA graph numbers itself on every replay; they only
+// grow (from 1; the flags block starts zeroed), so the flags never need resetting. A rank whose grid differs from its
+// peers' (shapes that differ between ranks) leaves pairs unmatched: the waits time out and raise the status bit.
 #pragma once
 
 #include "ptx.cuh"
@@ -20,20 +36,21 @@
 namespace vkb {
 
 constexpr int P2P_MAX_RANKS = 8;
-constexpr int P2P_READY = 0;                      // [P2P_MAX_RANKS]
-constexpr int P2P_DONE = P2P_MAX_RANKS;           // [P2P_MAX_RANKS]
-constexpr int P2P_COUNT = 2 * P2P_MAX_RANKS;      // CTA counter of the current call
-constexpr int P2P_FLAG_WORDS = 64;                // flags block: 256 bytes after the data
+constexpr int P2P_MAX_CTAS = 256;                                  // grids of the fused kernels (<= SM count)
+constexpr int P2P_READY = 0;                                       // [P2P_MAX_RANKS][P2P_MAX_CTAS]
+constexpr int P2P_DONE = P2P_MAX_RANKS * P2P_MAX_CTAS;             // [P2P_MAX_RANKS][P2P_MAX_CTAS]
+constexpr int P2P_EPOCH = 2 * P2P_MAX_RANKS * P2P_MAX_CTAS;        // [P2P_MAX_CTAS]
+constexpr int P2P_FLAG_WORDS = P2P_EPOCH + P2P_MAX_CTAS;
+constexpr size_t P2P_FLAG_BYTES = (P2P_FLAG_WORDS * 4 + 255) / 256 * 256;   // the block after the (256-aligned) data
 
 struct P2PArgs {
     void* peer_base[P2P_MAX_RANKS];        // the symmetric buffer on every rank (peer_base[rank] = this rank's)
     uint32_t* peer_flags[P2P_MAX_RANKS];   // its flags block on every rank
     int rank, size;
-    uint32_t epoch;
 };
 
-__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
-    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+__device__ __forceinline__ void st_relaxed_sys(uint32_t* p, uint32_t v) {
+    asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
     uint32_t v;
@@ -53,37 +70,87 @@ __device__ __forceinline__ bool p2p_wait_flag(const uint32_t* flag, uint32_t e) 
                 raise_status(DEV_ERR_PEER_TIMEOUT);
                 return false;
             }
-            __nanosleep(256);
+            __nanosleep(64);
         }
     }
 }
 
-// Step 1 (one thread, after griddepcontrol.wait): this rank may now be written by call e.
-__device__ __forceinline__ void p2p_post_ready(const P2PArgs& p) {
-    for (int r = 0; r < p.size; ++r)
-        if (r != p.rank) st_release_sys(p.peer_flags[r] + P2P_READY + p.rank, p.epoch);
+// The number of this CTA's call (only after griddepcontrol.wait, or in a thread ordered after one that did).
+__device__ __forceinline__ uint32_t p2p_epoch(const P2PArgs& p) {
+    return *reinterpret_cast<volatile const uint32_t*>(p.peer_flags[p.rank] + P2P_EPOCH + blockIdx.x) + 1u;
 }
 
-// Step 2 (any thread; lane 0 of a warp, then __syncwarp): every peer accepts writes of call e.
-__device__ __forceinline__ bool p2p_wait_ready(const P2PArgs& p) {
-    const uint32_t* f = p.peer_flags[p.rank];
+// Step 1 (one thread per CTA, after griddepcontrol.wait).
+__device__ __forceinline__ void p2p_post_ready(const P2PArgs& p, uint32_t e) {
     for (int r = 0; r < p.size; ++r)
-        if (r != p.rank && !p2p_wait_flag(f + P2P_READY + r, p.epoch)) return false;
+        if (r != p.rank) st_relaxed_sys(p.peer_flags[r] + P2P_READY + p.rank * P2P_MAX_CTAS + blockIdx.x, e);
+}
+
+// Step 2 (lane 0 of a warp, then a warp broadcast): every peer's CTA of this index accepts writes of call e.
+__device__ __forceinline__ bool p2p_wait_ready(const P2PArgs& p, uint32_t e) {
+    const uint32_t* f = p.peer_flags[p.rank] + P2P_READY + blockIdx.x;
+    for (int r = 0; r < p.size; ++r)
+        if (r != p.rank && !p2p_wait_flag(f + r * P2P_MAX_CTAS, e)) return false;
     return true;
 }
 
-// Step 3 (every CTA, after __syncthreads that follows all of its stores; thread 0 only).
+// Push finished rows of this rank's copy to the same place in every peer's copy: `rows` rows of row_bytes bytes,
+// row r at byte offset row_off(r). Thread t of nth cooperating threads takes every nth vector, loads it once (the
+// rows were just written: L2) and stores it to each peer; four loads are in flight per thread. V is the widest word
+// that every row offset and row_bytes are multiples of (16 bytes: a warp's store then covers 512 contiguous bytes,
+// few and large NVLink writes instead of the scattered 2-byte stores of an epilogue). The rows must be complete and
+// visible to the calling threads (a barrier after their stores).
+template <typename V, typename RowOff>
+__device__ __forceinline__ void p2p_push_rows(const P2PArgs& p, int rows, int row_bytes, RowOff row_off, int t,
+                                              int nth) {
+    const int vpr = row_bytes / (int)sizeof(V);
+    if (rows <= 0 || vpr <= 0) return;
+    const int total = rows * vpr;
+    const uint8_t* src = static_cast<const uint8_t*>(p.peer_base[p.rank]);
+    constexpr int U = 4;
+    for (int v0 = t; v0 < total; v0 += U * nth) {
+        V val[U];
+        size_t o[U];
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            const int v = v0 + u * nth;
+            if (v < total) {
+                const int r = v / vpr, c = v - r * vpr;
+                o[u] = row_off(r) + (size_t)c * sizeof(V);
+                val[u] = *reinterpret_cast<const V*>(src + o[u]);
+            }
+        }
+        for (int k = 0; k < p.size; ++k) {
+            if (k == p.rank) continue;
+            uint8_t* dst = static_cast<uint8_t*>(p.peer_base[k]);
+#pragma unroll
+            for (int u = 0; u < U; ++u)
+                if (v0 + u * nth < total) *reinterpret_cast<V*>(dst + o[u]) = val[u];
+        }
+    }
+}
+
+// The widest copy word for byte offsets / lengths whose OR is m.
+template <typename RowOff>
+__device__ __forceinline__ void p2p_push(const P2PArgs& p, int rows, int row_bytes, size_t m, RowOff row_off, int t,
+                                         int nth) {
+    m |= (size_t)row_bytes;
+    if ((m & 15) == 0) p2p_push_rows<uint4>(p, rows, row_bytes, row_off, t, nth);
+    else if ((m & 3) == 0) p2p_push_rows<uint32_t>(p, rows, row_bytes, row_off, t, nth);
+    else p2p_push_rows<uint16_t>(p, rows, row_bytes, row_off, t, nth);
+}
+
+// Step 3 (one thread per CTA, after a barrier that follows every store of the CTA).
 __device__ __forceinline__ void p2p_finish(const P2PArgs& p) {
-    fence_acq_rel_sys();   // this CTA's stores (local and remote) before its count
+    const uint32_t e = p2p_epoch(p);
+    fence_acq_rel_sys();   // this CTA's stores (local and remote) before its DONE flags
+    for (int r = 0; r < p.size; ++r)
+        if (r != p.rank) st_relaxed_sys(p.peer_flags[r] + P2P_DONE + p.rank * P2P_MAX_CTAS + blockIdx.x, e);
     uint32_t* f = p.peer_flags[p.rank];
-    const uint32_t old = atomicAdd(f + P2P_COUNT, 1u);
-    if (old != gridDim.x - 1) return;
-    f[P2P_COUNT] = 0;      // every CTA of this call has counted; the next call starts from zero
-    fence_acq_rel_sys();
     for (int r = 0; r < p.size; ++r)
-        if (r != p.rank) st_release_sys(p.peer_flags[r] + P2P_DONE + p.rank, p.epoch);
-    for (int r = 0; r < p.size; ++r)
-        if (r != p.rank && !p2p_wait_flag(f + P2P_DONE + r, p.epoch)) return;
+        if (r != p.rank && !p2p_wait_flag(f + P2P_DONE + r * P2P_MAX_CTAS + blockIdx.x, e)) break;
+    // call e is complete for this CTA (also after a timeout, so the ranks' numbering stays aligned)
+    *reinterpret_cast<volatile uint32_t*>(f + P2P_EPOCH + blockIdx.x) = e;
 }
 
 }  // namespace vkb

@@ -28,6 +28,7 @@
 //   * per-tile partial sums of the NW warps are added in shared memory and written by warp 0.
 #pragma once
 
+#include "p2p.cuh"
 #include "ptx.cuh"
 
 namespace vkb {
@@ -44,7 +45,8 @@ constexpr int QMV_KS_UNIT = 256;   // stage widths are multiples of this (8 grou
 constexpr int QMV_ROWS = 16;       // weight rows per tile (the MMA's M)
 constexpr int QMV_MAXTOK = 8;      // tokens per MMA column group (the MMA's N)
 
-enum : int { QMV_DENSE = 0, QMV_MOE = 1 };
+// QMV_MOE_P2P: MoE whose outputs are also pushed into every peer's copy of y (expert parallelism, peer stores).
+enum : int { QMV_DENSE = 0, QMV_MOE = 1, QMV_MOE_P2P = 2 };
 
 struct QmvArgs {
     const __half* x;         // [T][K]
@@ -55,6 +57,7 @@ struct QmvArgs {
     int topk;                // MoE: slots per token
     int E_local, e0;         // MoE: experts held in this pool, id of the first one
     int zero_foreign;        // MoE: write zeros into the slots of experts outside the pool (expert-parallel combine)
+    P2PArgs pp;              // QMV_MOE_P2P: every rank's copy of y (pp.peer_base) and flags of the epoch protocol
     int KS, nchunks;         // stage width in k values, stages per row tile
     int cpitch, spitch;      // shared bytes per row of a stage: codes (KS*bits/8 + pad), scales (KS/16 + 16)
     int nstage;              // ring depth
@@ -284,6 +287,37 @@ __device__ __forceinline__ int moe_route(const QmvArgs& a, MoeTables tb) {
     return tb.segoff[a.E_local];
 }
 
+// ---- expert-parallel MoE with peer stores: the push of a CTA's outputs ---------------------------------------------
+//
+// Called by every consumer thread after its tile loop (also after a failed wait). The CTA's outputs are then complete
+// in this rank's y: segment sg's slots over the CTA's tiles [w0, w1) of that segment, one contiguous run of n per
+// slot. After a barrier every consumer thread pushes them to the peers (p2p_push); after a second barrier thread 0's
+// system-scope fence in p2p_finish releases the stores of every consumer thread (the producer warp stores nothing).
+// Kept out of line, so that the tile loop's register allocation does not carry it.
+template <typename OutT>
+__device__ __noinline__ void qmv_moe_push(const QmvArgs& a, MoeTables tb, int w0, int w1, bool ok) {
+    named_sync(1, QMV_NW * 32);
+    bool rd = ok;
+    if ((threadIdx.x & 31) == 0 && rd) rd = p2p_wait_ready(a.pp, p2p_epoch(a.pp));
+    rd = __shfl_sync(0xffffffffu, rd ? 1 : 0, 0) != 0;
+    if (rd && w1 > w0) {
+        const size_t rowp = (size_t)a.N * sizeof(OutT);
+        for (int sg = w0 / a.tilesN; sg <= (w1 - 1) / a.tilesN; ++sg) {
+            const int ta = max(w0, sg * a.tilesN) - sg * a.tilesN;
+            const int tb_ = min(w1, (sg + 1) * a.tilesN) - sg * a.tilesN;
+            const int n0 = ta * QMV_ROWS, n1 = min(a.N, tb_ * QMV_ROWS);
+            if (n1 <= n0) continue;
+            const int first = tb.seg[sg] & 0xFFFF, e = tb.seg[sg] >> 16;
+            const int cnt = min(QMV_MAXTOK, tb.off[e + 1] - first);
+            const size_t off0 = (size_t)n0 * sizeof(OutT);
+            p2p_push(a.pp, cnt, (n1 - n0) * (int)sizeof(OutT), rowp | off0,
+                     [&](int r) { return (size_t)tb.slots[first + r] * rowp + off0; }, threadIdx.x, QMV_NW * 32);
+        }
+    }
+    named_sync(1, QMV_NW * 32);
+    if (threadIdx.x == 0) p2p_finish(a.pp);
+}
+
 // ---- the kernel ---------------------------------------------------------------------------------------------------
 //
 // The consumer warps form WG groups of QMV_NW / WG warps. Group j takes every WG-th tile of the CTA's range (tiles
@@ -300,7 +334,7 @@ __host__ __device__ constexpr int qmv_nbars(int nstage) { return 2 * nstage + 4 
 
 template <int F, int MODE, typename OutT>
 __global__ void __launch_bounds__(32 * (QMV_NW + 1), 2)
-qmv_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap ts, const QmvArgs a) {
+qmv_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap ts, const __grid_constant__ QmvArgs a) {
     const int WG = a.wg;
     const int WPG = QMV_NW / WG;
     extern __shared__ uint8_t smem_raw[];
@@ -340,7 +374,7 @@ qmv_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUten
 
     int nseg = 1;
     MoeTables tb{};
-    if constexpr (MODE == QMV_MOE) {
+    if constexpr (MODE != QMV_DENSE) {
         tb = moe_tables(sm + a.moe_off, a.E_local, a.T * a.topk);
         nseg = moe_route(a, tb);   // contains __syncthreads
     } else {
@@ -354,17 +388,17 @@ qmv_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUten
 
     // segment accessors: expert (weight row base), token count, and the slot (dense: token) of column j
     auto seg_expert = [&](int sg) -> int {
-        if constexpr (MODE == QMV_MOE) return tb.seg[sg] >> 16; else return 0;
+        if constexpr (MODE != QMV_DENSE) return tb.seg[sg] >> 16; else return 0;
     };
     auto seg_first = [&](int sg) -> int {
-        if constexpr (MODE == QMV_MOE) return tb.seg[sg] & 0xFFFF; else return 0;
+        if constexpr (MODE != QMV_DENSE) return tb.seg[sg] & 0xFFFF; else return 0;
     };
     auto seg_count = [&](int sg) -> int {
-        if constexpr (MODE == QMV_MOE) return min(QMV_MAXTOK, tb.off[(tb.seg[sg] >> 16) + 1] - seg_first(sg));
+        if constexpr (MODE != QMV_DENSE) return min(QMV_MAXTOK, tb.off[(tb.seg[sg] >> 16) + 1] - seg_first(sg));
         else return a.T;
     };
     auto seg_slot = [&](int sg, int j) -> int {
-        if constexpr (MODE == QMV_MOE) return tb.slots[seg_first(sg) + j]; else return j;
+        if constexpr (MODE != QMV_DENSE) return tb.slots[seg_first(sg) + j]; else return j;
     };
 
     constexpr int BITS = FmtTraits<F>::BITS;
@@ -405,7 +439,7 @@ qmv_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUten
                 mbar_arrive_expect_tx(&xfull[xb], (uint32_t)(cnt * a.K * 2));
                 for (int j = 0; j < cnt; ++j) {
                     int tok = seg_slot(xs, j);
-                    if constexpr (MODE == QMV_MOE) tok /= a.topk;
+                    if constexpr (MODE != QMV_DENSE) tok /= a.topk;
                     bulk_load(dst + j * a.xpitch, a.x + (size_t)tok * a.K, (uint32_t)(a.K * 2), &xfull[xb]);
                 }
                 ++xsegs;
@@ -455,7 +489,10 @@ qmv_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUten
     const uint32_t s_row = (uint32_t)(QMV_ROWS * a.cpitch) + g * sp;     // row g's scales inside a stage
     OutT* y = reinterpret_cast<OutT*>(a.y);
     pdl_wait();   // x and y may still be written (or y read) by the previous grid
-    if constexpr (MODE == QMV_MOE) {
+    if constexpr (MODE == QMV_MOE_P2P) {   // peer stores: this rank's copy may be written from now on
+        if (warp == 0 && lane == 0) p2p_post_ready(a.pp, p2p_epoch(a.pp));
+    }
+    if constexpr (MODE != QMV_DENSE) {
         if (a.zero_foreign) {   // another rank computes these slots; the combine adds this rank's zeros to them
             const int nslots = a.T * a.topk;
             for (int i = blockIdx.x; i < nslots; i += gridDim.x) {
@@ -556,6 +593,7 @@ qmv_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUten
     // release the rest of the CTA's segments (also those this group had no tile in)
     if (ok) ok = enter_upto(last_seg - first_seg);
     leave();
+    if constexpr (MODE == QMV_MOE_P2P) qmv_moe_push<OutT>(a, tb, w0, w1, ok);
 }
 
 }  // namespace vkb

@@ -68,7 +68,7 @@ struct TcArgs {
     int x_off, p_off, bar_off;   // shared-memory region offsets (1024-aligned)
     int tmem_cols;
     int ldy, ycol0;     // output row stride and first column (row split: the full y, this rank's columns)
-    int p2p;            // 1: also store into every peer's copy of y (pp.peer_base) and run the epoch protocol
+    int p2p;            // 1: push every tile into every peer's copy of y (pp.peer_base), epoch protocol (P2P kernels)
     P2PArgs pp;
 };
 
@@ -215,10 +215,21 @@ template <typename OutT> __device__ __forceinline__ OutT tc_out(float v);
 template <> __device__ __forceinline__ __half tc_out<__half>(float v) { return __float2half_rn(v); }
 template <> __device__ __forceinline__ float tc_out<float>(float v) { return v; }
 
-template <typename OutT, int PK>
+// Push the finished tile (weight rows row0.., tokens tok0..) from this rank's y to every peer; thread t of nth.
+// Out of line, so that the epilogue's register allocation does not carry it.
+template <typename OutT>
+__device__ __noinline__ void tc_push_tile(const TcArgs& a, int row0, int tok0, int t, int nth) {
+    const int rows = min(a.NT, a.M - tok0), cols = min(TC_BM, a.N - row0);
+    const size_t off = ((size_t)tok0 * a.ldy + a.ycol0 + row0) * sizeof(OutT);
+    const size_t pitch = (size_t)a.ldy * sizeof(OutT);
+    p2p_push(a.pp, rows, cols * (int)sizeof(OutT), off | pitch, [&](int r) { return off + (size_t)r * pitch; }, t,
+             nth);
+}
+
+template <typename OutT, int PK, bool P2P>
 __global__ void __launch_bounds__(TC_THREADS, 1)
 tc_q4_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap ts,
-             const __grid_constant__ CUtensorMap tx, const TcArgs a) {
+             const __grid_constant__ CUtensorMap tx, const __grid_constant__ TcArgs a) {
     constexpr int PPITCH = tc_ppitch(PK), PCHUNK = tc_pchunk(PK), SCOFF = TC_BM * PPITCH;
     extern __shared__ uint8_t smem_raw[];
     const uint32_t pad = (1024u - (smem_u32(smem_raw) & 1023u)) & 1023u;
@@ -462,66 +473,67 @@ tc_q4_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUt
     // Epilogue warps (12-15) empty every accumulator; the dequantising warps, idle by then, join for the CTA's last
     // tile, whose epilogue nothing else overlaps. A warp reads TMEM lanes 32 (w % 4).. (weight rows): the participants
     // of a lane quarter take interleaved 32-token chunks, two TMEM loads in flight, and store y directly (a warp's
-    // store covers 32 consecutive outputs of one token: 64 or 128 contiguous bytes).
+    // store covers 32 consecutive outputs of one token: 64 or 128 contiguous bytes). With peer stores, the
+    // participants of a tile then push the finished tile from this rank's y to every peer (p2p_push: 16-byte words)
+    // while the MMA warp works on the next tile.
     if (warp >= TC_WDQ0) {
         const bool epi = warp >= TC_WEPI0;
         const int q = warp & 3;
         const int sub = epi ? 0 : 1 + ((warp - TC_WDQ0) >> 2);   // participant index within the lane quarter
         pdl_wait();   // y may still be read or written by the previous grid
-        if (a.p2p) {   // this rank's copy may now be written; wait until every peer's may be
-            if (blockIdx.x == 0 && warp == TC_WEPI0 && lane == 0) p2p_post_ready(a.pp);
-            if (lane == 0 && !p2p_wait_ready(a.pp)) ok = false;
+        uint32_t p2p_e = 0;
+        if constexpr (P2P) {   // this rank's copy may now be written; wait until every peer's may be
+            p2p_e = p2p_epoch(a.pp);
+            if (warp == TC_WEPI0 && lane == 0) p2p_post_ready(a.pp, p2p_e);
+            if (lane == 0 && !p2p_wait_ready(a.pp, p2p_e)) ok = false;
             ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
         }
         OutT* y = reinterpret_cast<OutT*>(a.y);
-        for (int i = epi ? 0 : ntl - 1; i < ntl && ok; ++i) {
+        // With peer stores every participant of a tile passes the tile's named barrier, also after a failed wait (it
+        // then skips the work), so that no barrier waits for a warp that left the loop.
+        for (int i = epi ? 0 : ntl - 1; i < ntl && (ok || P2P); ++i) {
             const int acc = i % a.nacc, t = tile_of(i), row0 = row0_of(t), tok0 = tok0_of(t);
             const bool last = i == ntl - 1;
             const int parts = last ? 3 : 1;
-            ok = __all_sync(0xffffffffu, wait_parity_sleep(&accfull[acc], (i / a.nacc) & 1));
-            if (!ok) break;
-            tc_fence_after();
-            const uint32_t tq_addr = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(acc * 128);
-            const int n = row0 + 32 * q + lane;
-            const int step = 32 * parts;
-            auto put = [&](const uint32_t (&v)[32], int c) {
-                if (n >= a.N) return;
-                const size_t off = (size_t)(tok0 + c) * a.ldy + a.ycol0 + n;
-                const int lim = a.M - (tok0 + c);
-                if (!a.p2p) {
-                    OutT* yp = y + off;
+            if (ok) ok = __all_sync(0xffffffffu, wait_parity_sleep(&accfull[acc], (i / a.nacc) & 1));
+            if (ok) {
+                tc_fence_after();
+                const uint32_t tq_addr = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(acc * 128);
+                const int n = row0 + 32 * q + lane;
+                const int step = 32 * parts;
+                auto put = [&](const uint32_t (&v)[32], int c) {
+                    if (n >= a.N) return;
+                    OutT* yp = y + (size_t)(tok0 + c) * a.ldy + a.ycol0 + n;
+                    const int lim = a.M - (tok0 + c);
 #pragma unroll
                     for (int j = 0; j < 32; ++j, yp += a.ldy)
                         if (j < lim) *yp = tc_out<OutT>(__uint_as_float(v[j]));
-                } else {   // every rank's copy, this rank's included (peer stores go over NVLink)
-                    for (int r = 0; r < a.pp.size; ++r) {
-                        OutT* yp = reinterpret_cast<OutT*>(a.pp.peer_base[r]) + off;
-#pragma unroll 8
-                        for (int j = 0; j < 32; ++j, yp += a.ldy)
-                            if (j < lim) *yp = tc_out<OutT>(__uint_as_float(v[j]));
-                    }
+                };
+                uint32_t va[32], vb[32];
+                int c = 32 * sub;
+                if (c < a.NT) tmem_ld32_async(tq_addr + (uint32_t)c, va);
+                for (; c < a.NT; c += 2 * step) {
+                    tmem_wait_ld(va);
+                    if (c + step < a.NT) tmem_ld32_async(tq_addr + (uint32_t)(c + step), vb);
+                    put(va, c);
+                    if (c + step >= a.NT) break;
+                    tmem_wait_ld(vb);
+                    if (c + 2 * step < a.NT) tmem_ld32_async(tq_addr + (uint32_t)(c + 2 * step), va);
+                    put(vb, c + step);
                 }
-            };
-            uint32_t va[32], vb[32];
-            int c = 32 * sub;
-            if (c < a.NT) tmem_ld32_async(tq_addr + (uint32_t)c, va);
-            for (; c < a.NT; c += 2 * step) {
-                tmem_wait_ld(va);
-                if (c + step < a.NT) tmem_ld32_async(tq_addr + (uint32_t)(c + step), vb);
-                put(va, c);
-                if (c + step >= a.NT) break;
-                tmem_wait_ld(vb);
-                if (c + 2 * step < a.NT) tmem_ld32_async(tq_addr + (uint32_t)(c + 2 * step), va);
-                put(vb, c + step);
+                // every TMEM read of this accumulator has completed: the MMA warp may overwrite it
+                if (epi) {
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&accempty[acc]);
+                }
             }
-            // every TMEM read of this accumulator has completed: the MMA warp may overwrite it
-            if (epi) {
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&accempty[acc]);
+            if constexpr (P2P) {   // the tile is complete in this rank's copy: its participants push it to every peer
+                named_sync(2, 128u * (uint32_t)parts);
+                if (ok) tc_push_tile<OutT>(a, row0, tok0, (epi ? warp - TC_WEPI0 : warp - TC_WDQ0 + 4) * 32 + lane,
+                                           128 * parts);
             }
         }
-        if (a.p2p) fence_acq_rel_sys();   // this thread's peer stores before the CTA's completion count
     }
     // teardown: every MMA has completed (the epilogue waited on each accumulator) before TMEM is released
     if (warp == 1 && !ok && ntl > 0) wait_parity_sleep(&accfull[(ntl - 1) % a.nacc], ((ntl - 1) / a.nacc) & 1,
@@ -532,7 +544,9 @@ tc_q4_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUt
         tc_fence_after();
         tmem_dealloc(tmem, (uint32_t)a.tmem_cols);
     }
-    if (a.p2p && threadIdx.x == 0) p2p_finish(a.pp);   // every store of this CTA is done (the barrier above)
+    // every store of this CTA precedes the barrier above; thread 0's system-scope fence in p2p_finish releases them
+    // all (cumulativity), so no per-thread fence is needed
+    if (P2P && threadIdx.x == 0) p2p_finish(a.pp);
 }
 
 }  // namespace vkb

@@ -6,6 +6,7 @@
 #include <cstdlib>
 #include <cstring>
 #include <mutex>
+#include <type_traits>
 #include <unordered_map>
 
 #include "../../include/vkb.h"
@@ -280,8 +281,9 @@ static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 
 // Common body of the dense and MoE entry points.
 template <int F>
 static int qmv_entry(const void* q, const void* s, const void* x, void* y, bool f32, const int32_t* idx, int N, int K,
-                     int M, int topk, int E_local, int e0, int zero_foreign, cudaStream_t st) {
+                     int M, int topk, int E_local, int e0, int zero_foreign, cudaStream_t st, const P2PArgs* p2p) {
     const bool moe = idx != nullptr;
+    if (p2p && (!moe || zero_foreign)) return VKB_EINVAL;
     if (!q || !s || !x || !y) return VKB_EINVAL;
     if (N < 1 || K < 32 || M < 1) return VKB_EINVAL;
     if (K % 32 != 0) return VKB_EUNSUPPORTED;
@@ -315,18 +317,23 @@ static int qmv_entry(const void* q, const void* s, const void* x, void* y, bool 
         p.a.E_local = E_local;
         p.a.e0 = e0;
         p.a.zero_foreign = zero_foreign;
+        if (p2p) p.a.pp = *p2p;
         int grid;
         if (moe) {
             grid = d.sm_count;
         } else {
             grid = p.a.tilesN < d.sm_count ? p.a.tilesN : d.sm_count;
         }
+        if (p2p && grid > P2P_MAX_CTAS) return VKB_EUNSUPPORTED;   // one flag pair per CTA
         if (moe)
-            return f32 ? launch_qmv<F, QMV_MOE, float>(p, tq, ts, grid, st, dev)
-                       : launch_qmv<F, QMV_MOE, __half>(p, tq, ts, grid, st, dev);
+            return p2p ? (f32 ? launch_qmv<F, QMV_MOE_P2P, float>(p, tq, ts, grid, st, dev)
+                              : launch_qmv<F, QMV_MOE_P2P, __half>(p, tq, ts, grid, st, dev))
+                       : (f32 ? launch_qmv<F, QMV_MOE, float>(p, tq, ts, grid, st, dev)
+                              : launch_qmv<F, QMV_MOE, __half>(p, tq, ts, grid, st, dev));
         return f32 ? launch_qmv<F, QMV_DENSE, float>(p, tq, ts, grid, st, dev)
                    : launch_qmv<F, QMV_DENSE, __half>(p, tq, ts, grid, st, dev);
     }
+    if (p2p) return VKB_EUNSUPPORTED;   // peer stores: the pipelined kernel only
     // general path: 4-byte aligned words for Q4/Q2, 2-byte aligned fp16
     if (F != FMT_Q8 && (reinterpret_cast<uintptr_t>(q) & 3u)) return VKB_EUNSUPPORTED;
     if ((reinterpret_cast<uintptr_t>(s) | reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(y)) & 1u)
@@ -336,11 +343,14 @@ static int qmv_entry(const void* q, const void* s, const void* x, void* y, bool 
 }
 
 int qmv_dispatch(int fmt, const void* q, const void* s, const void* x, void* y, bool f32, const int32_t* idx, int N,
-                 int K, int M, int topk, int E_local, int e0, int zero_foreign, cudaStream_t st) {
+                 int K, int M, int topk, int E_local, int e0, int zero_foreign, cudaStream_t st, const P2PArgs* p2p) {
     switch (fmt) {
-        case VKB_FMT_Q4: return qmv_entry<FMT_Q4>(q, s, x, y, f32, idx, N, K, M, topk, E_local, e0, zero_foreign, st);
-        case VKB_FMT_Q8: return qmv_entry<FMT_Q8>(q, s, x, y, f32, idx, N, K, M, topk, E_local, e0, zero_foreign, st);
-        case VKB_FMT_Q2: return qmv_entry<FMT_Q2>(q, s, x, y, f32, idx, N, K, M, topk, E_local, e0, zero_foreign, st);
+        case VKB_FMT_Q4:
+            return qmv_entry<FMT_Q4>(q, s, x, y, f32, idx, N, K, M, topk, E_local, e0, zero_foreign, st, p2p);
+        case VKB_FMT_Q8:
+            return qmv_entry<FMT_Q8>(q, s, x, y, f32, idx, N, K, M, topk, E_local, e0, zero_foreign, st, p2p);
+        case VKB_FMT_Q2:
+            return qmv_entry<FMT_Q2>(q, s, x, y, f32, idx, N, K, M, topk, E_local, e0, zero_foreign, st, p2p);
         default: return VKB_EUNSUPPORTED;
     }
 }
@@ -416,6 +426,18 @@ static bool plan_tc(int N, int K, int M, int out_bytes, const DeviceInfo& d, TcP
     return false;
 }
 
+// Opt one prompt-GEMM kernel variant into the device's shared memory, once per device.
+template <typename OutT, int PK, bool P2P>
+static int tc_attr(int dev, int smem_optin) {
+    static std::once_flag once[kMaxDevices];
+    static cudaError_t err[kMaxDevices];
+    std::call_once(once[dev], [&] {
+        err[dev] = cudaFuncSetAttribute(tc_q4_kernel<OutT, PK, P2P>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        smem_optin);
+    });
+    return err[dev] == cudaSuccess ? 0 : -(int)err[dev];
+}
+
 template <typename OutT>
 static int tc_entry(const void* q, const void* s, const void* x, void* y, int N, int K, int M, cudaStream_t st,
                     const TcOut* out = nullptr) {
@@ -434,6 +456,7 @@ static int tc_entry(const void* q, const void* s, const void* x, void* y, int N,
     p.a.ycol0 = out ? out->col0 : 0;
     p.a.p2p = out && out->p2p ? 1 : 0;
     if (p.a.p2p) p.a.pp = *out->p2p;
+    if (p.a.p2p && p.grid.x > (unsigned)P2P_MAX_CTAS) return VKB_EUNSUPPORTED;   // one flag pair per CTA
     CUtensorMap tq, ts, tx;
     int r = get_tmap_2d(&tq, q, (uint64_t)N, (uint64_t)K / 2, CU_TENSOR_MAP_DATA_TYPE_UINT64, 8,
                         (uint32_t)tc_ppitch(p.pk) / 8, TC_BM, CU_TENSOR_MAP_SWIZZLE_NONE);
@@ -443,17 +466,18 @@ static int tc_entry(const void* q, const void* s, const void* x, void* y, int N,
     if (r) return r;
     r = get_tmap_x3d(&tx, x, M, K, p.a.NT, p.a.xk);
     if (r) return r;
-    auto kern = p.pk == 8 ? tc_q4_kernel<OutT, 8> : tc_q4_kernel<OutT, 4>;
-    static std::once_flag once[kMaxDevices];
-    static cudaError_t attr_err[kMaxDevices];
-    std::call_once(once[dev], [&] {
-        attr_err[dev] = cudaFuncSetAttribute(tc_q4_kernel<OutT, 8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             d.smem_optin);
-        if (attr_err[dev] == cudaSuccess)
-            attr_err[dev] = cudaFuncSetAttribute(tc_q4_kernel<OutT, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                 d.smem_optin);
-    });
-    if (attr_err[dev] != cudaSuccess) return -(int)attr_err[dev];
+    void (*kern)(CUtensorMap, CUtensorMap, CUtensorMap, TcArgs) = nullptr;
+    int ra = 0;
+    if (!p.a.p2p) {
+        kern = p.pk == 8 ? tc_q4_kernel<OutT, 8, false> : tc_q4_kernel<OutT, 4, false>;
+        ra = p.pk == 8 ? tc_attr<OutT, 8, false>(dev, d.smem_optin) : tc_attr<OutT, 4, false>(dev, d.smem_optin);
+    } else if constexpr (std::is_same<OutT, __half>::value) {   // peer stores: fp16 outputs only
+        kern = p.pk == 8 ? tc_q4_kernel<OutT, 8, true> : tc_q4_kernel<OutT, 4, true>;
+        ra = p.pk == 8 ? tc_attr<OutT, 8, true>(dev, d.smem_optin) : tc_attr<OutT, 4, true>(dev, d.smem_optin);
+    } else {
+        return VKB_EUNSUPPORTED;
+    }
+    if (ra) return ra;
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = p.grid;
     cfg.blockDim = dim3(TC_THREADS);

@@ -28,9 +28,10 @@ int get_tmap_2d(CUtensorMap* out, const void* ptr, uint64_t rows, uint64_t row_b
 
 // The decode / MoE entry (formats VKB_FMT_*; idx == nullptr: dense) and the prompt GEMM entry, shared with the
 // multi-GPU entry points. Same return codes as the C ABI.
-int qmv_dispatch(int fmt, const void* q, const void* s, const void* x, void* y, bool f32, const int32_t* idx, int N,
-                 int K, int M, int topk, int E_local, int e0, int zero_foreign, cudaStream_t st);
 struct P2PArgs;
+int qmv_dispatch(int fmt, const void* q, const void* s, const void* x, void* y, bool f32, const int32_t* idx, int N,
+                 int K, int M, int topk, int E_local, int e0, int zero_foreign, cudaStream_t st,
+                 const P2PArgs* p2p = nullptr);
 // Where the prompt GEMM writes: y rows of ldy elements starting at column col0, and with p2p also into every peer's
 // copy of a symmetric buffer (epoch protocol of p2p.cuh).
 struct TcOut {

@@ -95,6 +95,7 @@ def _register_optional(L) -> None:
         "vkb_comm_alloc": ([vp, ctypes.c_size_t, ctypes.POINTER(vp)], i),
         "vkb_comm_free": ([vp, vp], i),
         "vkb_gemm_q4_tc_rowsplit_p2p": ([vp, vp, vp, vp, vp, i, i, i, vp], i),
+        "vkb_moe_ep_p2p": ([vp, i, vp, vp, vp, i, i, vp, vp, i, i, i, i, i, vp], i),
         "vkb_graph_begin": ([vp], i),
         "vkb_graph_end": ([vp, ctypes.POINTER(vp)], i),
         "vkb_graph_launch": ([vp, vp], i),

@@ -105,6 +105,19 @@ class Comm:
         check(rc, "vkb_moe_ep")
         return y
 
+    def moe_ep_p2p(self, qpool, spool, idx, x, E_local: int, e0: int, y_sym: "SymTensor", fmt: int = FMT_Q4,
+                   stream=None):
+        """Expert-parallel MoE with the combine fused into the kernel (peer stores over NVLink): y_sym (from alloc,
+        [T][k][N], fp16 or fp32) holds every slot on every rank after the call."""
+        import torch
+        N = spool.shape[1]
+        T, topk = idx.shape
+        K = x.shape[1]
+        rc = lib().vkb_moe_ep_p2p(self._h, fmt, _ptr(qpool), _ptr(spool), _ptr(idx), T, topk, _ptr(x), y_sym.ptr,
+                                  int(y_sym.dtype == torch.float32), E_local, e0, N, K, _stream(stream))
+        check(rc, "vkb_moe_ep_p2p")
+        return y_sym
+
     def alloc(self, shape, dtype):
         """A symmetric tensor (collective: same shape on every rank): this rank's buffer, mapped into every peer, for
         the fused peer-store calls. Freed with free()."""
