@@ -126,7 +126,7 @@ int vkb_gemm_q4_tc_rowsplit_noalloc(vkb_comm_t* comm, const void* q_local, const
 
 /* ---- multi-GPU, fused: the exchange inside the kernel (peer stores over NVLink, no NCCL call) --------------------
  * Symmetric device buffers: collective, the same `bytes` on every rank; each rank's buffer is mapped into every peer
- * (CUDA IPC, exchanged over the communicator) and followed by a 17 KiB flags block. Freed by vkb_comm_free
+ * (CUDA IPC, exchanged over the communicator) and followed by an 8448-byte flags block. Freed by vkb_comm_free
  * (collective) or vkb_comm_destroy. At most 8 ranks.
  * The fused calls below write every rank's copy of a symmetric y. Every rank makes the same fused calls on a buffer in
  * the same order; each call is numbered by an epoch kept in the buffer's flags (device memory, so the calls may be

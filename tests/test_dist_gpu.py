@@ -105,7 +105,7 @@ def _rank_main(rank, world, port, q):
                 out.append((f"rowsplit_p2p N{N} K{K} M{M} call{i}", bool(torch.equal(y_one, snaps[i])), 0.0, 1.0))
             ysym.free()
             # the same call captured once in a CUDA graph and replayed: the epochs live in device memory, so every
-            # replay is a new call (the buffer's per-CTA epoch words, after the 256-byte aligned data, count the replays)
+            # replay is a new call (the buffer's epoch word, in the flags after the 256-byte aligned data, counts the replays)
             if (N, K, M) == (1024, 2048, 64):
                 ysym = comm.alloc((M, N), torch.float16)
                 yv = ysym.tensor()
@@ -122,9 +122,9 @@ def _rank_main(rank, world, port, q):
                 torch.cuda.synchronize()
                 del g
                 data_bytes = (M * N * 2 + 255) // 256 * 256
-                flags = _raw_u32(torch, ysym.ptr.value, data_bytes + 4352 * 4)[data_bytes // 4:]
-                # EPOCH[cta] words (after READY and DONE, 8 ranks x 256 CTAs each): CTA 0 completed every replay
-                out.append(("rowsplit_p2p graph epochs", int(flags[4096].item()) == len(xs), 0.0, 1.0))
+                flags = _raw_u32(torch, ysym.ptr.value, data_bytes + 2058 * 4)[data_bytes // 4:]
+                # the EPOCH word follows READY [8 ranks][256 CTAs], DONE [8 ranks] and the CTA count
+                out.append(("rowsplit_p2p graph epochs", int(flags[2057].item()) == len(xs), 0.0, 1.0))
                 for i, x in enumerate(xs):
                     y_one = vkb.gemm_tc(qfull, sfull, x)
                     torch.cuda.synchronize()

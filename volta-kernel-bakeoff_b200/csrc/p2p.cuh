@@ -2,33 +2,36 @@
 // output straight into every rank's copy of a symmetric buffer (same size and layout on every rank, mapped into
 // every peer by CUDA IPC), ordered by per-call epochs in a flags block that follows the data in the buffer.
 //
-// The protocol is per CTA: every rank launches the same grid for a call (the calls have equal shapes on every rank,
-// and the grid depends only on the shape and the device's SM count), and CTA b of one rank pairs with CTA b of every
-// other rank. Flags of the block (32-bit words):
-//
-//   READY[p][b] = e   CTA b of rank p has started call e (rank p's earlier work, which may still read this buffer,
-//                     is complete), so call e may write into rank p's buffer
-//   DONE[p][b]  = e   every store of CTA b of rank p for call e into this buffer is visible
-//   EPOCH[b]          the last call that CTA b completed on this rank (local)
-//
 // The kernels store their results into this rank's copy as on one GPU; as soon as a region (a tile) is complete,
 // the warps that wrote it push it to every peer with wide vector copies (p2p_push), overlapping the copies with the
 // CTA's next tiles. NVLink moves large writes far faster than the scattered 2-byte stores of an epilogue.
 //
-// Call e on rank r, CTA b (all waits bounded by time; a timeout raises DEV_ERR_PEER_TIMEOUT and gives up):
-//   1. after griddepcontrol.wait: e = EPOCH[b] + 1; post READY[r][b] = e into every peer (relaxed system-scope
-//      store: it orders nothing but the end of this rank's earlier kernels, which the grid dependency already did);
-//   2. before its first push a warp waits until READY[p][b] >= e for every peer p (in this rank's flags);
-//   3. after a barrier that follows all of the CTA's stores: one thread's fence.acq_rel.sys (cumulative: it releases
-//      the stores of every thread ordered before it by the barrier), then DONE[r][b] = e into every peer (relaxed),
-//      then it waits (acquire) until DONE[p][b] >= e for every peer p, and stores EPOCH[b] = e.
-// The kernel ends when all its CTAs have, i.e. when every CTA of every peer has delivered its part. One system-scope
-// fence per CTA is the only one on the critical path (a system fence costs microseconds on B200; acquire loads and
-// relaxed stores cost only the link latency).
+// Every rank launches the same grid for a call (the calls have equal shapes on every rank, and the grid depends only
+// on the shape and the device's SM count); CTA b of one rank pairs with CTA b of every other rank for READY. Flags of
+// the block (32-bit words):
 //
-// The epochs live in device memory, so a call captured in a CUDA graph numbers itself on every replay; they only
+//   READY[p][b] = e   CTA b of rank p has started call e (rank p's earlier work, which may still read this buffer,
+//                     is complete), so call e may write into rank p's buffer
+//   DONE[p]     = e   every store of rank p's call e into this buffer is visible
+//   COUNT             CTAs of this rank that finished the current call (local)
+//   EPOCH             the last call completed on this rank (local)
+//
+// Call e on rank r (all waits bounded by time; a timeout raises DEV_ERR_PEER_TIMEOUT and gives up):
+//   1. after griddepcontrol.wait every CTA b reads e = EPOCH + 1 and posts READY[r][b] = e into every peer (relaxed
+//      system-scope store: it orders nothing but the end of this rank's earlier kernels, which the grid dependency
+//      already did);
+//   2. before its first push a warp waits until READY[p][b] >= e for every peer p (in this rank's flags);
+//   3. after a barrier that follows all of its stores, one thread of every CTA makes a GPU-scope release
+//      (fence.acq_rel.gpu, cumulative over the barrier) and counts the CTA; the last CTA acquires the others
+//      (fence.acq_rel.sys, which also releases the whole grid's stores to the system), posts DONE[r] = e into every
+//      peer (relaxed) and waits (acquire) until DONE[p] >= e for every peer p, then stores EPOCH = e.
+// So the kernel ends only when every peer's part has arrived. A system-scope fence costs microseconds on B200, more
+// when many SMs issue one at once; GPU-scope fences, acquire loads and relaxed stores cost about the link latency.
+// One uncontended system fence per call is the only one on the critical path.
+//
+// The epoch lives in device memory, so a call captured in a CUDA graph numbers itself on every replay; epochs only
 // grow (from 1; the flags block starts zeroed), so the flags never need resetting. A rank whose grid differs from its
-// peers' (shapes that differ between ranks) leaves pairs unmatched: the waits time out and raise the status bit.
+// peers' (shapes that differ between ranks) leaves READY pairs unmatched: the waits time out and raise the status bit.
 #pragma once
 
 #include "ptx.cuh"
@@ -38,9 +41,10 @@ namespace vkb {
 constexpr int P2P_MAX_RANKS = 8;
 constexpr int P2P_MAX_CTAS = 256;                                  // grids of the fused kernels (<= SM count)
 constexpr int P2P_READY = 0;                                       // [P2P_MAX_RANKS][P2P_MAX_CTAS]
-constexpr int P2P_DONE = P2P_MAX_RANKS * P2P_MAX_CTAS;             // [P2P_MAX_RANKS][P2P_MAX_CTAS]
-constexpr int P2P_EPOCH = 2 * P2P_MAX_RANKS * P2P_MAX_CTAS;        // [P2P_MAX_CTAS]
-constexpr int P2P_FLAG_WORDS = P2P_EPOCH + P2P_MAX_CTAS;
+constexpr int P2P_DONE = P2P_MAX_RANKS * P2P_MAX_CTAS;             // [P2P_MAX_RANKS]
+constexpr int P2P_COUNT = P2P_DONE + P2P_MAX_RANKS;
+constexpr int P2P_EPOCH = P2P_COUNT + 1;
+constexpr int P2P_FLAG_WORDS = P2P_EPOCH + 1;
 constexpr size_t P2P_FLAG_BYTES = (P2P_FLAG_WORDS * 4 + 255) / 256 * 256;   // the block after the (256-aligned) data
 
 struct P2PArgs {
@@ -75,9 +79,9 @@ __device__ __forceinline__ bool p2p_wait_flag(const uint32_t* flag, uint32_t e) 
     }
 }
 
-// The number of this CTA's call (only after griddepcontrol.wait, or in a thread ordered after one that did).
+// The number of the call now running (only after griddepcontrol.wait, or in a thread ordered after one that did).
 __device__ __forceinline__ uint32_t p2p_epoch(const P2PArgs& p) {
-    return *reinterpret_cast<volatile const uint32_t*>(p.peer_flags[p.rank] + P2P_EPOCH + blockIdx.x) + 1u;
+    return *reinterpret_cast<volatile const uint32_t*>(p.peer_flags[p.rank] + P2P_EPOCH) + 1u;
 }
 
 // Step 1 (one thread per CTA, after griddepcontrol.wait).
@@ -142,15 +146,19 @@ __device__ __forceinline__ void p2p_push(const P2PArgs& p, int rows, int row_byt
 
 // Step 3 (one thread per CTA, after a barrier that follows every store of the CTA).
 __device__ __forceinline__ void p2p_finish(const P2PArgs& p) {
-    const uint32_t e = p2p_epoch(p);
-    fence_acq_rel_sys();   // this CTA's stores (local and remote) before its DONE flags
-    for (int r = 0; r < p.size; ++r)
-        if (r != p.rank) st_relaxed_sys(p.peer_flags[r] + P2P_DONE + p.rank * P2P_MAX_CTAS + blockIdx.x, e);
     uint32_t* f = p.peer_flags[p.rank];
+    const uint32_t e = p2p_epoch(p);   // read before the count: the last CTA stores the new value after every count
+    asm volatile("fence.acq_rel.gpu;" ::: "memory");   // this CTA's stores (and its epoch read) before its count
+    const uint32_t old = atomicAdd(f + P2P_COUNT, 1u);
+    if (old != gridDim.x - 1) return;
+    f[P2P_COUNT] = 0;        // every CTA of this call has counted; the next call starts from zero
+    fence_acq_rel_sys();     // acquire every CTA's stores, release them (and this CTA's) to the peers
     for (int r = 0; r < p.size; ++r)
-        if (r != p.rank && !p2p_wait_flag(f + P2P_DONE + r * P2P_MAX_CTAS + blockIdx.x, e)) break;
-    // call e is complete for this CTA (also after a timeout, so the ranks' numbering stays aligned)
-    *reinterpret_cast<volatile uint32_t*>(f + P2P_EPOCH + blockIdx.x) = e;
+        if (r != p.rank) st_relaxed_sys(p.peer_flags[r] + P2P_DONE + p.rank, e);
+    for (int r = 0; r < p.size; ++r)
+        if (r != p.rank && !p2p_wait_flag(f + P2P_DONE + r, e)) break;
+    // call e is complete here (also after a timeout, so the ranks' numbering stays aligned)
+    *reinterpret_cast<volatile uint32_t*>(f + P2P_EPOCH) = e;
 }
 
 }  // namespace vkb
