@@ -173,7 +173,9 @@ static int round_up(int v, int m) { return (v + m - 1) / m * m; }
 // next call, under PDL) share the SM.
 static bool plan_qmv(int fmt, int N, int K, int xrows, int moe_slots, int E_local, const DeviceInfo& d, QmvPlan* p) {
     const int bits = fmt_bits(fmt), unit = QMV_KS_UNIT;
-    const int ks_max = 12288 / bits;   // 1.5 KB of codes per row per stage (the 8-byte box row limit is 2 KB)
+    static const int ks_force = getenv("VKB_QMV_KSMAX") ? atoi(getenv("VKB_QMV_KSMAX")) : 0;   // tuning override
+    const int ks_max = ks_force >= unit ? ks_force : 12288 / bits;   // 1.5 KB of codes per row per stage (the
+                                                                      // 8-byte box row limit is 2 KB)
     const int nchunks = (K + ks_max - 1) / ks_max;
     const int KS = round_up((K + nchunks - 1) / nchunks, unit);
     const int cpitch = KS * bits / 8 + (fmt == VKB_FMT_Q8 ? 32 : 16);
@@ -210,7 +212,16 @@ static bool plan_qmv(int fmt, int N, int K, int xrows, int moe_slots, int E_loca
     a.wg = 1;
     for (int wg = QMV_MAXWG; wg > 1; wg /= 2)
         if (nstage >= wg * nchunks) { a.wg = wg; break; }
-    (void)moe_slots;
+    // dense calls with at most one or two row tiles per CTA: groups beyond the CTA's tiles would idle, so long rows
+    // go to fewer, larger groups (measured on B200: K = 6144 over 128 tiles, 2-bit: 4.9 us with one group, 6.5 with
+    // four)
+    if (moe_slots == 0 && K >= 2048) {
+        const int tiles = a.tilesN;
+        if (tiles <= d.sm_count && K >= 4096) a.wg = 1;
+        else if (tiles <= d.sm_count || (tiles <= 2 * d.sm_count && K >= 4096)) a.wg = a.wg < 2 ? a.wg : 2;
+    }
+    static const int wg_force = getenv("VKB_QMV_WG") ? atoi(getenv("VKB_QMV_WG")) : 0;   // tuning override
+    if (wg_force == 1 || ((wg_force == 2 || wg_force == 4) && nstage >= wg_force * nchunks)) a.wg = wg_force;
     p->smem = a.moe_off + moebytes + slack;
     return true;
 }
