@@ -39,8 +39,9 @@ def _torch_ref(codes, scales, x_bits):
     return x @ w16.T
 
 
+# (1031, 768, 200): ragged last row tile and a token tile that overruns M
 @pytest.mark.parametrize("N,K,M", [(512, 256, 16), (256, 512, 64), (384, 1024, 128), (1031, 768, 65),
-                                   (1024, 2048, 1), (640, 2560, 130), (2048, 2048, 511)])
+                                   (1024, 2048, 1), (640, 2560, 130), (2048, 2048, 511), (1031, 768, 200)])
 def test_tc_vs_torch_fp32(cuda, N, K, M):
     rng = np.random.default_rng(N + K + M)
     codes, scales = random_codes(rng, O.FMT_Q4, N, K)
@@ -85,3 +86,40 @@ def test_tc_rejects_unsupported(cuda):
     p = vkb._ptr(buf)
     assert L.vkb_gemm_q4_tc(p, p, p, p, 128, 320, 64, vkb._stream()) == vkb.EUNSUPPORTED   # K % 256 != 0
     assert L.vkb_gemm_q4_tc(p, p, p, p, 128, 256, 0, vkb._stream()) == vkb.EINVAL
+
+
+_PAIR_SCRIPT = r"""
+import sys
+import numpy as np
+sys.path[:0] = sys.argv[1:4]
+import vkb
+from oracle import oracle as O
+from gpu_util import device_weights, random_codes, uniform_x
+from test_tc_gpu import _tc, _torch_ref
+worst = 0.0
+for N, K, M in [(384, 1024, 128), (1031, 768, 200), (2048, 2048, 511), (512, 256, 16)]:
+    rng = np.random.default_rng(N + K + M)
+    codes, scales = random_codes(rng, O.FMT_Q4, N, K)
+    q, s = device_weights(O.FMT_Q4, codes, scales)
+    x = uniform_x(rng, M, K)
+    y = _tc(q, s, x, M, out_f32=True)
+    ref = _torch_ref(codes, scales, x)
+    worst = max(worst, ((y - ref).abs().max() / (ref.abs().max() + 1e-12)).item())
+print("WORST", worst, "STATUS", vkb.device_status())
+"""
+
+
+def test_tc_pair_kernel_opt_in(cuda):
+    """The CTA-pair prompt kernel (tcgen05 cta_group::2, selected by VKB_TC_CG=2) against torch fp32, in a child
+    process (the override is read once per process)."""
+    import os
+    import subprocess
+    import sys
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    env = dict(os.environ, VKB_TC_CG="2")
+    paths = [root, os.path.join(root, "volta-kernel-bakeoff_b200"), os.path.join(root, "tests")]
+    r = subprocess.run([sys.executable, "-c", _PAIR_SCRIPT] + paths, env=env, capture_output=True, text=True,
+                       timeout=300, cwd=root)
+    assert r.returncode == 0, r.stderr[-2000:]
+    line = [l for l in r.stdout.splitlines() if l.startswith("WORST")][-1].split()
+    assert float(line[1]) < 1e-5 and int(line[3]) == 0, line

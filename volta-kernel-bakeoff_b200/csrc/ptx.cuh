@@ -123,6 +123,63 @@ __device__ __forceinline__ bool wait_parity_sleep(uint64_t* bar, uint32_t parity
     }
 }
 
+// ---- clusters (pairs of CTAs) ----------------------------------------------------------------------------------
+
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+__device__ __forceinline__ uint32_t cluster_id_x() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%clusterid.x;" : "=r"(r));
+    return r;
+}
+__device__ __forceinline__ uint32_t cluster_count_x() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%nclusterid.x;" : "=r"(r));
+    return r;
+}
+// Shared::cluster address of the variable at this CTA's shared address a, in cluster CTA `rank`.
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t a, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(rank));
+    return r;
+}
+// Arrive on an mbarrier of any CTA of the cluster (address from mapa_shared), releasing at cluster scope.
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+// Every thread of every CTA of the cluster (all threads execute it).
+__device__ __forceinline__ void cluster_sync() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// wait_parity_sleep for barriers that other CTAs of the cluster arrive on (acquire at cluster scope).
+__device__ __forceinline__ bool mbar_try_wait_sleep_cl(uint32_t bar_addr, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(bar_addr), "r"(parity), "r"(100000u)
+        : "memory");
+    return ok != 0;
+}
+__device__ __forceinline__ bool wait_parity_sleep_cl(uint64_t* bar, uint32_t parity,
+                                                     unsigned err = DEV_ERR_WAIT_TIMEOUT) {
+    const uint32_t a = smem_u32(bar);
+    if (mbar_try_wait_sleep_cl(a, parity)) return true;
+    const uint64_t t0 = globaltimer();
+    for (;;) {
+        if (mbar_try_wait_sleep_cl(a, parity)) return true;
+        if (globaltimer() - t0 > VKB_WAIT_NS) {
+            raise_status(err);
+            return false;
+        }
+    }
+}
+
 // ---- TMA ------------------------------------------------------------------------------------------------------
 
 // 2-D tiled tensor load (no multicast) into this CTA's shared memory, completing bytes on bar.
@@ -130,6 +187,17 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, i
     asm volatile(
         "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];"
         ::"r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y)
+        : "memory");
+}
+
+// 3-D tiled tensor load of a CTA pair (cta_group::2, no multicast): the box lands in this CTA's shared memory and its
+// bytes complete on the mbarrier at bar_cluster (a shared::cluster address, e.g. the pair leader's barrier).
+__device__ __forceinline__ void tma_load_3d_cg2(void* dst, const CUtensorMap* map, int x, int y, int z,
+                                                uint32_t bar_cluster) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, "
+        "%5}], [%2];"
+        ::"r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(bar_cluster), "r"(x), "r"(y), "r"(z)
         : "memory");
 }
 

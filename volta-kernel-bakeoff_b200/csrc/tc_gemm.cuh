@@ -74,14 +74,28 @@ struct TcArgs {
 
 // ---- tcgen05 wrappers ----------------------------------------------------------------------------------------------
 
+// TMEM allocation of one CTA (CG = 1) or of a CTA pair (CG = 2: the same warp of both CTAs issues it, with the same
+// shared-memory slot; each CTA gets the columns in its own TMEM at the same address).
+template <int CG>
 __device__ __forceinline__ void tmem_alloc(uint32_t* dst_smem, uint32_t ncols) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst_smem)),
-                 "r"(ncols)
-                 : "memory");
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    if constexpr (CG == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst_smem)),
+                     "r"(ncols)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    } else {
+        asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst_smem)),
+                     "r"(ncols)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+    }
 }
+template <int CG>
 __device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+    if constexpr (CG == 1)
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+    else
+        asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
 }
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
@@ -100,9 +114,9 @@ __device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t saddr) {
     return d;
 }
 
-// kind::f16 instruction descriptor: f16 A and B, f32 D, both K-major, M = 128, N = n.
-__host__ __device__ constexpr uint32_t umma_idesc_f16(int n) {
-    return (1u << 4) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(TC_BM >> 4) << 24);
+// kind::f16 instruction descriptor: f16 A and B, f32 D, both K-major, M = m (128, or 256 for a CTA pair), N = n.
+__host__ __device__ constexpr uint32_t umma_idesc_f16(int n, int m = TC_BM) {
+    return (1u << 4) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
 }
 
 __device__ __forceinline__ void umma_f16(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t idesc, uint32_t accum) {
@@ -124,6 +138,27 @@ __device__ __forceinline__ void umma_f16_ts(uint32_t tmem_d, uint32_t tmem_a, ui
         "setp.ne.b32 p, %4, 0;\n\t"
         "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, {%5, %5, %5, %5}, p;\n\t}"
         ::"r"(tmem_d), "r"(tmem_a), "l"(db), "r"(idesc), "r"(accum), "r"(z)
+        : "memory");
+}
+
+// The same issued by the leader of a CTA pair (cta_group::2, M = 256): A is 128 rows of each CTA's TMEM at tmem_a, B
+// is N/2 rows of each CTA's shared memory at the descriptor's address, D is each CTA's 128 rows x N in its own TMEM.
+__device__ __forceinline__ void umma_f16_ts_cg2(uint32_t tmem_d, uint32_t tmem_a, uint64_t db, uint32_t idesc,
+                                                uint32_t accum) {
+    const uint32_t z = 0;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], [%1], %2, %3, {%5, %5, %5, %5, %5, %5, %5, %5}, p;\n\t}"
+        ::"r"(tmem_d), "r"(tmem_a), "l"(db), "r"(idesc), "r"(accum), "r"(z)
+        : "memory");
+}
+
+// Commit of a pair's MMAs: one arrive on the mbarrier at this shared offset in both CTAs of the pair.
+__device__ __forceinline__ void umma_commit_pair(uint64_t* bar) {
+    asm volatile(
+        "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;"
+        ::"r"(smem_u32(bar)), "h"((uint16_t)3)
         : "memory");
 }
 
@@ -226,10 +261,17 @@ __device__ __noinline__ void tc_push_tile(const TcArgs& a, int row0, int tok0, i
              nth);
 }
 
-template <typename OutT, int PK, bool P2P>
+// CG = 2: a cluster of two CTAs (a pair) shares each 256-row tile. Each CTA dequantises its own 128 weight rows into
+// its own TMEM and loads half of the tile's tokens into its shared memory; the pair leader (cluster rank 0) issues
+// tcgen05.mma.cta_group::2 (M = 256), which reads A from both TMEMs and B from both shared memories, so each SM
+// streams half of the activations it would stream alone: the shared-memory traffic per MMA halves. The leader's
+// barriers count both CTAs (the peer's dequantising and epilogue warps arrive remotely, the peer's activation loads
+// complete on the leader's barrier); the leader's commits arrive on both CTAs' barriers. No TMA multicast.
+template <typename OutT, int PK, bool P2P, int CG>
 __global__ void __launch_bounds__(TC_THREADS, 1)
 tc_q4_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap ts,
              const __grid_constant__ CUtensorMap tx, const __grid_constant__ TcArgs a) {
+    static_assert(CG == 1 || (CG == 2 && !P2P), "peer stores use the one-CTA kernel");
     constexpr int PPITCH = tc_ppitch(PK), PCHUNK = tc_pchunk(PK), SCOFF = TC_BM * PPITCH;
     extern __shared__ uint8_t smem_raw[];
     const uint32_t pad = (1024u - (smem_u32(smem_raw) & 1023u)) & 1023u;
@@ -247,11 +289,31 @@ tc_q4_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUt
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int nk = a.nk, nch = nk / PK, nxs = nk / a.xk, nslots = nk / TC_SLOT;
-    // tiles of this CTA: t = blockIdx.x + i * gridDim.x
-    const int ntl = blockIdx.x < (unsigned)a.tiles ? (a.tiles - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
-    auto tile_of = [&](int i) { return (int)blockIdx.x + i * (int)gridDim.x; };
-    auto row0_of = [&](int t) { return (t % a.tiles_n) * TC_BM; };
+    // the CTA's place in its pair (CG = 2) and the pairs of the grid; a "unit" is a CTA (CG = 1) or a pair
+    const uint32_t crank = CG == 2 ? cluster_ctarank() : 0u;
+    const bool leader = crank == 0;
+    const int units = CG == 2 ? (int)cluster_count_x() : (int)gridDim.x;
+    const int unit = CG == 2 ? (int)cluster_id_x() : (int)blockIdx.x;
+    // tiles of this unit: t = unit + i * units (a tile: 128 CG weight rows x NT tokens; this CTA's rows start at
+    // row0_of(t), its tokens for the B operand at tok0_of(t) + crank NT / CG)
+    const int ntl = unit < a.tiles ? (a.tiles - 1 - unit) / units + 1 : 0;
+    auto tile_of = [&](int i) { return unit + i * units; };
+    auto row0_of = [&](int t) { return (t % a.tiles_n) * (TC_BM * CG) + TC_BM * (int)crank; };
     auto tok0_of = [&](int t) { return (t / a.tiles_n) * a.NT; };
+    // barrier helpers: waits that a peer CTA may have released acquire at cluster scope; arrivals that the MMA
+    // issuer waits for go to the leader's barrier; commits of a pair's MMAs arrive in both CTAs
+    auto wait_b = [&](uint64_t* bar, uint32_t par, unsigned err = DEV_ERR_WAIT_TIMEOUT) {
+        if constexpr (CG == 2) return wait_parity_sleep_cl(bar, par, err);
+        else return wait_parity_sleep(bar, par, err);
+    };
+    auto arrive_leader = [&](uint64_t* bar) {
+        if constexpr (CG == 2) mbar_arrive_cluster(mapa_shared(smem_u32(bar), 0));
+        else mbar_arrive(bar);
+    };
+    auto commit = [&](uint64_t* bar) {
+        if constexpr (CG == 2) umma_commit_pair(bar);
+        else umma_commit(bar);
+    };
     const int total_ch = ntl * nch;
 
     auto issue_chunk = [&](int g, int b) {   // chunk g of this CTA's stream into ring slot b
@@ -273,12 +335,12 @@ tc_q4_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUt
             mbar_init(&xempty[i], 1);
         }
         for (int i = 0; i < a.na; ++i) {
-            mbar_init(&afull[i], TC_NDQ);
+            mbar_init(&afull[i], TC_NDQ * CG);     // the leader's counts both CTAs' dequantising warps
             mbar_init(&aempty[i], 1);
         }
         for (int i = 0; i < a.nacc; ++i) {
             mbar_init(&accfull[i], 1);
-            mbar_init(&accempty[i], TC_NEPI);
+            mbar_init(&accempty[i], TC_NEPI * CG);   // the leader's counts both CTAs' epilogue warps
         }
         fence_mbar_init();
         // the first chunks start now, before the TMEM allocation and the block-wide barrier
@@ -286,9 +348,10 @@ tc_q4_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUt
         prefetch_tmap(&ts);
         for (int g = 0; g < min(total_ch, a.np); ++g) issue_chunk(g, g);
     }
-    if (warp == 1) tmem_alloc(tmem_slot, (uint32_t)a.tmem_cols);
+    if (warp == 1) tmem_alloc<CG>(tmem_slot, (uint32_t)a.tmem_cols);
     tc_fence_before();
-    __syncthreads();
+    if constexpr (CG == 2) cluster_sync();   // both CTAs' barriers exist before any remote arrive or pair load
+    else __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
 
@@ -315,36 +378,45 @@ tc_q4_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUt
         int last = -1;
         for (int gs = par; gs < total_xs; gs += 2) {
             const int b = gs % a.nx, rnd = gs / a.nx;
-            if (rnd > 0) ok = __all_sync(0xffffffffu, wait_parity_sleep(&xempty[b], (rnd - 1) & 1));
+            if (rnd > 0) ok = __all_sync(0xffffffffu, wait_b(&xempty[b], (rnd - 1) & 1));
             if (!ok) break;
             if (elect_one()) {
                 const int t = tile_of(gs / nxs), xs = gs % nxs;
-                mbar_arrive_expect_tx(&xfull[b], (uint32_t)a.x_stage);
-                tma_load_3d(sm + a.x_off + b * a.x_stage, &tx, 0, tok0_of(t), xs * a.xk, &xfull[b]);
+                if constexpr (CG == 1) {
+                    mbar_arrive_expect_tx(&xfull[b], (uint32_t)a.x_stage);
+                    tma_load_3d(sm + a.x_off + b * a.x_stage, &tx, 0, tok0_of(t), xs * a.xk, &xfull[b]);
+                } else {   // this CTA's half of the tokens; both halves complete on the leader's barrier
+                    if (leader) mbar_arrive_expect_tx(&xfull[b], (uint32_t)(2 * a.x_stage));
+                    tma_load_3d_cg2(sm + a.x_off + b * a.x_stage, &tx, 0, tok0_of(t) + (int)crank * (a.NT / 2),
+                                    xs * a.xk, mapa_shared(smem_u32(&xfull[b]), 0));
+                }
             }
             __syncwarp();
             last = gs;
         }
-        for (int gs = last; gs >= 0 && gs > last - a.nx; gs -= 2)
-            if (!wait_parity_sleep(&xfull[gs % a.nx], (gs / a.nx) & 1, DEV_ERR_DRAIN_TIMEOUT)) break;
-    } else if (warp == 1) {
-        // ===================== MMA issuer =====================
+        // drain: the loads still in flight land before exit (the leader's barrier counts the peer's loads too, and
+        // the pair leaves only together)
+        if (leader)
+            for (int gs = last; gs >= 0 && gs > last - a.nx; gs -= 2)
+                if (!wait_b(&xfull[gs % a.nx], (gs / a.nx) & 1, DEV_ERR_DRAIN_TIMEOUT)) break;
+    } else if (warp == 1 && leader) {
+        // ===================== MMA issuer (the pair leader's, CG = 2) =====================
         // per slot: wait for its A (TMEM) and the X stages its 4 K steps read, then 16 UMMAs (4 per K step). When the
         // X ring holds at least two slots of K steps all of a slot's X waits come first and the 16 UMMAs issue back
         // to back; otherwise (large token tiles, shallow X ring) the waits interleave with the K steps so that each
         // X stage is released as soon as its own MMAs complete.
-        const uint32_t idesc = umma_idesc_f16(a.NT);
-        const uint32_t xtile = (uint32_t)a.NT * 128;
+        const uint32_t idesc = umma_idesc_f16(a.NT, TC_BM * CG);
+        const uint32_t xtile = (uint32_t)(a.NT / CG) * 128;   // one K step of this CTA's tokens in a stage
         const bool hoist = a.nx * a.xk >= 2 * TC_SLOT;
         int ab = 0, arnd = 0, xb = 0, xrnd = 0, xj = 0;
         for (int i = 0; i < ntl && ok; ++i) {
             const int acc = i % a.nacc;
-            if (i >= a.nacc) ok = __all_sync(0xffffffffu, wait_parity_sleep(&accempty[acc], ((i / a.nacc) - 1) & 1));
+            if (i >= a.nacc) ok = __all_sync(0xffffffffu, wait_b(&accempty[acc], ((i / a.nacc) - 1) & 1));
             if (!ok) break;
             tc_fence_after();
             const uint32_t td = tmem + (uint32_t)(acc * 128);
             for (int sl = 0; sl < nslots && ok; ++sl) {
-                ok = __all_sync(0xffffffffu, wait_parity_sleep(&afull[ab], arnd & 1));
+                ok = __all_sync(0xffffffffu, wait_b(&afull[ab], arnd & 1));
                 if (!ok) break;
                 tc_fence_after();
                 const uint32_t ta = tmem + (uint32_t)(a.a_col0 + ab * TC_SLOT * TC_ACOLS);
@@ -353,7 +425,7 @@ tc_q4_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUt
                     int rel[TC_SLOT];   // X stage to release after K step j (-1: none)
 #pragma unroll
                     for (int j = 0; j < TC_SLOT; ++j) {
-                        if (xj == 0 && ok) ok = __all_sync(0xffffffffu, wait_parity_sleep(&xfull[xb], xrnd & 1));
+                        if (xj == 0 && ok) ok = __all_sync(0xffffffffu, wait_b(&xfull[xb], xrnd & 1));
                         sb[j] = smem_u32(sm + a.x_off + xb * a.x_stage) + xj * xtile;
                         rel[j] = xj + 1 == a.xk ? xb : -1;
                         if (++xj == a.xk) {
@@ -367,19 +439,24 @@ tc_q4_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUt
                         for (int j = 0; j < TC_SLOT; ++j) {
                             const int it = sl * TC_SLOT + j;
 #pragma unroll
-                            for (int kk = 0; kk < TC_BK / 16; ++kk)   // 16 k: 8 TMEM columns of A, 32 bytes of B row
-                                umma_f16_ts(td, ta + (uint32_t)(j * TC_ACOLS + 8 * kk),
-                                            umma_desc_sw128(sb[j] + 32 * kk), idesc, (it | kk) != 0);
-                            if (rel[j] >= 0) umma_commit(&xempty[rel[j]]);   // free the stage after these MMAs
+                            for (int kk = 0; kk < TC_BK / 16; ++kk) {   // 16 k: 8 TMEM columns of A, 32 B of a B row
+                                if constexpr (CG == 2)
+                                    umma_f16_ts_cg2(td, ta + (uint32_t)(j * TC_ACOLS + 8 * kk),
+                                                    umma_desc_sw128(sb[j] + 32 * kk), idesc, (it | kk) != 0);
+                                else
+                                    umma_f16_ts(td, ta + (uint32_t)(j * TC_ACOLS + 8 * kk),
+                                                umma_desc_sw128(sb[j] + 32 * kk), idesc, (it | kk) != 0);
+                            }
+                            if (rel[j] >= 0) commit(&xempty[rel[j]]);   // free the stage after these MMAs
                         }
-                        umma_commit(&aempty[ab]);
+                        commit(&aempty[ab]);
                     }
                     __syncwarp();
                 } else {
 #pragma unroll
                     for (int j = 0; j < TC_SLOT; ++j) {
                         if (xj == 0) {
-                            ok = __all_sync(0xffffffffu, wait_parity_sleep(&xfull[xb], xrnd & 1));
+                            ok = __all_sync(0xffffffffu, wait_b(&xfull[xb], xrnd & 1));
                             if (!ok) break;
                         }
                         const int it = sl * TC_SLOT + j;
@@ -387,11 +464,16 @@ tc_q4_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUt
                         const bool last_x = xj + 1 == a.xk;
                         if (elect_one()) {
 #pragma unroll
-                            for (int kk = 0; kk < TC_BK / 16; ++kk)
-                                umma_f16_ts(td, ta + (uint32_t)(j * TC_ACOLS + 8 * kk), umma_desc_sw128(sb + 32 * kk),
-                                            idesc, (it | kk) != 0);
-                            if (last_x) umma_commit(&xempty[xb]);
-                            if (j == TC_SLOT - 1) umma_commit(&aempty[ab]);
+                            for (int kk = 0; kk < TC_BK / 16; ++kk) {
+                                if constexpr (CG == 2)
+                                    umma_f16_ts_cg2(td, ta + (uint32_t)(j * TC_ACOLS + 8 * kk),
+                                                    umma_desc_sw128(sb + 32 * kk), idesc, (it | kk) != 0);
+                                else
+                                    umma_f16_ts(td, ta + (uint32_t)(j * TC_ACOLS + 8 * kk),
+                                                umma_desc_sw128(sb + 32 * kk), idesc, (it | kk) != 0);
+                            }
+                            if (last_x) commit(&xempty[xb]);
+                            if (j == TC_SLOT - 1) commit(&aempty[ab]);
                         }
                         __syncwarp();
                         if (last_x) {
@@ -406,10 +488,10 @@ tc_q4_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUt
                 if (++ab == a.na) { ab = 0; ++arnd; }
             }
             if (!ok) break;
-            if (elect_one()) umma_commit(&accfull[acc]);   // the tile's MMAs are done: its accumulator is final
+            if (elect_one()) commit(&accfull[acc]);   // the tile's MMAs are done: its accumulator is final
             __syncwarp();
         }
-    } else if (warp < TC_WEPI0) {
+    } else if (warp >= TC_WDQ0 && warp < TC_WEPI0) {
         // ===================== dequantise (two groups, half a slot each) =====================
         const int dw = warp - TC_WDQ0;            // 0..7
         const int grp = dw >> 2;                  // K steps 2 grp, 2 grp + 1 of every slot
@@ -460,12 +542,12 @@ tc_q4_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUt
                 dequant8_to(w3.y, b_hi, v + 52);
                 dequant8_to(w3.z, b_hi, v + 56);
                 dequant8_to(w3.w, b_hi, v + 60);
-                if (sl >= a.na && !wait_parity_sleep(&aempty[ab], ((sl / a.na) - 1) & 1)) { ok = false; break; }
+                if (sl >= a.na && !wait_b(&aempty[ab], ((sl / a.na) - 1) & 1)) { ok = false; break; }
                 tc_fence_after();                                   // the slot's previous MMAs are done
                 tmem_st64(tlane + (uint32_t)(ab * TC_SLOT * TC_ACOLS), v);
                 tc_fence_before();
                 __syncwarp();
-                if (lane == 0) mbar_arrive(&afull[ab]);
+                if (lane == 0) arrive_leader(&afull[ab]);
             }
         }
     }
@@ -495,7 +577,7 @@ tc_q4_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUt
             const int acc = i % a.nacc, t = tile_of(i), row0 = row0_of(t), tok0 = tok0_of(t);
             const bool last = i == ntl - 1;
             const int parts = last ? 3 : 1;
-            if (ok) ok = __all_sync(0xffffffffu, wait_parity_sleep(&accfull[acc], (i / a.nacc) & 1));
+            if (ok) ok = __all_sync(0xffffffffu, wait_b(&accfull[acc], (i / a.nacc) & 1));
             if (ok) {
                 tc_fence_after();
                 const uint32_t tq_addr = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(acc * 128);
@@ -525,7 +607,7 @@ tc_q4_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUt
                 if (epi) {
                     tc_fence_before();
                     __syncwarp();
-                    if (lane == 0) mbar_arrive(&accempty[acc]);
+                    if (lane == 0) arrive_leader(&accempty[acc]);
                 }
             }
             if constexpr (P2P) {   // the tile is complete in this rank's copy: its participants push it to every peer
@@ -536,13 +618,15 @@ tc_q4_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUt
         }
     }
     // teardown: every MMA has completed (the epilogue waited on each accumulator) before TMEM is released
-    if (warp == 1 && !ok && ntl > 0) wait_parity_sleep(&accfull[(ntl - 1) % a.nacc], ((ntl - 1) / a.nacc) & 1,
-                                                       DEV_ERR_DRAIN_TIMEOUT);
+    if (warp == 1 && !ok && ntl > 0) wait_b(&accfull[(ntl - 1) % a.nacc], ((ntl - 1) / a.nacc) & 1,
+                                            DEV_ERR_DRAIN_TIMEOUT);
     tc_fence_before();
-    __syncthreads();
+    // a pair leaves together: no remote arrive, pair load or MMA touches a CTA that has released its TMEM or exited
+    if constexpr (CG == 2) cluster_sync();
+    else __syncthreads();
     if (warp == 1) {
         tc_fence_after();
-        tmem_dealloc(tmem, (uint32_t)a.tmem_cols);
+        tmem_dealloc<CG>(tmem, (uint32_t)a.tmem_cols);
     }
     // every store of this CTA precedes the barrier above; thread 0's system-scope fence in p2p_finish releases them
     // all (cumulativity), so no per-thread fence is needed

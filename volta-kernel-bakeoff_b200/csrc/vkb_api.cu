@@ -371,6 +371,7 @@ int qmv_dispatch(int fmt, const void* q, const void* s, const void* x, void* y, 
 struct TcPlan {
     TcArgs a;
     int pk;     // K steps per packed chunk (kernel template argument)
+    int cg;     // CTAs per tile: 1, or 2 (a cluster pair on 256-row tiles, tcgen05 cta_group::2)
     int smem;
     dim3 grid;
 };
@@ -379,10 +380,11 @@ struct TcPlan {
 // CTA; a K step costs 4 UMMAs of (32 + 0.41 NT) cycles (measured, A in TMEM) or the dequantisation floor, and a
 // single-buffered accumulator (NT > 128) exposes the epilogue once per extra tile. Ring depths: X stages of up to
 // 32 KB (an even count: two producers), P chunks of 8 K steps when they fit (else 4), both deepened while shared
-// memory lasts.
-static bool plan_tc(int N, int K, int M, int out_bytes, const DeviceInfo& d, TcPlan* p) {
+// memory lasts. With cg = 2 the units are CTA pairs (at most `units_max` co-resident), a tile has 256 rows and each
+// CTA's X stages hold half of the tile's tokens.
+static bool plan_tc(int N, int K, int M, int out_bytes, const DeviceInfo& d, TcPlan* p, int cg, int units_max) {
     TcArgs& a = p->a;
-    const int tiles_n = (N + TC_BM - 1) / TC_BM;
+    const int tiles_n = (N + TC_BM * cg - 1) / (TC_BM * cg);
     const int nk = K / TC_BK;
     int NT = 0;
     double best = 1e300;
@@ -391,7 +393,7 @@ static bool plan_tc(int N, int K, int M, int out_bytes, const DeviceInfo& d, TcP
     for (int nt = nt_max; nt >= 32; nt -= 32) {
         if (nt_force > 0 && nt != nt_force && nt_force <= nt_max) continue;
         const long tiles = (long)tiles_n * ((M + nt - 1) / nt);
-        const long grid = tiles < d.sm_count ? tiles : d.sm_count;
+        const long grid = tiles < units_max ? tiles : units_max;
         const long per_cta = (tiles + grid - 1) / grid;
         const double umma = 4.0 * (32.0 + 0.41 * nt);
         const double step = umma > 180.0 ? umma : 180.0;
@@ -407,46 +409,74 @@ static bool plan_tc(int N, int K, int M, int out_bytes, const DeviceInfo& d, TcP
     a.a_col0 = 256;
     a.tmem_cols = 512;
     int xk = 8;
-    while (xk > 1 && (xk * NT * 128 > 32768 || nk % xk != 0)) xk /= 2;
+    while (xk > 1 && (xk * (NT / cg) * 128 > 32768 || nk % xk != 0)) xk /= 2;
     (void)out_bytes;
     for (int pk : {8, 4}) {
         if (nk % pk != 0) continue;
         const int pchunk = tc_pchunk(pk);
         int nx = 4, np = 2;   // four X stages first: the activations are the fast-consumed stream
         auto bars_bytes = [&]() { return 8 * (2 * np + 2 * nx + 2 * a.na + 2 * a.nacc) + 16; };
-        auto total = [&]() { return nx * xk * NT * 128 + np * pchunk + bars_bytes() + 1024; };
+        auto total = [&]() { return nx * xk * (NT / cg) * 128 + np * pchunk + bars_bytes() + 1024; };
         if (total() > d.smem_optin) nx = 2;
         if (total() > d.smem_optin) continue;
         for (bool grew = true; grew;) {
             grew = false;
             if (np < 6) { ++np; if (total() <= d.smem_optin) grew = true; else --np; }
-            if (nx < 6) { nx += 2; if (total() <= d.smem_optin) grew = true; else nx -= 2; }
+            if (nx < 4 + 2 * cg) { nx += 2; if (total() <= d.smem_optin) grew = true; else nx -= 2; }
         }
         p->pk = pk;
         a.xk = xk;
-        a.x_stage = xk * NT * 128;
+        a.x_stage = xk * (NT / cg) * 128;
         a.nx = nx;
         a.np = np;
         a.x_off = 0;
         a.p_off = nx * a.x_stage;
         a.bar_off = a.p_off + np * pchunk;
         p->smem = total();
-        p->grid = dim3((unsigned)(a.tiles < d.sm_count ? a.tiles : d.sm_count));
+        p->cg = cg;
+        p->grid = dim3((unsigned)((a.tiles < units_max ? a.tiles : units_max) * cg));
         return true;
     }
     return false;
 }
 
 // Opt one prompt-GEMM kernel variant into the device's shared memory, once per device.
-template <typename OutT, int PK, bool P2P>
+template <typename OutT, int PK, bool P2P, int CG>
 static int tc_attr(int dev, int smem_optin) {
     static std::once_flag once[kMaxDevices];
     static cudaError_t err[kMaxDevices];
     std::call_once(once[dev], [&] {
-        err[dev] = cudaFuncSetAttribute(tc_q4_kernel<OutT, PK, P2P>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        err[dev] = cudaFuncSetAttribute(tc_q4_kernel<OutT, PK, P2P, CG>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                         smem_optin);
     });
     return err[dev] == cudaSuccess ? 0 : -(int)err[dev];
+}
+
+// Co-resident CTA pairs of the pair kernel at full shared memory (clusters are placed inside GPCs, so this can be
+// less than half the SM count), once per device; 0 if the query fails.
+template <typename OutT>
+static int tc_max_pairs(int dev, int smem) {
+    static std::once_flag once[kMaxDevices];
+    static int pairs[kMaxDevices];
+    std::call_once(once[dev], [&] {
+        pairs[dev] = 0;
+        if (tc_attr<OutT, 8, false, 2>(dev, smem) != 0) return;
+        cudaLaunchConfig_t cfg{};
+        cfg.gridDim = dim3(2 * 512);
+        cfg.blockDim = dim3(TC_THREADS);
+        cfg.dynamicSmemBytes = (size_t)smem;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = 2;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        int n = 0;
+        if (cudaOccupancyMaxActiveClusters(&n, tc_q4_kernel<OutT, 8, false, 2>, &cfg) == cudaSuccess) pairs[dev] = n;
+        else cudaGetLastError();
+    });
+    return pairs[dev];
 }
 
 template <typename OutT>
@@ -460,8 +490,19 @@ static int tc_entry(const void* q, const void* s, const void* x, void* y, int N,
     if (int r = current_device(&dev)) return r;
     const DeviceInfo& d = device_info(dev);
     if (d.cc_major < 10) return VKB_EUNSUPPORTED;
+    // One CTA per tile. The CTA-pair kernel (tcgen05 cta_group::2, 256-row tiles, each SM streaming half of the
+    // activations) is correct but measured slower on B200 at every shape of the sweep (12288x2560 M=512: 38.8 vs
+    // 34.6 us; 8192x2048 M=64: 13.8 vs 10.6 us): VKB_TC_CG=2 selects it for experiments.
+    static const int cg_force = getenv("VKB_TC_CG") ? atoi(getenv("VKB_TC_CG")) : 0;   // tuning override
+    int cg = cg_force == 2 && N >= 2 * TC_BM ? 2 : 1;
+    if (out && out->p2p) cg = 1;
+    int units_max = d.sm_count;
+    if (cg == 2) {
+        units_max = tc_max_pairs<OutT>(dev, d.smem_optin);
+        if (units_max < 1) cg = 1, units_max = d.sm_count;
+    }
     TcPlan p{};
-    if (!plan_tc(N, K, M, (int)sizeof(OutT), d, &p)) return VKB_EUNSUPPORTED;
+    if (!plan_tc(N, K, M, (int)sizeof(OutT), d, &p, cg, units_max)) return VKB_EUNSUPPORTED;
     p.a.y = y;
     p.a.ldy = out ? out->ldy : N;
     p.a.ycol0 = out ? out->col0 : 0;
@@ -475,18 +516,24 @@ static int tc_entry(const void* q, const void* s, const void* x, void* y, int N,
     r = get_tmap_2d(&ts, s, (uint64_t)N, (uint64_t)K / 16, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, TC_SPITCH / 2, TC_BM,
                     CU_TENSOR_MAP_SWIZZLE_NONE);
     if (r) return r;
-    r = get_tmap_x3d(&tx, x, M, K, p.a.NT, p.a.xk);
+    r = get_tmap_x3d(&tx, x, M, K, p.a.NT / p.cg, p.a.xk);   // a CTA's share of a tile's tokens
     if (r) return r;
     void (*kern)(CUtensorMap, CUtensorMap, CUtensorMap, TcArgs) = nullptr;
     int ra = 0;
-    if (!p.a.p2p) {
-        kern = p.pk == 8 ? tc_q4_kernel<OutT, 8, false> : tc_q4_kernel<OutT, 4, false>;
-        ra = p.pk == 8 ? tc_attr<OutT, 8, false>(dev, d.smem_optin) : tc_attr<OutT, 4, false>(dev, d.smem_optin);
-    } else if constexpr (std::is_same<OutT, __half>::value) {   // peer stores: fp16 outputs only
-        kern = p.pk == 8 ? tc_q4_kernel<OutT, 8, true> : tc_q4_kernel<OutT, 4, true>;
-        ra = p.pk == 8 ? tc_attr<OutT, 8, true>(dev, d.smem_optin) : tc_attr<OutT, 4, true>(dev, d.smem_optin);
+    if (p.a.p2p) {
+        if constexpr (std::is_same<OutT, __half>::value) {   // peer stores: fp16 outputs, one CTA per tile
+            kern = p.pk == 8 ? tc_q4_kernel<OutT, 8, true, 1> : tc_q4_kernel<OutT, 4, true, 1>;
+            ra = p.pk == 8 ? tc_attr<OutT, 8, true, 1>(dev, d.smem_optin)
+                           : tc_attr<OutT, 4, true, 1>(dev, d.smem_optin);
+        } else {
+            return VKB_EUNSUPPORTED;
+        }
+    } else if (p.cg == 2) {
+        kern = p.pk == 8 ? tc_q4_kernel<OutT, 8, false, 2> : tc_q4_kernel<OutT, 4, false, 2>;
+        ra = p.pk == 8 ? tc_attr<OutT, 8, false, 2>(dev, d.smem_optin) : tc_attr<OutT, 4, false, 2>(dev, d.smem_optin);
     } else {
-        return VKB_EUNSUPPORTED;
+        kern = p.pk == 8 ? tc_q4_kernel<OutT, 8, false, 1> : tc_q4_kernel<OutT, 4, false, 1>;
+        ra = p.pk == 8 ? tc_attr<OutT, 8, false, 1>(dev, d.smem_optin) : tc_attr<OutT, 4, false, 1>(dev, d.smem_optin);
     }
     if (ra) return ra;
     cudaLaunchConfig_t cfg{};
@@ -494,11 +541,22 @@ static int tc_entry(const void* q, const void* s, const void* x, void* y, int N,
     cfg.blockDim = dim3(TC_THREADS);
     cfg.dynamicSmemBytes = p.smem;
     cfg.stream = st;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchAttribute attr[2];
+    int na = 0;
+    if (pdl_enabled() && pdl_stream_ok(st)) {
+        attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[na].val.programmaticStreamSerializationAllowed = 1;
+        ++na;
+    }
+    if (p.cg == 2) {   // clusters of two CTAs along x: blocks 2c and 2c + 1 form pair c
+        attr[na].id = cudaLaunchAttributeClusterDimension;
+        attr[na].val.clusterDim.x = 2;
+        attr[na].val.clusterDim.y = 1;
+        attr[na].val.clusterDim.z = 1;
+        ++na;
+    }
     cfg.attrs = attr;
-    cfg.numAttrs = pdl_enabled() && pdl_stream_ok(st) ? 1 : 0;
+    cfg.numAttrs = na;
     const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, tq, ts, tx, p.a);
     return e == cudaSuccess ? 0 : -(int)e;
 }

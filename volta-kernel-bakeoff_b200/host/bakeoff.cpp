@@ -242,7 +242,7 @@ static void run_sweep() {
             sets.push_back(std::move(st));
         }
         const Weights w4 = make_weights(VKB_FMT_Q4, sh.N, sh.K, rng);
-        const int cf = want("cublas") ? copies_for(NK * 2) : 0;
+        const int cf = (want("cublas_fp16") || want("cublas_bf16")) ? copies_for(NK * 2) : 0;
         std::vector<void*> df, db;
         if (cf) {
             const auto wf = dequant(w4, false), wb = dequant(w4, true);
