@@ -85,3 +85,15 @@ def test_quantizer_rule():
     for fmt, lo, hi in ((O.FMT_Q8, -127, 127), (O.FMT_Q2, -2, 1)):
         c, _ = O.quantize(fmt, w)
         assert c.min() >= lo and c.max() <= hi
+
+
+def test_swiglu_ref_and_glu_error():
+    """silu(g) * u over a stacked product (src/stage5_gap8.cuh:232-238) and the reference's relative check."""
+    ys = np.array([[0.0, 1.0, 2.0, 3.0], [-2.0, 0.5, 4.0, -1.0]])
+    want = np.array([[0.0, 3.0 / (1.0 + np.exp(-1.0))],
+                     [-2.0 / (1.0 + np.exp(2.0)) * 4.0, 0.5 / (1.0 + np.exp(-0.5)) * -1.0]])
+    assert np.allclose(O.swiglu_ref(ys, 2), want, rtol=1e-15, atol=0)
+    assert O.glu_error(want, ys, 2) < 1e-12
+    bad = want.copy()
+    bad[1, 1] *= 1.001
+    assert O.glu_error(bad, ys, 2) > 5e-4

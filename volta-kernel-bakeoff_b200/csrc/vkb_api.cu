@@ -164,6 +164,7 @@ struct QmvPlan {
     QmvArgs a;
     int smem;
     int grid;
+    bool paired;   // fits the two-CTAs-per-SM budget (the next call's weight prefetch can share the SM)
 };
 
 static int round_up(int v, int m) { return (v + m - 1) / m * m; }
@@ -171,7 +172,10 @@ static int round_up(int v, int m) { return (v + m - 1) / m * m; }
 // Stage: 16 rows x KS values, up to 1.5 KB of codes per row (one TMA box each for codes and scales, rows padded so
 // the fragment reads are conflict free); ring as deep as fits, preferring a footprint that lets a second CTA (the
 // next call, under PDL) share the SM.
-static bool plan_qmv(int fmt, int N, int K, int xrows, int moe_slots, int E_local, const DeviceInfo& d, QmvPlan* p) {
+// xb: bytes per staged activation (2, or 4 for fp32 activations); glu: gate/up tiles (two stage streams per tile,
+// two reduction regions).
+static bool plan_qmv(int fmt, int N, int K, int xrows, int moe_slots, int E_local, const DeviceInfo& d, QmvPlan* p,
+                     int xb = 2, bool glu = false) {
     const int bits = fmt_bits(fmt), unit = QMV_KS_UNIT;
     static const int ks_force = getenv("VKB_QMV_KSMAX") ? atoi(getenv("VKB_QMV_KSMAX")) : 0;   // tuning override
     const int ks_max = ks_force >= unit ? ks_force : 12288 / bits;   // 1.5 KB of codes per row per stage (the
@@ -181,10 +185,10 @@ static bool plan_qmv(int fmt, int N, int K, int xrows, int moe_slots, int E_loca
     const int cpitch = KS * bits / 8 + (fmt == VKB_FMT_Q8 ? 32 : 16);
     const int spitch = KS / 16 + ((KS / 256) % 2 == 0 ? 16 : 32);   // pitch / 4 = 4 x odd: conflict-free rows
     const int stage_bytes = round_up(QMV_ROWS * (cpitch + spitch), 128);
-    const int xpitch = round_up(K * 2, 128) + 64;
+    const int xpitch = round_up(K * xb, 128) + 64;
     const int xbufs = moe_slots > 0 ? 2 : 1;
     const int xbytes = round_up(xbufs * xrows * xpitch, 16);
-    const int redbytes = 2 * QMV_NW * 32 * 16;
+    const int redbytes = 2 * QMV_NW * 32 * 16 * (glu ? 2 : 1);
     const int moebytes = moe_slots > 0 ? round_up(4 * (3 * E_local + 2 + 2 * moe_slots), 16) : 0;
     const int slack = 1024;
     auto fixed_for = [&](int nstage) { return 8 * qmv_nbars(nstage) + xbytes + redbytes + moebytes + slack; };
@@ -198,6 +202,7 @@ static bool plan_qmv(int fmt, int N, int K, int xrows, int moe_slots, int E_loca
         if (nstage >= 3 || (pass == 1 && nstage >= 2)) break;
     }
     if (nstage < 2) return false;
+    p->paired = budget == pair_budget;
     QmvArgs& a = p->a;
     a.N = N; a.K = K; a.KS = KS; a.nchunks = nchunks; a.nstage = nstage; a.stage_bytes = stage_bytes;
     a.cpitch = cpitch; a.spitch = spitch;
@@ -209,9 +214,10 @@ static bool plan_qmv(int fmt, int N, int K, int xrows, int moe_slots, int E_loca
     a.moe_off = a.bar_off + 8 * qmv_nbars(nstage);
     // warp groups: as many tiles in flight as the ring allows (nstage >= wg * nchunks); MoE too (every warp passes
     // through every activation segment of its CTA in order, also those it has no tile in)
+    const int nch_tile = nchunks * (glu ? 2 : 1);   // stages per output tile
     a.wg = 1;
     for (int wg = QMV_MAXWG; wg > 1; wg /= 2)
-        if (nstage >= wg * nchunks) { a.wg = wg; break; }
+        if (nstage >= wg * nch_tile) { a.wg = wg; break; }
     // dense calls with at most one or two row tiles per CTA: groups beyond the CTA's tiles would idle, so long rows
     // go to fewer, larger groups (measured on B200: K = 6144 over 128 tiles, 2-bit: 4.9 us with one group, 6.5 with
     // four)
@@ -221,15 +227,15 @@ static bool plan_qmv(int fmt, int N, int K, int xrows, int moe_slots, int E_loca
         else if (tiles <= d.sm_count || (tiles <= 2 * d.sm_count && K >= 4096)) a.wg = a.wg < 2 ? a.wg : 2;
     }
     static const int wg_force = getenv("VKB_QMV_WG") ? atoi(getenv("VKB_QMV_WG")) : 0;   // tuning override
-    if (wg_force == 1 || ((wg_force == 2 || wg_force == 4) && nstage >= wg_force * nchunks)) a.wg = wg_force;
+    if (wg_force == 1 || ((wg_force == 2 || wg_force == 4) && nstage >= wg_force * nch_tile)) a.wg = wg_force;
     p->smem = a.moe_off + moebytes + slack;
     return true;
 }
 
-template <int F, int MODE, typename OutT>
+template <int F, int MODE, typename OutT, bool XF32 = false>
 static int launch_qmv(const QmvPlan& p, const CUtensorMap& tq, const CUtensorMap& ts, int grid, cudaStream_t st,
                       int dev) {
-    auto kern = qmv_kernel<F, MODE, OutT>;
+    auto kern = qmv_kernel<F, MODE, OutT, XF32>;
     static std::once_flag once[kMaxDevices];
     static cudaError_t attr_err[kMaxDevices];
     std::call_once(once[dev], [&] {
@@ -351,6 +357,83 @@ static int qmv_entry(const void* q, const void* s, const void* x, void* y, bool 
         return VKB_EUNSUPPORTED;
     return f32 ? launch_simple<F, float>(q, s, x, y, idx, N, K, M, topk, E_local, e0, zero_foreign, slots, st)
                : launch_simple<F, __half>(q, s, x, y, idx, N, K, M, topk, E_local, e0, zero_foreign, slots, st);
+}
+
+// fp32 activations -> fp16, round to nearest even (the reference's conversion step, used when the fp32 staging does
+// not fit the decode kernel's shared memory). Ordered after the previous kernel like every call.
+__global__ void __launch_bounds__(256) f32_to_f16_kernel(const float* __restrict__ x, __half* __restrict__ xh, int n) {
+    pdl_wait();
+    pdl_trigger();
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) xh[i] = __float2half_rn(x[i]);
+}
+
+static int launch_f32_to_f16(const float* x, void* xh, int n, cudaStream_t st) {
+    cudaLaunchConfig_t cfg{};
+    cfg.blockDim = dim3(256);
+    cfg.gridDim = dim3((unsigned)((n + 255) / 256 < 1024 ? (n + 255) / 256 : 1024));
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl_enabled() && pdl_stream_ok(st) ? 1 : 0;
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, f32_to_f16_kernel, x, (__half*)xh, n);
+    return e == cudaSuccess ? 0 : -(int)e;
+}
+
+// Q4 decode with fp32 activations (x_f32) and/or gate + up + SwiGLU over a stacked [2N][K] table (glu; ys: the
+// stacked products [M][2N] fp32, or null). fp32 activations are staged and rounded inside the decode kernel when the
+// staging fits next to the weight ring with two CTAs per SM; otherwise they are converted into xh (M x K fp16,
+// caller-owned) by one small kernel first, as the reference does. fp16 activations (x_f32 false) go straight in.
+static int qmv_q4_ext(const void* q, const void* s, const void* x, bool x_f32, void* xh, float* ys, void* y,
+                      bool out_f32, bool glu, int N, int K, int M, cudaStream_t st) {
+    if (!q || !s || !x || !y) return VKB_EINVAL;
+    if (N < 1 || K < 32 || M < 1) return VKB_EINVAL;
+    if (K % 32 != 0 || M > QMV_MAXTOK) return VKB_EUNSUPPORTED;
+    const long long rows = glu ? 2ll * N : (long long)N;
+    if (rows > (1ll << 31) - 1) return VKB_EUNSUPPORTED;
+    int dev = 0;
+    if (int r = current_device(&dev)) return r;
+    const DeviceInfo& d = device_info(dev);
+    const bool fast_w = K % 256 == 0 && aligned16(q) && aligned16(s);
+    if (!glu && !x_f32) return qmv_dispatch(VKB_FMT_Q4, q, s, x, y, out_f32, nullptr, N, K, M, 0, 0, 0, 0, st);
+    QmvPlan p{};
+    bool staged_f32 = false;
+    if (x_f32 && fast_w && aligned16(x) && plan_qmv(VKB_FMT_Q4, N, K, M, 0, 0, d, &p, 4, glu) && p.paired)
+        staged_f32 = true;
+    const void* xin = x;
+    if (x_f32 && !staged_f32) {   // convert first (xh: M x K fp16, caller-owned)
+        if (!xh) return VKB_EINVAL;
+        if (glu && !(fast_w && aligned16(xh))) return VKB_EUNSUPPORTED;   // before anything is launched
+        if (int r = launch_f32_to_f16((const float*)x, xh, M * K, st)) return r;
+        xin = xh;
+        if (!glu) return qmv_dispatch(VKB_FMT_Q4, q, s, xh, y, out_f32, nullptr, N, K, M, 0, 0, 0, 0, st);
+    }
+    if (!staged_f32) {   // gate/up with fp16 activations: the pipelined kernel only
+        if (!fast_w || !aligned16(xin) || !plan_qmv(VKB_FMT_Q4, N, K, M, 0, 0, d, &p, 2, true))
+            return VKB_EUNSUPPORTED;
+    }
+    CUtensorMap tq, ts;
+    int r = get_tmap_2d(&tq, q, (uint64_t)rows, (uint64_t)K / 2, CU_TENSOR_MAP_DATA_TYPE_UINT64, 8,
+                        (uint32_t)(p.a.cpitch / 8), QMV_ROWS, CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (r) return r;
+    r = get_tmap_2d(&ts, s, (uint64_t)rows, (uint64_t)K / 16, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2,
+                    (uint32_t)(p.a.spitch / 2), QMV_ROWS, CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (r) return r;
+    p.a.x = (const __half*)xin;
+    p.a.y = y;
+    p.a.ys = glu ? ys : nullptr;
+    p.a.T = M;
+    const int grid = p.a.tilesN < d.sm_count ? p.a.tilesN : d.sm_count;
+    if (glu) {
+        if (staged_f32)
+            return out_f32 ? launch_qmv<FMT_Q4, QMV_GLU, float, true>(p, tq, ts, grid, st, dev)
+                           : launch_qmv<FMT_Q4, QMV_GLU, __half, true>(p, tq, ts, grid, st, dev);
+        return out_f32 ? launch_qmv<FMT_Q4, QMV_GLU, float, false>(p, tq, ts, grid, st, dev)
+                       : launch_qmv<FMT_Q4, QMV_GLU, __half, false>(p, tq, ts, grid, st, dev);
+    }
+    return out_f32 ? launch_qmv<FMT_Q4, QMV_DENSE, float, true>(p, tq, ts, grid, st, dev)
+                   : launch_qmv<FMT_Q4, QMV_DENSE, __half, true>(p, tq, ts, grid, st, dev);
 }
 
 int qmv_dispatch(int fmt, const void* q, const void* s, const void* x, void* y, bool f32, const int32_t* idx, int N,
@@ -604,6 +687,21 @@ int vkb_moe(int fmt, const void* qpool, const void* spool, const int32_t* idx, i
 int vkb_moe_q4(const void* qpool, const void* spool, const int32_t* idx, int T, int topk, const void* x, void* y,
                int E_local, int e0, int N, int K, vkb_stream_t stream) {
     return vkb_moe(VKB_FMT_Q4, qpool, spool, idx, T, topk, x, y, 0, E_local, e0, N, K, stream);
+}
+
+int vkb_gemv_q4_f32in(const void* q, const void* s, const float* x, void* xh, float* y, int N, int K, int M,
+                      vkb_stream_t stream) {
+    return qmv_q4_ext(q, s, x, true, xh, nullptr, y, true, false, N, K, M, (cudaStream_t)stream);
+}
+
+int vkb_gate_up_glu_q4_f32in(const void* q, const void* s, const float* x, void* xh, float* ystack, float* out, int N,
+                             int K, int M, vkb_stream_t stream) {
+    return qmv_q4_ext(q, s, x, true, xh, ystack, out, true, true, N, K, M, (cudaStream_t)stream);
+}
+
+int vkb_gate_up_glu_q4(const void* q, const void* s, const void* x, float* ystack, void* out, int out_f32, int N, int K,
+                       int M, vkb_stream_t stream) {
+    return qmv_q4_ext(q, s, x, false, nullptr, ystack, out, out_f32 != 0, true, N, K, M, (cudaStream_t)stream);
 }
 
 int vkb_gemm_q4_tc(const void* q, const void* s, const void* x, void* y, int N, int K, int M, vkb_stream_t stream) {

@@ -96,6 +96,9 @@ def _register_optional(L) -> None:
         "vkb_comm_free": ([vp, vp], i),
         "vkb_gemm_q4_tc_rowsplit_p2p": ([vp, vp, vp, vp, vp, i, i, i, vp], i),
         "vkb_moe_ep_p2p": ([vp, i, vp, vp, vp, i, i, vp, vp, i, i, i, i, i, vp], i),
+        "vkb_gemv_q4_f32in": ([vp, vp, vp, vp, vp, i, i, i, vp], i),
+        "vkb_gate_up_glu_q4_f32in": ([vp, vp, vp, vp, vp, vp, i, i, i, vp], i),
+        "vkb_gate_up_glu_q4": ([vp, vp, vp, vp, vp, i, i, i, i, vp], i),
         "vkb_graph_begin": ([vp], i),
         "vkb_graph_end": ([vp, ctypes.POINTER(vp)], i),
         "vkb_graph_launch": ([vp, vp], i),
@@ -193,6 +196,11 @@ def _ptr(t) -> ctypes.c_void_p:
     return ctypes.c_void_p(t.data_ptr())
 
 
+def _optr(t) -> ctypes.c_void_p | None:
+    """_ptr, or a null pointer for None (optional outputs)."""
+    return None if t is None else _ptr(t)
+
+
 def gemv(fmt: int, q, s, x, y=None, out_f32: bool = False, stream=None):
     """y[M][N] = x[M][K] . W[N][K]^T for M <= 8. q: packed codes (uint8/int8/int32 storage), s: fp16 [N][K/32],
     x: fp16 [M][K] on the same CUDA device. Returns y (fp16, or fp32 with out_f32)."""
@@ -204,6 +212,47 @@ def gemv(fmt: int, q, s, x, y=None, out_f32: bool = False, stream=None):
     rc = lib().vkb_gemv(fmt, _ptr(q), _ptr(s), _ptr(x), _ptr(y), int(out_f32), N, K, M, _stream(stream))
     check(rc, "vkb_gemv")
     return y
+
+
+def gemv_q4_f32in(q, s, x, xh=None, y=None, stream=None):
+    """Q4 decode with fp32 activations x [M][K] (rounded to fp16, round to nearest even): y fp32 [M][N]. xh: fp16
+    scratch of M x K, used when the kernel cannot stage the fp32 activations itself (allocated here if not given)."""
+    torch = _torch()
+    M, K = x.shape
+    N = s.shape[0]
+    if y is None:
+        y = torch.empty((M, N), dtype=torch.float32, device=x.device)
+    if xh is None:
+        xh = torch.empty((M, K), dtype=torch.float16, device=x.device)
+    check(lib().vkb_gemv_q4_f32in(_ptr(q), _ptr(s), _ptr(x), _ptr(xh), _ptr(y), N, K, M, _stream(stream)),
+          "vkb_gemv_q4_f32in")
+    return y
+
+
+def gate_up_glu_q4(q, s, x, ystack=None, out=None, out_f32: bool = True, want_stack: bool = True, xh=None,
+                   stream=None):
+    """Gate + up + SwiGLU: q, s the stacked [2N][K] Q4 table (gate rows, then up rows), x [M][K] fp32 (the
+    reference's fp32-in entry) or fp16. Returns (out [M][N] = silu(gate) * up, ystack [M][2N] fp32 or None)."""
+    torch = _torch()
+    M, K = x.shape
+    N = s.shape[0] // 2
+    if want_stack and ystack is None:
+        ystack = torch.empty((M, 2 * N), dtype=torch.float32, device=x.device)
+    if x.dtype == torch.float32:
+        if out is None:
+            out = torch.empty((M, N), dtype=torch.float32, device=x.device)
+        if xh is None:
+            xh = torch.empty((M, K), dtype=torch.float16, device=x.device)
+        rc = lib().vkb_gate_up_glu_q4_f32in(_ptr(q), _ptr(s), _ptr(x), _ptr(xh), _optr(ystack), _ptr(out), N, K, M,
+                                            _stream(stream))
+        check(rc, "vkb_gate_up_glu_q4_f32in")
+    else:
+        if out is None:
+            out = torch.empty((M, N), dtype=torch.float32 if out_f32 else torch.float16, device=x.device)
+        rc = lib().vkb_gate_up_glu_q4(_ptr(q), _ptr(s), _ptr(x), _optr(ystack), _ptr(out),
+                                      int(out.dtype == torch.float32), N, K, M, _stream(stream))
+        check(rc, "vkb_gate_up_glu_q4")
+    return out, ystack
 
 
 def moe(fmt: int, qpool, spool, idx, x, y=None, E_local: int | None = None, e0: int = 0, out_f32: bool = False,
