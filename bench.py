@@ -291,6 +291,39 @@ def moe_section(torch, vkb, dev, stream, L2, comm=None, rank=0, world=1):
     return out
 
 
+def glu_section(torch, vkb, dev, stream, L2):
+    """SURVEY 8(f) row 1, the reference's like-for-like decode entries: Q4 decode with fp32 activations (rounded to
+    fp16 inside the kernel) on configs[0]'s table, and gate + up + SwiGLU (Qwen3-1.7B's MLP, gate and up 6144x2048
+    stacked) with fp32 activations, one kernel; weights cycled over >= 4x L2. GB/s: packed weights + activations +
+    outputs per call."""
+    out = {}
+    cases = [("q4_f32in_8192x2048", 8192, 2048, False), ("glu_q4_f32in_2x6144x2048", 6144, 2048, True)]
+    for name, N, K, glu in cases:
+        rows = 2 * N if glu else N
+        codes, scales = vkb.quantize(0, vkb.synth_normal(3, (rows, K), 0.02))
+        q0 = vkb.to_device_packed(vkb.pack(0, codes), dev)
+        s0 = vkb.to_device_f16(scales, dev)
+        wbytes = q0.numel() + 2 * s0.numel()
+        n = _copies(wbytes, L2)
+        ql, sl = [q0] + [q0.clone() for _ in range(n - 1)], [s0] + [s0.clone() for _ in range(n - 1)]
+        for M in (1, 2, 4, 8):
+            x = torch.from_numpy(vkb.synth_normal(17 + M, (M, K), 1.0).astype("float32")).to(dev)
+            xh = torch.empty((M, K), dtype=torch.float16, device=dev)
+            if glu:
+                ys = torch.empty((M, 2 * N), dtype=torch.float32, device=dev)
+                y = torch.empty((M, N), dtype=torch.float32, device=dev)
+                us = _median_us(torch, stream, lambda i: vkb.gate_up_glu_q4(ql[i % n], sl[i % n], x, ystack=ys, out=y,
+                                                                              xh=xh))
+                nbytes = wbytes + M * K * 4 + M * 2 * N * 4 + M * N * 4
+            else:
+                y = torch.empty((M, N), dtype=torch.float32, device=dev)
+                us = _median_us(torch, stream, lambda i: vkb.gemv_q4_f32in(ql[i % n], sl[i % n], x, xh=xh, y=y))
+                nbytes = wbytes + M * K * 4 + M * N * 4
+            out[f"{name}_m{M}"] = {"us": round(us, 2), "GBps": round(nbytes / us / 1e3, 1)}
+        del ql, sl
+    return out
+
+
 def rowsplit_section(torch, vkb, dev, stream, L2, comm, rank, world):
     """configs[4] with the weight rows split over the ranks (vkb_gemm_q4_tc_rowsplit: local tcgen05 GEMM, in-place
     all-gather, permute)."""
@@ -493,6 +526,7 @@ def run_ours(args, rank: int, world: int, local_rank: int, dist):
     # prompt GEMM and MoE on this GPU (every rank runs them: replicas), then the sharded paths when world > 1
     prompt = prompt_section(torch, vkb, dev, stream, L2, peaks)
     moe1 = moe_section(torch, vkb, dev, stream, L2)
+    glu1 = glu_section(torch, vkb, dev, stream, L2)
     sharded = None
     if dist is not None:
         from vkb import dist as D
@@ -568,6 +602,7 @@ def run_ours(args, rank: int, world: int, local_rank: int, dist):
         "headline": headline,
         "prompt_gemm": prompt,
         "moe": moe1,
+        "f32in_and_glu": glu1,
         "sharded": sharded,
     }
 

@@ -68,15 +68,14 @@ int vkb_gemv(int fmt, const void* q, const void* s, const void* x, void* y, int 
  * Replace fused_q4_v3_fp32in and gate_up_glu_fp32in (reference src/stage5_gap8.cuh:207-245), Q4 only like them.
  *
  * vkb_gemv_q4_f32in: x fp32 [M][K] is rounded to fp16 (round to nearest even) and multiplied as vkb_gemv_q4_f32
- * would: the result equals vkb_gemv_q4_f32 on the rounded x. The rounding happens inside the decode kernel, which
- * stages the fp32 activations, when they fit its shared memory next to the weight ring. Otherwise the call first
- * converts x into xh (M * K fp16, caller-owned scratch, the reference's xh) with one small kernel; xh may be null
- * when the staging fits.
+ * would on the rounded x (up to the order of fp32 sums). The pipelined decode kernel (K % 256 == 0, 16-byte aligned
+ * q, s, x) reads and rounds the fp32 activations itself: one launch. Other shapes first convert x into xh (M * K fp16,
+ * caller-owned scratch, the reference's xh) with one small kernel; xh may be null when the pipelined kernel runs.
  *
  * vkb_gate_up_glu_q4_f32in: q, s hold the stacked [2N][K] table (rows 0..N-1 gate, N..2N-1 up). ystack [M][2N] fp32
  * receives the stacked product (may be null); out [M][N] fp32 = silu(gate) * up, silu(g) = g / (1 + exp(-g)).
- * One kernel: each 16-row output tile streams its gate rows, then its up rows; the SwiGLU is applied where the two
- * sums meet. It needs K % 256 == 0 and 16-byte aligned q, s, x (and xh when used): VKB_EUNSUPPORTED otherwise.
+ * One kernel: gate tile j and up tile j go to adjacent warp groups of one CTA; the SwiGLU is applied where the two
+ * sums meet. It needs K % 256 == 0 and 16-byte aligned q, s, x: VKB_EUNSUPPORTED otherwise (xh is not used).
  * vkb_gate_up_glu_q4 is the same with fp16 activations and fp16 (out_f32 = 0) or fp32 output.
  *
  * Token counts 1..8 (the reference: 1, 2, 4, 8 only; 3, 5, 6, 7 work here too); M > 8 is VKB_EUNSUPPORTED. */

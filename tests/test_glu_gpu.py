@@ -2,9 +2,9 @@
 (vkb_gate_up_glu_q4_f32in / vkb_gate_up_glu_q4) through the C ABI.
 
 - fp32 in: the result must match the fp16-activation GEMV on the activations rounded to fp16 (the reference's
-  conversion step, src/stage5_gap8.cuh:207-228) to fp32 summation-order differences (the two paths may split K over
-  the warps differently), on both of the library's paths: fp32 staged inside the kernel (short rows) and the
-  separate conversion into xh (K = 6144 at 8 tokens does not fit the staging), and the oracle.
+  conversion step, src/stage5_gap8.cuh:207-228) to fp32 summation-order differences, on both of the library's
+  paths: rounding inside the pipelined kernel, and the separate conversion into xh followed by the general kernel
+  (K = 640, not a multiple of 256), and the oracle.
 - gate/up: the reference's own check (src/bakeoff.cu:370-406) on its table (Qwen3-1.7B MLP, gate and up 6144x2048
   stacked): the stacked product against the oracle (exact-code class here, 1e-4; the reference allows 2e-3), and
   out against silu(gate) * up recomputed from that product (1e-5).
@@ -67,8 +67,8 @@ def test_gate_up_glu_reference_check(cuda, M):
 
 @pytest.mark.parametrize("N,K,M", [(1000, 2048, 5), (256, 6144, 8), (6144, 2048, 1)])
 def test_gate_up_glu_shapes_and_outputs(cuda, N, K, M):
-    """Ragged N (1000: the last output tile is partial in both halves), long rows (K = 6144: fp32 staging does not fit
-    at 8 tokens, so xh is used), fp16 activations with fp16 and fp32 outputs, and no stacked output."""
+    """Ragged N (1000: the last output tile pair is partial in both halves), long rows (K = 6144), a single tile pair
+    per CTA (N = 256), fp16 activations with fp16 and fp32 outputs, and no stacked output."""
     import torch
     rng = np.random.default_rng(N + K + M)
     codes, scales = random_codes(rng, O.FMT_Q4, 2 * N, K)

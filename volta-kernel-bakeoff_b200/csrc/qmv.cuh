@@ -46,13 +46,14 @@ constexpr int QMV_ROWS = 16;       // weight rows per tile (the MMA's M)
 constexpr int QMV_MAXTOK = 8;      // tokens per MMA column group (the MMA's N)
 
 // QMV_MOE_P2P: MoE whose outputs are also pushed into every peer's copy of y (expert parallelism, peer stores).
-// QMV_GLU: gate + up + SwiGLU over a stacked [2N][K] table (rows 0..N-1 gate, N..2N-1 up): every 16-row output
-// tile streams its gate rows, then its up rows, into two accumulators; the reducer writes out = silu(gate) * up (and
-// the stacked products, when asked).
+// QMV_GLU: gate + up + SwiGLU over a stacked [2N][K] table (rows 0..N-1 gate, N..2N-1 up). Tiles come in pairs: tile
+// 2j = gate rows 16j.., tile 2j + 1 = up rows N + 16j.. (a CTA's range is pair aligned, so adjacent warp groups take
+// the two halves); the gate tile's reducer hands its sums to the up tile's reducer through shared memory, which
+// writes out = silu(gate) * up (and the stacked products, when asked). Stages and reductions are the dense GEMV's.
 enum : int { QMV_DENSE = 0, QMV_MOE = 1, QMV_MOE_P2P = 2, QMV_GLU = 3 };
 
 struct QmvArgs {
-    const __half* x;         // [T][K] (fp32 for the XF32 kernels)
+    const __half* x;         // [T][K] (fp32 [T][K] for the XF32 kernels)
     float* ys;               // QMV_GLU: the stacked products [T][2N] (gate, then up) or null
     void* y;                 // dense: [T][N]; MoE: [T*topk][N]
     const int32_t* idx;      // MoE: [T*topk] global expert ids
@@ -124,42 +125,12 @@ __device__ __forceinline__ void load_a(uint32_t a, int t, uint32_t (&r)[4]) {
     }
 }
 
-// Two fp32 activations (bit patterns) -> one f16x2 register (lo in the low half), round to nearest even: the
-// reference's fp32 -> fp16 conversion of the activations.
-__device__ __forceinline__ uint32_t cvt_h2(uint32_t lo, uint32_t hi) {
-    uint32_t d;
-    asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(__uint_as_float(hi)), "f"(__uint_as_float(lo)));
-    return d;
-}
-
 // The B registers (two k16 steps) of this thread's token for the group whose activations start at shared address xa
 // (xa already includes the thread's t offset). Padding token columns read a real row: their MMA columns are never
-// stored, and the MMA keeps columns independent. XF32: the activations are staged as fp32 (twice the bytes, same
-// order) and rounded to fp16 here, in the pairs the format's unpack order wants.
-template <int F, bool XF32 = false>
+// stored, and the MMA keeps columns independent.
+template <int F>
 __device__ __forceinline__ void load_b(uint32_t xa, uint32_t (&b)[4]) {
-    if constexpr (XF32) {
-        if constexpr (F == FMT_Q2) {
-            const uint4 lo = lds128(xa), hi = lds128(xa + 32);   // x0..x3, x8..x11
-            b[0] = cvt_h2(lo.x, hi.x);
-            b[1] = cvt_h2(lo.y, hi.y);
-            b[2] = cvt_h2(lo.z, hi.z);
-            b[3] = cvt_h2(lo.w, hi.w);
-        } else {
-            const uint4 v0 = lds128(xa), v1 = lds128(xa + 16);   // x0..x3, x4..x7
-            if constexpr (F == FMT_Q4) {
-                b[0] = cvt_h2(v0.x, v1.x);   // (x0, x4)
-                b[1] = cvt_h2(v0.y, v1.y);   // (x1, x5)
-                b[2] = cvt_h2(v0.z, v1.z);   // (x2, x6)
-                b[3] = cvt_h2(v0.w, v1.w);   // (x3, x7)
-            } else {
-                b[0] = cvt_h2(v0.x, v0.y);
-                b[1] = cvt_h2(v0.z, v0.w);
-                b[2] = cvt_h2(v1.x, v1.y);
-                b[3] = cvt_h2(v1.z, v1.w);
-            }
-        }
-    } else if constexpr (F == FMT_Q2) {
+    if constexpr (F == FMT_Q2) {
         const uint2 xa0 = lds64(xa), xb0 = lds64(xa + 16);
         b[0] = prmt(xa0.x, xb0.x, 0x5410u);   // (x0, x8)
         b[1] = prmt(xa0.x, xb0.x, 0x7632u);   // (x1, x9)
@@ -178,21 +149,20 @@ __device__ __forceinline__ void load_b(uint32_t xa, uint32_t (&b)[4]) {
     }
 }
 
-// Per-thread byte offset of its activations inside a 32-value group (see load_b); doubled for fp32 activations.
-template <int F, bool XF32 = false>
+// Per-thread byte offset of its activations inside a 32-value group (see load_b).
+template <int F>
 __device__ __forceinline__ uint32_t x_lane_off(int t) {
-    constexpr uint32_t XS = XF32 ? 2 : 1;
-    if constexpr (F == FMT_Q2) return XS * (32 * (t >> 1) + 8 * (t & 1));
-    else return XS * 16 * t;
+    if constexpr (F == FMT_Q2) return 32 * (t >> 1) + 8 * (t & 1);
+    else return 16 * t;
 }
 
 // One group: two k16 MMAs into a fresh fragment, then the per-row fp32 scales. ca: row g's codes in the stage;
 // row g+8 is 8 * cp further.
-template <int F, bool XF32 = false>
+template <int F>
 __device__ __forceinline__ void qmv_group(uint32_t ca, uint32_t cp, int G, int t, uint32_t xa, float s0, float s1,
                                           float (&acc)[4]) {
     uint32_t b[4], ar[4], ar8[4];
-    load_b<F, XF32>(xa, b);
+    load_b<F>(xa, b);
     const uint32_t a = ca + code_off<F>(G, t);
     load_a<F>(a, t, ar);
     load_a<F>(a + 8 * cp, t, ar8);
@@ -209,28 +179,35 @@ __device__ __forceinline__ void qmv_group(uint32_t ca, uint32_t cp, int G, int t
 //   ca, cp: shared address of row g's codes in the stage, code row pitch
 //   sc, sp: shared address of row g's scales in the stage, scale row pitch
 //   xa:     shared address of this thread's activations for stage-local group 0
-template <int F, bool XF32 = false>
+template <int F>
 __device__ __forceinline__ void consume_stage(uint32_t ca, uint32_t cp, uint32_t sc, uint32_t sp, int G0, int G1,
                                               uint32_t xa, int t, float (&acc)[4]) {
-    constexpr uint32_t XG = XF32 ? 128 : 64;   // activation bytes of one 32-value group
     int G = G0;
     if (G & 1) {   // odd start: single group, its scale from the aligned pair
         if (G < G1) {
             const uint32_t p0 = lds32(sc + 2 * (G - 1)), p1 = lds32(sc + 8 * sp + 2 * (G - 1));
-            qmv_group<F, XF32>(ca, cp, G, t, xa + XG * G, half_hi_f32(p0), half_hi_f32(p1), acc);
+            qmv_group<F>(ca, cp, G, t, xa + 64 * G, half_hi_f32(p0), half_hi_f32(p1), acc);
         }
         ++G;
     }
 #pragma unroll 1
     for (; G + 1 < G1; G += 2) {
         const uint32_t p0 = lds32(sc + 2 * G), p1 = lds32(sc + 8 * sp + 2 * G);
-        qmv_group<F, XF32>(ca, cp, G, t, xa + XG * G, half_lo_f32(p0), half_lo_f32(p1), acc);
-        qmv_group<F, XF32>(ca, cp, G + 1, t, xa + XG * (G + 1), half_hi_f32(p0), half_hi_f32(p1), acc);
+        qmv_group<F>(ca, cp, G, t, xa + 64 * G, half_lo_f32(p0), half_lo_f32(p1), acc);
+        qmv_group<F>(ca, cp, G + 1, t, xa + 64 * (G + 1), half_hi_f32(p0), half_hi_f32(p1), acc);
     }
     if (G < G1) {
         const uint32_t p0 = lds32(sc + 2 * G), p1 = lds32(sc + 8 * sp + 2 * G);
-        qmv_group<F, XF32>(ca, cp, G, t, xa + XG * G, half_lo_f32(p0), half_lo_f32(p1), acc);
+        qmv_group<F>(ca, cp, G, t, xa + 64 * G, half_lo_f32(p0), half_lo_f32(p1), acc);
     }
+}
+
+// Two fp32 activations (bit patterns) -> one f16x2 register (lo in the low half), round to nearest even: the
+// reference's fp32 -> fp16 conversion of the activations.
+__device__ __forceinline__ uint32_t cvt_h2(uint32_t lo, uint32_t hi) {
+    uint32_t d;
+    asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(__uint_as_float(hi)), "f"(__uint_as_float(lo)));
+    return d;
 }
 
 template <typename OutT> __device__ __forceinline__ OutT to_out(float v);
@@ -364,20 +341,21 @@ __device__ __noinline__ void qmv_moe_push(const QmvArgs& a, MoeTables tb, int w0
 // slot's last completed phase, which is all an mbarrier parity wait can tell apart.
 //
 // Barrier block layout (uint64 slots from bar_off): full[nstage], empty[nstage], xfull[2], xempty[2],
-// redfull[2 * QMV_MAXWG], redfree[2 * QMV_MAXWG].
+// redfull[2 * QMV_MAXWG], redfree[2 * QMV_MAXWG], gfull[2], gfree[2]. The reduction region holds 2 * QMV_NW * 32
+// float4 (plus 2 x 32 float4 of gate hand-over slots for QMV_GLU).
 constexpr int QMV_MAXWG = 4;
-__host__ __device__ constexpr int qmv_nbars(int nstage) { return 2 * nstage + 4 + 4 * QMV_MAXWG; }
+__host__ __device__ constexpr int qmv_nbars(int nstage) { return 2 * nstage + 4 + 4 * QMV_MAXWG + 4; }
 
-// XF32: the activations arrive as fp32 (the reference's fp32-in decode entry); they are staged as fp32 and rounded to
-// fp16 while the MMA operands are built, so no separate conversion pass or launch.
+// XF32: the activations arrive as fp32 (the reference's fp32-in decode entry). After the dependency wait the consumer
+// warps read them from global memory (16-byte loads), round them to fp16 (round to nearest even, the reference's
+// conversion) straight into the fp16 activation buffer and complete its barrier themselves: no conversion launch,
+// no extra shared memory, and the MMA path is the fp16 one.
 template <int F, int MODE, typename OutT, bool XF32 = false>
 __global__ void __launch_bounds__(32 * (QMV_NW + 1), 2)
 qmv_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap ts, const __grid_constant__ QmvArgs a) {
     static_assert(!XF32 || MODE == QMV_DENSE || MODE == QMV_GLU, "fp32 activations: dense and gate/up calls");
     constexpr bool GLU = MODE == QMV_GLU;
     constexpr bool MOE = MODE == QMV_MOE || MODE == QMV_MOE_P2P;
-    constexpr int XB = XF32 ? 4 : 2;   // bytes per staged activation
-    const int NCH = (GLU ? 2 : 1) * a.nchunks;   // stages per output tile (gate chunks, then up chunks)
     const int WG = a.wg;
     const int WPG = QMV_NW / WG;
     extern __shared__ uint8_t smem_raw[];
@@ -393,6 +371,8 @@ qmv_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUten
     uint64_t* xempty = xfull + 2;
     uint64_t* redfull = xfull + 4;
     uint64_t* redfree = redfull + 2 * QMV_MAXWG;
+    uint64_t* gfull = redfree + 2 * QMV_MAXWG;   // QMV_GLU: gate sums handed over in slot 0 / 1
+    uint64_t* gfree = gfull + 2;                 // QMV_GLU: the up reducer has taken them
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int KG = a.K / 32;
@@ -412,6 +392,10 @@ qmv_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUten
             mbar_init(&redfull[i], WPG);
             mbar_init(&redfree[i], 1);
         }
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(&gfull[i], 1);
+            mbar_init(&gfree[i], 1);
+        }
         fence_mbar_init();
     }
 
@@ -425,8 +409,10 @@ qmv_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUten
     }
 
     const int total = nseg * a.tilesN;
-    const int w0 = (int)(((long long)blockIdx.x * total) / gridDim.x);
-    const int w1 = (int)(((long long)(blockIdx.x + 1) * total) / gridDim.x);
+    // the CTA's tiles [w0, w1); gate/up tiles are split in whole pairs
+    const int units = GLU ? total / 2 : total, ustep = GLU ? 2 : 1;
+    const int w0 = ustep * (int)(((long long)blockIdx.x * units) / gridDim.x);
+    const int w1 = ustep * (int)(((long long)(blockIdx.x + 1) * units) / gridDim.x);
     const int ntl = w1 - w0;   // tiles of this CTA
 
     // segment accessors: expert (weight row base), token count, and the slot (dense: token) of column j
@@ -453,21 +439,20 @@ qmv_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUten
         if (lane == 0) {
             prefetch_tmap(&tq);
             prefetch_tmap(&ts);
-            const int total_it = ntl * NCH;
+            const int total_it = ntl * a.nchunks;
             const int pre = min(total_it, a.nstage);
             // iteration cursor: chunk c of tile `tile` of segment `sg`; ring slot stg in round rnd
             int c = 0, sg = w0 / a.tilesN, tile = w0 % a.tilesN, stg = 0, rnd = 0, issued = 0;
             auto issue_w = [&]() {
                 uint8_t* st = ring + stg * a.stage_bytes;
                 uint64_t* fb = &full[stg];
-                const bool up = GLU && c >= a.nchunks;               // gate/up: the up rows' chunks come second
-                const int kch = up ? c - a.nchunks : c;
-                const int row = (up ? a.N : seg_expert(sg) * a.N) + tile * QMV_ROWS;
+                const int row = GLU ? ((tile & 1) ? a.N : 0) + (tile >> 1) * QMV_ROWS    // gate / up tile pair
+                                    : seg_expert(sg) * a.N + tile * QMV_ROWS;
                 mbar_arrive_expect_tx(fb, stage_tx);
-                tma_load_2d(st, &tq, kch * ksb / 8, row, fb);                              // 8-byte elements
-                tma_load_2d(st + QMV_ROWS * a.cpitch, &ts, kch * (a.KS / 32), row, fb);  // fp16 elements
+                tma_load_2d(st, &tq, c * ksb / 8, row, fb);                              // 8-byte elements
+                tma_load_2d(st + QMV_ROWS * a.cpitch, &ts, c * (a.KS / 32), row, fb);  // fp16 elements
                 ++issued;
-                if (++c == NCH) {
+                if (++c == a.nchunks) {
                     c = 0;
                     if (++tile == a.tilesN) { tile = 0; ++sg; }
                 }
@@ -481,12 +466,11 @@ qmv_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUten
                 if (!ok) return;
                 const int cnt = seg_count(xs);
                 uint8_t* dst = xbuf + xb * a.xrows * a.xpitch;
-                mbar_arrive_expect_tx(&xfull[xb], (uint32_t)(cnt * a.K * XB));
+                mbar_arrive_expect_tx(&xfull[xb], (uint32_t)(cnt * a.K * 2));
                 for (int j = 0; j < cnt; ++j) {
                     int tok = seg_slot(xs, j);
-                    if constexpr (MODE == QMV_MOE || MODE == QMV_MOE_P2P) tok /= a.topk;
-                    bulk_load(dst + j * a.xpitch, reinterpret_cast<const uint8_t*>(a.x) + (size_t)tok * a.K * XB,
-                              (uint32_t)(a.K * XB), &xfull[xb]);
+                    if constexpr (MOE) tok /= a.topk;
+                    bulk_load(dst + j * a.xpitch, a.x + (size_t)tok * a.K, (uint32_t)(a.K * 2), &xfull[xb]);
                 }
                 ++xsegs;
             };
@@ -496,13 +480,20 @@ qmv_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUten
             int last_seg = -1;
             {
                 int xsg = w0 / a.tilesN, xtile = w0 % a.tilesN;
-                for (int it = 0; it < pre && ok; it += NCH) {
-                    if (xsg != last_seg) { issue_x(xsg); last_seg = xsg; }
+                for (int it = 0; it < pre && ok; it += a.nchunks) {
+                    if (xsg != last_seg) {
+                        if constexpr (!XF32) issue_x(xsg);   // XF32: the consumers fill the buffer
+                        last_seg = xsg;
+                    }
                     if (++xtile == a.tilesN) { xtile = 0; ++xsg; }
                 }
             }
             for (int it = pre; it < total_it && ok; ++it) {
-                if (c == 0 && sg != last_seg) { issue_x(sg); last_seg = sg; if (!ok) break; }
+                if (c == 0 && sg != last_seg) {   // dense and gate/up calls have one segment: never for XF32
+                    if constexpr (!XF32) issue_x(sg);
+                    last_seg = sg;
+                    if (!ok) break;
+                }
                 ok = wait_parity(&empty[stg], (rnd - 1) & 1);
                 if (!ok) break;
                 issue_w();
@@ -535,6 +526,21 @@ qmv_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUten
     const uint32_t s_row = (uint32_t)(QMV_ROWS * a.cpitch) + g * sp;     // row g's scales inside a stage
     OutT* y = reinterpret_cast<OutT*>(a.y);
     pdl_wait();   // x and y may still be written (or y read) by the previous grid
+    if constexpr (XF32) {   // fp32 activations -> the fp16 buffer of segment 0, then its barrier (count 1, no bytes)
+        const float4* xf = reinterpret_cast<const float4*>(a.x);
+        const int total4 = a.T * a.K / 4;
+        for (int i = threadIdx.x; i < total4; i += QMV_NW * 32) {
+            const float4 v = xf[i];
+            const int e = 4 * i, m = e / a.K, k = e - m * a.K;
+            const uint32_t lo = cvt_h2(__float_as_uint(v.x), __float_as_uint(v.y));
+            const uint32_t hi = cvt_h2(__float_as_uint(v.z), __float_as_uint(v.w));
+            asm volatile("st.shared.v2.b32 [%0], {%1, %2};" ::"r"(xbuf_s + (uint32_t)(m * a.xpitch + 2 * k)), "r"(lo),
+                         "r"(hi)
+                         : "memory");
+        }
+        named_sync(1, QMV_NW * 32);
+        if (threadIdx.x == 0) mbar_arrive(&xfull[0]);
+    }
     if constexpr (MODE == QMV_MOE_P2P) {   // peer stores: this rank's copy may be written from now on
         if (warp == 0 && lane == 0) p2p_post_ready(a.pp, p2p_epoch(a.pp));
     }
@@ -579,7 +585,7 @@ qmv_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUten
     int sg = (w0 + grp) / a.tilesN, tile = (w0 + grp) % a.tilesN;
     int stg = 0, rnd = 0;
     {
-        const int it0 = grp * NCH;   // the first iteration of this group (no division in the loop)
+        const int it0 = grp * a.nchunks;   // the first iteration of this group (no division in the loop)
         rnd = it0 / a.nstage;
         stg = it0 - rnd * a.nstage;
     }
@@ -590,21 +596,15 @@ qmv_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUten
             const int xb = (jn - 1) & 1;
             cnt = seg_count(sg);
             xrow = xbuf_s + (uint32_t)(xb * a.xrows * a.xpitch + (g < cnt ? g : 0) * a.xpitch) +
-                   x_lane_off<F, XF32>(t);
+                   x_lane_off<F>(t);
         }
         float acc[4] = {0.f, 0.f, 0.f, 0.f};
-        float accg[4] = {0.f, 0.f, 0.f, 0.f};   // QMV_GLU: the gate rows' sums (acc then takes the up rows')
         int kc = 0;
-        for (int c = 0; c < NCH; ++c, kc += GS) {
-            if (GLU && c == a.nchunks) {
-#pragma unroll
-                for (int q = 0; q < 4; ++q) { accg[q] = acc[q]; acc[q] = 0.f; }
-                kc = 0;
-            }
+        for (int c = 0; c < a.nchunks; ++c, kc += GS) {
             if (!wait_parity(&full[stg], rnd & 1)) { ok = false; break; }
             const uint32_t st = ring_s + (uint32_t)(stg * a.stage_bytes);
             const int G1 = min(G1w, KG - kc);
-            consume_stage<F, XF32>(st + c_row, cp, st + s_row, sp, G0, G1, xrow + (uint32_t)(kc * 32 * XB), t, acc);
+            consume_stage<F>(st + c_row, cp, st + s_row, sp, G0, G1, xrow + (uint32_t)(kc * 64), t, acc);
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[stg]);
             if (++stg == a.nstage) { stg = 0; ++rnd; }
@@ -615,10 +615,8 @@ qmv_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUten
         uint64_t* rfull = &redfull[grp * 2 + tp];
         uint64_t* rfree = &redfree[grp * 2 + tp];
         float4* rb = red + ((grp * 2 + tp) * WPG) * 32;
-        float4* rbg = rb + 2 * QMV_NW * 32;   // QMV_GLU: the gate partials, in a second region
         if (use > 0 && !wait_parity(rfree, (use - 1) & 1)) { ok = false; break; }
         rb[wi * 32 + lane] = make_float4(acc[0], acc[1], acc[2], acc[3]);
-        if constexpr (GLU) rbg[wi * 32 + lane] = make_float4(accg[0], accg[1], accg[2], accg[3]);
         __syncwarp();
         if (lane == 0) mbar_arrive(rfull);
         if (wi == reducer) {
@@ -628,30 +626,42 @@ qmv_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUten
                 const float4 q = rb[v * 32 + lane];
                 r.x += q.x; r.y += q.y; r.z += q.z; r.w += q.w;
             }
-            float4 rg = make_float4(0.f, 0.f, 0.f, 0.f);
-            if constexpr (GLU) {
-                rg = rbg[lane];
-                for (int v = 1; v < WPG; ++v) {
-                    const float4 q = rbg[v * 32 + lane];
-                    rg.x += q.x; rg.y += q.y; rg.z += q.z; rg.w += q.w;
-                }
-            }
             __syncwarp();
             if (lane == 0) mbar_arrive(rfree);
-            const int n0 = tile * QMV_ROWS + g, n1 = n0 + 8;
+            const int n0 = (GLU ? (tile >> 1) : tile) * QMV_ROWS + g, n1 = n0 + 8;
             const float vals[4] = {r.x, r.y, r.z, r.w};
-            if constexpr (GLU) {   // vals: up; gv: gate. out = silu(gate) * up, as the reference's swiglu_split
-                const float gv[4] = {rg.x, rg.y, rg.z, rg.w};
+            if constexpr (GLU) {
+                // tile pair pl of the CTA: the gate half (even local tile) hands its sums over in slot pl & 1, the up
+                // half takes them, frees the slot and writes out = silu(gate) * up (the reference's swiglu_split)
+                const int pl = tl >> 1, slot = pl & 1, su = pl >> 1;
+                float4* xs = red + 2 * QMV_NW * 32 + slot * 32;
+                if (!(tl & 1)) {
+                    if (su > 0 && !wait_parity(&gfree[slot], (su - 1) & 1)) { ok = false; break; }
+                    xs[lane] = r;
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&gfull[slot]);
+                    if (a.ys) {
 #pragma unroll
-                for (int q = 0; q < 4; ++q) {
-                    const int col = 2 * t + (q & 1);
-                    const int n = (q < 2) ? n0 : n1;
-                    if (col < cnt && n < a.N) {
-                        if (a.ys) {
-                            a.ys[(size_t)col * 2 * a.N + n] = gv[q];
-                            a.ys[(size_t)col * 2 * a.N + a.N + n] = vals[q];
+                        for (int q = 0; q < 4; ++q) {
+                            const int col = 2 * t + (q & 1);
+                            const int n = (q < 2) ? n0 : n1;
+                            if (col < cnt && n < a.N) a.ys[(size_t)col * 2 * a.N + n] = vals[q];
                         }
-                        y[(size_t)col * a.N + n] = to_out<OutT>(gv[q] / (1.f + __expf(-gv[q])) * vals[q]);
+                    }
+                } else {
+                    if (!wait_parity(&gfull[slot], su & 1)) { ok = false; break; }
+                    const float4 gg = xs[lane];
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&gfree[slot]);
+                    const float gv[4] = {gg.x, gg.y, gg.z, gg.w};
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) {
+                        const int col = 2 * t + (q & 1);
+                        const int n = (q < 2) ? n0 : n1;
+                        if (col < cnt && n < a.N) {
+                            if (a.ys) a.ys[(size_t)col * 2 * a.N + a.N + n] = vals[q];
+                            y[(size_t)col * a.N + n] = to_out<OutT>(gv[q] / (1.f + __expf(-gv[q])) * vals[q]);
+                        }
                     }
                 }
             } else {
@@ -666,7 +676,7 @@ qmv_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUten
         // next tile of this group: WG tiles further; its first iteration is (WG - 1) * nchunks stages further
         tile += WG;
         while (tile >= a.tilesN) { tile -= a.tilesN; ++sg; }
-        stg += (WG - 1) * NCH;
+        stg += (WG - 1) * a.nchunks;
         while (stg >= a.nstage) { stg -= a.nstage; ++rnd; }
     }
     // release the rest of the CTA's segments (also those this group had no tile in)

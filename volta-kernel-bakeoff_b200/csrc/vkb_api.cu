@@ -164,7 +164,6 @@ struct QmvPlan {
     QmvArgs a;
     int smem;
     int grid;
-    bool paired;   // fits the two-CTAs-per-SM budget (the next call's weight prefetch can share the SM)
 };
 
 static int round_up(int v, int m) { return (v + m - 1) / m * m; }
@@ -172,10 +171,10 @@ static int round_up(int v, int m) { return (v + m - 1) / m * m; }
 // Stage: 16 rows x KS values, up to 1.5 KB of codes per row (one TMA box each for codes and scales, rows padded so
 // the fragment reads are conflict free); ring as deep as fits, preferring a footprint that lets a second CTA (the
 // next call, under PDL) share the SM.
-// xb: bytes per staged activation (2, or 4 for fp32 activations); glu: gate/up tiles (two stage streams per tile,
-// two reduction regions).
+// glu: gate/up tile pairs over a [2N][K] table (N output rows, 2 ceil(N / 16) tiles, the gate hand-over slots after
+// the reduction region).
 static bool plan_qmv(int fmt, int N, int K, int xrows, int moe_slots, int E_local, const DeviceInfo& d, QmvPlan* p,
-                     int xb = 2, bool glu = false) {
+                     bool glu = false) {
     const int bits = fmt_bits(fmt), unit = QMV_KS_UNIT;
     static const int ks_force = getenv("VKB_QMV_KSMAX") ? atoi(getenv("VKB_QMV_KSMAX")) : 0;   // tuning override
     const int ks_max = ks_force >= unit ? ks_force : 12288 / bits;   // 1.5 KB of codes per row per stage (the
@@ -185,10 +184,10 @@ static bool plan_qmv(int fmt, int N, int K, int xrows, int moe_slots, int E_loca
     const int cpitch = KS * bits / 8 + (fmt == VKB_FMT_Q8 ? 32 : 16);
     const int spitch = KS / 16 + ((KS / 256) % 2 == 0 ? 16 : 32);   // pitch / 4 = 4 x odd: conflict-free rows
     const int stage_bytes = round_up(QMV_ROWS * (cpitch + spitch), 128);
-    const int xpitch = round_up(K * xb, 128) + 64;
+    const int xpitch = round_up(K * 2, 128) + 64;
     const int xbufs = moe_slots > 0 ? 2 : 1;
     const int xbytes = round_up(xbufs * xrows * xpitch, 16);
-    const int redbytes = 2 * QMV_NW * 32 * 16 * (glu ? 2 : 1);
+    const int redbytes = 2 * QMV_NW * 32 * 16 + (glu ? 2 * 32 * 16 : 0);
     const int moebytes = moe_slots > 0 ? round_up(4 * (3 * E_local + 2 + 2 * moe_slots), 16) : 0;
     const int slack = 1024;
     auto fixed_for = [&](int nstage) { return 8 * qmv_nbars(nstage) + xbytes + redbytes + moebytes + slack; };
@@ -202,11 +201,10 @@ static bool plan_qmv(int fmt, int N, int K, int xrows, int moe_slots, int E_loca
         if (nstage >= 3 || (pass == 1 && nstage >= 2)) break;
     }
     if (nstage < 2) return false;
-    p->paired = budget == pair_budget;
     QmvArgs& a = p->a;
     a.N = N; a.K = K; a.KS = KS; a.nchunks = nchunks; a.nstage = nstage; a.stage_bytes = stage_bytes;
     a.cpitch = cpitch; a.spitch = spitch;
-    a.xpitch = xpitch; a.xrows = xrows; a.tilesN = (N + QMV_ROWS - 1) / QMV_ROWS;
+    a.xpitch = xpitch; a.xrows = xrows; a.tilesN = (glu ? 2 : 1) * ((N + QMV_ROWS - 1) / QMV_ROWS);
     a.ring_off = 0;
     a.x_off = nstage * stage_bytes;
     a.red_off = a.x_off + xbytes;
@@ -214,7 +212,7 @@ static bool plan_qmv(int fmt, int N, int K, int xrows, int moe_slots, int E_loca
     a.moe_off = a.bar_off + 8 * qmv_nbars(nstage);
     // warp groups: as many tiles in flight as the ring allows (nstage >= wg * nchunks); MoE too (every warp passes
     // through every activation segment of its CTA in order, also those it has no tile in)
-    const int nch_tile = nchunks * (glu ? 2 : 1);   // stages per output tile
+    const int nch_tile = nchunks;   // stages per tile
     a.wg = 1;
     for (int wg = QMV_MAXWG; wg > 1; wg /= 2)
         if (nstage >= wg * nch_tile) { a.wg = wg; break; }
@@ -382,9 +380,10 @@ static int launch_f32_to_f16(const float* x, void* xh, int n, cudaStream_t st) {
 }
 
 // Q4 decode with fp32 activations (x_f32) and/or gate + up + SwiGLU over a stacked [2N][K] table (glu; ys: the
-// stacked products [M][2N] fp32, or null). fp32 activations are staged and rounded inside the decode kernel when the
-// staging fits next to the weight ring with two CTAs per SM; otherwise they are converted into xh (M x K fp16,
-// caller-owned) by one small kernel first, as the reference does. fp16 activations (x_f32 false) go straight in.
+// stacked products [M][2N] fp32, or null). The pipelined kernel reads fp32 activations itself and rounds them into
+// its fp16 buffer; shapes it does not take (K % 256 != 0, unaligned buffers) convert into xh (M x K fp16,
+// caller-owned) with one small kernel first, as the reference does, and run the general kernel (dense only: the fused
+// gate/up needs the pipelined kernel).
 static int qmv_q4_ext(const void* q, const void* s, const void* x, bool x_f32, void* xh, float* ys, void* y,
                       bool out_f32, bool glu, int N, int K, int M, cudaStream_t st) {
     if (!q || !s || !x || !y) return VKB_EINVAL;
@@ -392,26 +391,19 @@ static int qmv_q4_ext(const void* q, const void* s, const void* x, bool x_f32, v
     if (K % 32 != 0 || M > QMV_MAXTOK) return VKB_EUNSUPPORTED;
     const long long rows = glu ? 2ll * N : (long long)N;
     if (rows > (1ll << 31) - 1) return VKB_EUNSUPPORTED;
+    if (!glu && !x_f32) return qmv_dispatch(VKB_FMT_Q4, q, s, x, y, out_f32, nullptr, N, K, M, 0, 0, 0, 0, st);
     int dev = 0;
     if (int r = current_device(&dev)) return r;
     const DeviceInfo& d = device_info(dev);
-    const bool fast_w = K % 256 == 0 && aligned16(q) && aligned16(s);
-    if (!glu && !x_f32) return qmv_dispatch(VKB_FMT_Q4, q, s, x, y, out_f32, nullptr, N, K, M, 0, 0, 0, 0, st);
     QmvPlan p{};
-    bool staged_f32 = false;
-    if (x_f32 && fast_w && aligned16(x) && plan_qmv(VKB_FMT_Q4, N, K, M, 0, 0, d, &p, 4, glu) && p.paired)
-        staged_f32 = true;
-    const void* xin = x;
-    if (x_f32 && !staged_f32) {   // convert first (xh: M x K fp16, caller-owned)
+    const bool fast = K % 256 == 0 && aligned16(q) && aligned16(s) && aligned16(x) &&
+                      plan_qmv(VKB_FMT_Q4, N, K, M, 0, 0, d, &p, glu);
+    if (!fast) {
+        if (glu) return VKB_EUNSUPPORTED;   // nothing launched
         if (!xh) return VKB_EINVAL;
-        if (glu && !(fast_w && aligned16(xh))) return VKB_EUNSUPPORTED;   // before anything is launched
+        if ((reinterpret_cast<uintptr_t>(xh) & 1u) || (reinterpret_cast<uintptr_t>(x) & 3u)) return VKB_EUNSUPPORTED;
         if (int r = launch_f32_to_f16((const float*)x, xh, M * K, st)) return r;
-        xin = xh;
-        if (!glu) return qmv_dispatch(VKB_FMT_Q4, q, s, xh, y, out_f32, nullptr, N, K, M, 0, 0, 0, 0, st);
-    }
-    if (!staged_f32) {   // gate/up with fp16 activations: the pipelined kernel only
-        if (!fast_w || !aligned16(xin) || !plan_qmv(VKB_FMT_Q4, N, K, M, 0, 0, d, &p, 2, true))
-            return VKB_EUNSUPPORTED;
+        return qmv_dispatch(VKB_FMT_Q4, q, s, xh, y, out_f32, nullptr, N, K, M, 0, 0, 0, 0, st);
     }
     CUtensorMap tq, ts;
     int r = get_tmap_2d(&tq, q, (uint64_t)rows, (uint64_t)K / 2, CU_TENSOR_MAP_DATA_TYPE_UINT64, 8,
@@ -420,13 +412,14 @@ static int qmv_q4_ext(const void* q, const void* s, const void* x, bool x_f32, v
     r = get_tmap_2d(&ts, s, (uint64_t)rows, (uint64_t)K / 16, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2,
                     (uint32_t)(p.a.spitch / 2), QMV_ROWS, CU_TENSOR_MAP_SWIZZLE_NONE);
     if (r) return r;
-    p.a.x = (const __half*)xin;
+    p.a.x = (const __half*)x;
     p.a.y = y;
     p.a.ys = glu ? ys : nullptr;
     p.a.T = M;
-    const int grid = p.a.tilesN < d.sm_count ? p.a.tilesN : d.sm_count;
+    const int units = glu ? p.a.tilesN / 2 : p.a.tilesN;   // gate/up tiles go to CTAs in whole pairs
+    const int grid = units < d.sm_count ? units : d.sm_count;
     if (glu) {
-        if (staged_f32)
+        if (x_f32)
             return out_f32 ? launch_qmv<FMT_Q4, QMV_GLU, float, true>(p, tq, ts, grid, st, dev)
                            : launch_qmv<FMT_Q4, QMV_GLU, __half, true>(p, tq, ts, grid, st, dev);
         return out_f32 ? launch_qmv<FMT_Q4, QMV_GLU, float, false>(p, tq, ts, grid, st, dev)

@@ -12,8 +12,9 @@
 //   BAKEOFF_M=m          sweep one token count only
 //   BAKEOFF_CONTENDER=c  sweep the contenders whose name starts with c only (and allocate only their weights)
 //
-// Contenders: vkb_q4 / vkb_q8 / vkb_q2 (decode GEMV, 1-8 tokens), vkb_tc_q4 (prompt GEMM on tcgen05, any token
-// count), vkb_moe_q4 (MoE, one launch over a device index list), and the controls cublas_fp16 (the reference's
+// Contenders: vkb_q4 / vkb_q8 / vkb_q2 (decode GEMV, 1-8 tokens), vkb_q4_f32in (the same with fp32 activations),
+// vkb_glu_q4_f32in (gate + up + SwiGLU, fp32 activations), vkb_tc_q4 (prompt GEMM on tcgen05, any token count),
+// vkb_moe_q4 (MoE, one launch over a device index list), and the controls cublas_fp16 (the reference's
 // cublasGemmEx fp16 x fp16 -> fp32, src/bakeoff.cu:249-253) and cublas_bf16 (bf16 x bf16 -> bf16). Timing follows the
 // reference's time_us (src/bakeoff.cu:283-298: 20 warm-up calls, the median of 5 repetitions of 50 calls), with the 50
 // calls captured in a CUDA graph on a created stream so that host launch cost is not measured, and the weights
@@ -234,7 +235,9 @@ static void run_sweep() {
             const Weights w = make_weights(fmt, sh.N, sh.K, rng);
             const auto p = packed(w, false);
             Set st{fmt, p.size() + w.scale.size() * 2, 0, {}, {}};
-            if ((any_gemv && want(gname[fmt])) || (fmt == VKB_FMT_Q4 && want("vkb_tc_q4"))) st.c = copies_for(st.bytes);
+            if ((any_gemv && want(gname[fmt])) ||
+                (fmt == VKB_FMT_Q4 && (want("vkb_tc_q4") || (any_gemv && want("vkb_q4_f32in")))))
+                st.c = copies_for(st.bytes);
             for (int i = 0; i < st.c; ++i) {
                 st.q.push_back(dupload(p));
                 st.s.push_back(dupload(w.scale));
@@ -284,6 +287,14 @@ static void run_sweep() {
                                    return VK(gemv_f16(st.fmt, st.q[i % st.c], st.s[i % st.c], dx, dyh, sh.N, sh.K, M),
                                              "vkb_gemv");
                                }), st.bytes, st.c);
+            if (M <= 8 && want("vkb_q4_f32in")) {   // fp32 activations in (the reference's fused_q4_v3_fp32in row)
+                float* dxf = dupload(std::vector<float>((size_t)M * sh.K, 0.5f));
+                report("vkb_q4_f32in", time_us([&](int i) {
+                           return VK(vkb_gemv_q4_f32in(s4.q[i % s4.c], s4.s[i % s4.c], dxf, dxb, dy, sh.N, sh.K, M,
+                                                       (vkb_stream_t)g_st), "vkb_gemv_q4_f32in");
+                       }), s4.bytes, s4.c);
+                CK(cudaFree(dxf));
+            }
             CK(cudaFree(dx));
             CK(cudaFree(dxb));
             CK(cudaFree(dy));
@@ -297,6 +308,42 @@ static void run_sweep() {
         for (int i = 0; i < cf; ++i) {
             CK(cudaFree(df[i]));
             CK(cudaFree(db[i]));
+        }
+    }
+    // gate + up + SwiGLU on Qwen3-1.7B's MLP (gate and up 6144x2048 stacked), fp32 activations in, one call per
+    // step (the reference's gate_up_glu_fp32in row, src/bakeoff.cu:767-786); bytes: the stacked table
+    if ((!only || !strcmp(only, "qwen3_1p7b_mlp_gate_up")) && want("vkb_glu_q4_f32in")) {
+        const int N = 6144, K = 2048;
+        const Weights w = make_weights(VKB_FMT_Q4, 2 * N, K, rng);
+        const auto p = packed(w, false);
+        const size_t qb = p.size() + w.scale.size() * 2;
+        const int c = copies_for(qb);
+        std::vector<void*> q(c), sc(c);
+        for (int i = 0; i < c; ++i) {
+            q[i] = dupload(p);
+            sc[i] = dupload(w.scale);
+        }
+        for (int M : {1, 2, 4, 8}) {
+            if (only_m && M != only_m) continue;
+            float* dxf = dupload(std::vector<float>((size_t)M * K, 0.5f));
+            void* dxh = dalloc<uint16_t>((size_t)M * K);
+            float* dys = dalloc<float>((size_t)M * 2 * N);
+            float* dout = dalloc<float>((size_t)M * N);
+            const double us = time_us([&](int i) {
+                return VK(vkb_gate_up_glu_q4_f32in(q[i % c], sc[i % c], dxf, dxh, dys, dout, N, K, M,
+                                                   (vkb_stream_t)g_st), "vkb_gate_up_glu_q4_f32in");
+            });
+            printf("vkb_glu_q4_f32in,qwen3_1p7b_mlp_gate_up,%d,%d,%d,%.2f,%.1f,%.3f,%d\n", 2 * N, K, M, us, qb / us / 1e3,
+                   2.0 * M * 2 * N * K / us / 1e6, c);
+            fflush(stdout);
+            CK(cudaFree(dxf));
+            CK(cudaFree(dxh));
+            CK(cudaFree(dys));
+            CK(cudaFree(dout));
+        }
+        for (int i = 0; i < c; ++i) {
+            CK(cudaFree(q[i]));
+            CK(cudaFree(sc[i]));
         }
     }
     if (only || !want("vkb_moe_q4")) return;
@@ -535,14 +582,20 @@ static void check_odd_rows(bool sabotage, std::mt19937& rng) {
     for (int M : {1, 2, 3, 5, 8, 9, 100}) {
         const auto x = make_x(M, K, 0, rng);
         void* dx = dupload(x);
+        std::vector<float> xf(x.size());   // the same activations as fp32 (the fp32-in entry, src/bakeoff.cu:421-423)
+        for (size_t i = 0; i < x.size(); ++i) xf[i] = f32(x[i]);
+        float* dxf = dupload(xf);
+        void* dxh = dalloc<uint16_t>(x.size());
         const std::vector<float> init((size_t)M * N + 2 * PAD, SENT);
         float* dbuf = dupload(init);
-        for (int who = 0; who < 2; ++who) {
-            if (who == 0 && M > 8) continue;
+        for (int who = 0; who < 3; ++who) {   // decode GEMV, prompt GEMM, decode with fp32 activations
+            if (who != 1 && M > 8) continue;
             CK(cudaMemcpy(dbuf, init.data(), init.size() * 4, cudaMemcpyHostToDevice));
             const bool ran = who == 0 ? VK(gemv_f32(VKB_FMT_Q4, dq, ds, dx, dbuf + PAD, N, K, M), "vkb_gemv")
-                                      : VK(vkb_gemm_q4_tc_f32(dq, ds, dx, dbuf + PAD, N, K, M, (vkb_stream_t)g_st),
-                                           "vkb_gemm_q4_tc");
+                             : who == 1 ? VK(vkb_gemm_q4_tc_f32(dq, ds, dx, dbuf + PAD, N, K, M, (vkb_stream_t)g_st),
+                                             "vkb_gemm_q4_tc")
+                                        : VK(vkb_gemv_q4_f32in(dq, ds, dxf, dxh, dbuf + PAD, N, K, M,
+                                                               (vkb_stream_t)g_st), "vkb_gemv_q4_f32in");
             CK(cudaStreamSynchronize(g_st));
             std::vector<float> out(init.size());
             CK(cudaMemcpy(out.data(), dbuf, out.size() * 4, cudaMemcpyDeviceToHost));
@@ -556,10 +609,12 @@ static void check_odd_rows(bool sabotage, std::mt19937& rng) {
                     const double err = std::fabs(out[PAD + (size_t)m * N + n] - ref) / (mag + 1e-12);
                     if (err > r.err) { r.err = err; r.m = m; r.n = n; }
                 }
-            verdict(who == 0 ? "vkb_q4" : "vkb_tc_q4", "odd_rows_1031x2048", M, r,
-                    ran && spill == 0 && r.err <= (who == 0 ? 1e-4 : 2e-3));
+            verdict(who == 0 ? "vkb_q4" : who == 1 ? "vkb_tc_q4" : "vkb_q4_f32in", "odd_rows_1031x2048", M, r,
+                    ran && spill == 0 && r.err <= (who == 1 ? 2e-3 : 1e-4));
         }
         CK(cudaFree(dx));
+        CK(cudaFree(dxf));
+        CK(cudaFree(dxh));
         CK(cudaFree(dbuf));
     }
     {   // unsupported token count for the decode GEMV (9 > 8): returns "unsupported", writes nothing
@@ -579,6 +634,84 @@ static void check_odd_rows(bool sabotage, std::mt19937& rng) {
         CK(cudaFree(dx));
         CK(cudaFree(dy));
     }
+    {   // the same through the fp32-in entry on a big table (the reference's check, src/bakeoff.cu:448-470): nothing
+        // launched, so neither the output nor the fp16 scratch (where a conversion would land) is touched
+        const int M = 9, NB = 4096;
+        const Weights wb = make_weights(VKB_FMT_Q4, NB, K, rng);
+        void* dqb = dupload(packed(wb, sabotage));
+        void* dsb = dupload(wb.scale);
+        float* dxf = dupload(std::vector<float>((size_t)M * K, 0.5f));
+        const std::vector<uint16_t> hs((size_t)M * K, f16(-7.f));
+        void* dxh = dupload(hs);
+        const std::vector<float> init((size_t)M * NB, SENT);
+        float* dy = dupload(init);
+        const int rc = vkb_gemv_q4_f32in(dqb, dsb, dxf, dxh, dy, NB, K, M, (vkb_stream_t)g_st);
+        CK(cudaStreamSynchronize(g_st));
+        std::vector<float> out(init.size());
+        std::vector<uint16_t> hout(hs.size());
+        CK(cudaMemcpy(out.data(), dy, out.size() * 4, cudaMemcpyDeviceToHost));
+        CK(cudaMemcpy(hout.data(), dxh, hout.size() * 2, cudaMemcpyDeviceToHost));
+        bool untouched = true;
+        for (float v : out) untouched &= v == SENT;
+        for (uint16_t v : hout) untouched &= v == hs[0];
+        const bool ok = rc == VKB_EUNSUPPORTED && untouched;
+        g_failures += !ok;
+        printf("check,vkb_q4_f32in_unsupported_M,big_4096x2048,%d,0,%d,0,%s\n", M, rc, ok ? "ok" : "FAIL");
+        CK(cudaFree(dqb));
+        CK(cudaFree(dsb));
+        CK(cudaFree(dxf));
+        CK(cudaFree(dxh));
+        CK(cudaFree(dy));
+    }
+    CK(cudaFree(dq));
+    CK(cudaFree(ds));
+}
+
+// Qwen3-1.7B's MLP gate + up + SwiGLU (gate and up 6144x2048, stacked), the reference's check (src/bakeoff.cu:370-406):
+// the stacked product against the double reference on 256 sampled outputs (both halves; 1e-4 here, the exact-code
+// class -- the reference's own kernel is fp16-class, 2e-3) and out against silu(gate) * up recomputed in double from
+// that product (1e-5).
+static void check_glu(bool sabotage, std::mt19937& rng) {
+    const int N = 6144, K = 2048;
+    const Weights w = make_weights(VKB_FMT_Q4, 2 * N, K, rng);
+    void* dq = dupload(packed(w, sabotage));
+    void* ds = dupload(w.scale);
+    for (int M : {1, 2, 4, 8}) {
+        const auto x = make_x(M, K, 0, rng);
+        std::vector<float> xf(x.size());
+        for (size_t i = 0; i < x.size(); ++i) xf[i] = f32(x[i]);
+        float* dxf = dupload(xf);
+        void* dxh = dalloc<uint16_t>(x.size());
+        float* dys = dalloc<float>((size_t)M * 2 * N);
+        float* dout = dalloc<float>((size_t)M * N);
+        const bool ran = VK(vkb_gate_up_glu_q4_f32in(dq, ds, dxf, dxh, dys, dout, N, K, M, (vkb_stream_t)g_st),
+                            "vkb_gate_up_glu_q4_f32in");
+        CK(cudaStreamSynchronize(g_st));
+        std::vector<float> ys((size_t)M * 2 * N), out((size_t)M * N);
+        CK(cudaMemcpy(ys.data(), dys, ys.size() * 4, cudaMemcpyDeviceToHost));
+        CK(cudaMemcpy(out.data(), dout, out.size() * 4, cudaMemcpyDeviceToHost));
+        Worst mm, glu;
+        for (int i = 0; i < 256; ++i) {
+            const int m = (int)(rng() % (uint32_t)M), n = (int)(rng() % (uint32_t)N);
+            for (int part = 0; part < 2; ++part) {
+                const int row = n + part * N;
+                double mag;
+                const double ref = ref_dot(w, x.data() + (size_t)m * K, row, &mag);
+                const double e = std::fabs(ys[(size_t)m * 2 * N + row] - ref) / (mag + 1e-12);
+                if (e > mm.err) { mm.err = e; mm.m = m; mm.n = row; }
+            }
+            const double g = ys[(size_t)m * 2 * N + n], u = ys[(size_t)m * 2 * N + N + n];
+            const double want = g / (1.0 + std::exp(-g)) * u;
+            const double e = std::fabs(out[(size_t)m * N + n] - want) / (std::fabs(want) + 1e-6);
+            if (e > glu.err) { glu.err = e; glu.m = m; glu.n = n; }
+        }
+        verdict("vkb_glu_q4_f32in_stack", "qwen3_1p7b_mlp_gate_up", M, mm, ran && mm.err <= 1e-4);
+        verdict("vkb_glu_q4_f32in_swiglu", "qwen3_1p7b_mlp_gate_up", M, glu, ran && glu.err <= 1e-5);
+        CK(cudaFree(dxf));
+        CK(cudaFree(dxh));
+        CK(cudaFree(dys));
+        CK(cudaFree(dout));
+    }
     CK(cudaFree(dq));
     CK(cudaFree(ds));
 }
@@ -589,6 +722,7 @@ static int run_check(bool sabotage) {
     check_tables(sabotage, rng);
     check_moe(sabotage, rng);
     check_odd_rows(sabotage, rng);
+    check_glu(sabotage, rng);
     unsigned int bits = 0;
     const int rc = vkb_device_status(&bits);
     if (rc != 0 || bits != 0) {
