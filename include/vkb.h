@@ -86,6 +86,13 @@ int vkb_gate_up_glu_q4_f32in(const void* q, const void* s, const float* x, void*
 int vkb_gate_up_glu_q4(const void* q, const void* s, const void* x, float* ystack, void* out, int out_f32, int N, int K,
                        int M, vkb_stream_t stream);
 
+/* ---- GGUF Q4_0 / Q8_0 weights in device memory -> the split layout above ----------------------------------------------
+ * blocks: N * K/32 GGUF blocks (Q4_0 18 bytes, Q8_0 34 bytes; 2-byte aligned) in device memory; q (16-byte aligned)
+ * and scales receive the packed codes and fp16 scales of the formats above, bit-exactly (the host counterparts and
+ * the block layouts: vkb_host.h). One memory-bound kernel on stream. No counterpart in the reference, which states
+ * value parity with GGUF (src/bakeoff.cu:5-7) but loads no GGUF data. */
+int vkb_gguf_to_vkb_device(int fmt, const void* blocks, int N, int K, void* q, void* scales, vkb_stream_t stream);
+
 /* ---- MoE decode, one launch ----------------------------------------------------------------------------------------
  * Replaces moe_fused_q4 + MoePtrs (reference src/bakeoff.cu:157-186, :826-830), where the host picked one pointer set
  * per expert, with a device-side index list:

@@ -34,6 +34,21 @@ int vkb_f32_to_f16(const float* in, size_t n, uint16_t* out);
 /* T tokens x k distinct expert ids in [0, E) from std::mt19937(seed) (partial Fisher-Yates). */
 int vkb_synth_topk(uint32_t seed, int T, int E, int k, int32_t* idx);
 
+/* ---- GGUF interop (Q4_0 / Q8_0) -------------------------------------------------------------------------------------
+ * The reference stores its own layout but states value parity with GGUF's Q4_0 / Q8_0 (reference src/bakeoff.cu:5-7):
+ * one fp16 scale d per 32 consecutive values of a row, value = (q - 8) d (Q4_0) or q d (Q8_0). GGUF stores each
+ * block of 32 together, in row order, K / 32 blocks per row:
+ *   Q4_0  18 bytes: fp16 d, then 16 bytes qs; element j of the block in the low nibble of qs[j], element j + 16 in
+ *         the high nibble (j = 0..15), stored q = code + 8
+ *   Q8_0  34 bytes: fp16 d, then 32 int8 q
+ * These convert blocks [N][K/32] to this library's split layout (packed codes as vkb_pack writes them, scales
+ * [N][K/32]) and back, bit-exactly: the values, the scales and the codes are unchanged. K % 32 == 0. Q2 has no GGUF
+ * counterpart here (VKB_HOST_EINVAL). vkb_gguf_to_vkb_device (libvkb.so, vkb.h) does the GGUF -> split direction on
+ * the GPU for weights already in device memory. */
+size_t vkb_gguf_bytes(int fmt, int N, int K);
+int vkb_gguf_to_vkb(int fmt, const void* blocks, int N, int K, void* q, uint16_t* scales);
+int vkb_vkb_to_gguf(int fmt, const void* q, const uint16_t* scales, int N, int K, void* blocks);
+
 #ifdef __cplusplus
 }
 #endif

@@ -97,3 +97,16 @@ def test_swiglu_ref_and_glu_error():
     bad = want.copy()
     bad[1, 1] *= 1.001
     assert O.glu_error(bad, ys, 2) > 5e-4
+
+
+@pytest.mark.parametrize("fmt", [O.FMT_Q4, O.FMT_Q8])
+def test_gguf_blocks_values(fmt):
+    """The oracle's GGUF blocks encode exactly code * scale (the reference's value model, src/bakeoff.cu:5-7)."""
+    rng = np.random.default_rng(11 + fmt)
+    lo, hi = (-8, 7) if fmt == O.FMT_Q4 else (-127, 127)
+    codes = rng.integers(lo, hi + 1, size=(5, 96)).astype(np.int8)
+    scales = rng.uniform(0.004, 0.02, size=(5, 3)).astype(np.float16).view(np.uint16)
+    blocks = O.gguf_blocks(fmt, codes, scales)
+    assert blocks.size == 5 * 3 * (18 if fmt == O.FMT_Q4 else 34)
+    want = codes.astype(np.float64) * np.repeat(scales.view(np.float16).astype(np.float64), 32, axis=1)
+    assert np.array_equal(O.gguf_values(fmt, blocks, 5, 96), want)

@@ -142,3 +142,60 @@ int vkb_synth_topk(uint32_t seed, int T, int E, int k, int32_t* idx) {
 }
 
 }  // extern "C"
+
+// ---- GGUF Q4_0 / Q8_0 blocks <-> split codes + scales ---------------------------------------------------------------
+// Block layouts (GGUF's published format): Q4_0 = fp16 d + 16 bytes, element j in the low nibble of byte j and element
+// j + 16 in its high nibble, stored q = code + 8; Q8_0 = fp16 d + 32 int8. The split layout's Q4 word w of a row holds
+// elements 8w..8w+7, element i in nibble i (stored code + 8); Q8 is one int8 per element.
+
+extern "C" size_t vkb_gguf_bytes(int fmt, int N, int K) {
+    if (N < 1 || K < 32 || K % 32) return 0;
+    const size_t blocks = (size_t)N * (K / 32);
+    return fmt == VKB_FMT_Q4 ? blocks * 18 : fmt == VKB_FMT_Q8 ? blocks * 34 : 0;
+}
+
+extern "C" int vkb_gguf_to_vkb(int fmt, const void* blocks, int N, int K, void* q, uint16_t* scales) {
+    if (!blocks || !q || !scales || N < 1 || K < 32 || K % 32) return VKB_HOST_EINVAL;
+    if (fmt != VKB_FMT_Q4 && fmt != VKB_FMT_Q8) return VKB_HOST_EINVAL;
+    const size_t nb = (size_t)N * (K / 32);
+    const uint8_t* b = static_cast<const uint8_t*>(blocks);
+    const size_t bsz = fmt == VKB_FMT_Q4 ? 18 : 34;
+    for (size_t i = 0; i < nb; ++i, b += bsz) {
+        memcpy(&scales[i], b, 2);
+        if (fmt == VKB_FMT_Q4) {
+            uint8_t nib[32];
+            for (int j = 0; j < 16; ++j) {
+                nib[j] = b[2 + j] & 15u;
+                nib[j + 16] = b[2 + j] >> 4;
+            }
+            uint8_t* o = static_cast<uint8_t*>(q) + i * 16;   // 32 codes, two per byte, even element low
+            for (int j = 0; j < 16; ++j) o[j] = (uint8_t)(nib[2 * j] | (nib[2 * j + 1] << 4));
+        } else {
+            memcpy(static_cast<int8_t*>(q) + i * 32, b + 2, 32);
+        }
+    }
+    return 0;
+}
+
+extern "C" int vkb_vkb_to_gguf(int fmt, const void* q, const uint16_t* scales, int N, int K, void* blocks) {
+    if (!blocks || !q || !scales || N < 1 || K < 32 || K % 32) return VKB_HOST_EINVAL;
+    if (fmt != VKB_FMT_Q4 && fmt != VKB_FMT_Q8) return VKB_HOST_EINVAL;
+    const size_t nb = (size_t)N * (K / 32);
+    uint8_t* b = static_cast<uint8_t*>(blocks);
+    const size_t bsz = fmt == VKB_FMT_Q4 ? 18 : 34;
+    for (size_t i = 0; i < nb; ++i, b += bsz) {
+        memcpy(b, &scales[i], 2);
+        if (fmt == VKB_FMT_Q4) {
+            const uint8_t* in = static_cast<const uint8_t*>(q) + i * 16;
+            uint8_t nib[32];
+            for (int j = 0; j < 16; ++j) {
+                nib[2 * j] = in[j] & 15u;
+                nib[2 * j + 1] = in[j] >> 4;
+            }
+            for (int j = 0; j < 16; ++j) b[2 + j] = (uint8_t)(nib[j] | (nib[j + 16] << 4));
+        } else {
+            memcpy(b + 2, static_cast<const int8_t*>(q) + i * 32, 32);
+        }
+    }
+    return 0;
+}

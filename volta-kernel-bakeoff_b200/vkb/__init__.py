@@ -97,6 +97,10 @@ def _register_optional(L) -> None:
         "vkb_gemm_q4_tc_rowsplit_p2p": ([vp, vp, vp, vp, vp, i, i, i, vp], i),
         "vkb_moe_ep_p2p": ([vp, i, vp, vp, vp, i, i, vp, vp, i, i, i, i, i, vp], i),
         "vkb_gemv_q4_f32in": ([vp, vp, vp, vp, vp, i, i, i, vp], i),
+        "vkb_gguf_to_vkb_device": ([i, vp, i, i, vp, vp, vp], i),
+        "vkb_gguf_bytes": ([i, i, i], ctypes.c_size_t),
+        "vkb_gguf_to_vkb": ([i, vp, i, i, vp, vp], i),
+        "vkb_vkb_to_gguf": ([i, vp, vp, i, i, vp], i),
         "vkb_gate_up_glu_q4_f32in": ([vp, vp, vp, vp, vp, vp, i, i, i, vp], i),
         "vkb_gate_up_glu_q4": ([vp, vp, vp, vp, vp, i, i, i, i, vp], i),
         "vkb_graph_begin": ([vp], i),
@@ -253,6 +257,33 @@ def gate_up_glu_q4(q, s, x, ystack=None, out=None, out_f32: bool = True, want_st
                                       int(out.dtype == torch.float32), N, K, M, _stream(stream))
         check(rc, "vkb_gate_up_glu_q4")
     return out, ystack
+
+
+def gguf_to_vkb(fmt: int, blocks: np.ndarray, N: int, K: int) -> tuple[np.ndarray, np.ndarray]:
+    """Host: GGUF Q4_0 / Q8_0 blocks (uint8, N * K/32 blocks) -> (packed codes uint8, fp16 scale bits uint16 [N][K/32])."""
+    q = np.zeros(lib().vkb_packed_bytes(fmt, N, K), dtype=np.uint8)
+    s = np.zeros((N, K // 32), dtype=np.uint16)
+    b = np.ascontiguousarray(blocks, dtype=np.uint8)
+    check(lib().vkb_gguf_to_vkb(fmt, b.ctypes.data, N, K, q.ctypes.data, s.ctypes.data), "vkb_gguf_to_vkb")
+    return q, s
+
+
+def vkb_to_gguf(fmt: int, q: np.ndarray, s: np.ndarray, N: int, K: int) -> np.ndarray:
+    """Host: packed codes + fp16 scale bits -> GGUF Q4_0 / Q8_0 blocks (uint8)."""
+    out = np.zeros(lib().vkb_gguf_bytes(fmt, N, K), dtype=np.uint8)
+    qc, sc = np.ascontiguousarray(q), np.ascontiguousarray(s, dtype=np.uint16)
+    check(lib().vkb_vkb_to_gguf(fmt, qc.ctypes.data, sc.ctypes.data, N, K, out.ctypes.data), "vkb_vkb_to_gguf")
+    return out
+
+
+def gguf_to_vkb_device(fmt: int, blocks, N: int, K: int, stream=None):
+    """Device: GGUF blocks (a uint8 CUDA tensor) -> (packed codes, fp16 scales) CUDA tensors, one kernel."""
+    torch = _torch()
+    q = torch.empty(lib().vkb_packed_bytes(fmt, N, K), dtype=torch.uint8, device=blocks.device)
+    s = torch.empty((N, K // 32), dtype=torch.float16, device=blocks.device)
+    check(lib().vkb_gguf_to_vkb_device(fmt, _ptr(blocks), N, K, _ptr(q), _ptr(s), _stream(stream)),
+          "vkb_gguf_to_vkb_device")
+    return q, s
 
 
 def moe(fmt: int, qpool, spool, idx, x, y=None, E_local: int | None = None, e0: int = 0, out_f32: bool = False,
