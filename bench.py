@@ -62,10 +62,8 @@ def step_bytes() -> float:
 # ---- clocks ----------------------------------------------------------------------------------------------------------
 
 class ClockSampler:
-    """nvidia-smi samples of the SM clock and throttle reasons during the timed region."""
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    """nvidia-smi samples of the SM clock, clock-event reasons, utilisation, temperature and ECC during the timed
+    region, judged by vkb.load_judge (the B200 counterpart of the reference's bench/load_flag.py)."""
 
     def __init__(self, gpu_index: int):
         self.gpu = gpu_index
@@ -73,15 +71,18 @@ class ClockSampler:
         self.path = os.path.join(ROOT, "gpurun_out", f"clocks_gpu{gpu_index}.csv")
 
     def start(self):
+        from vkb import load_judge
         try:
             os.makedirs(os.path.dirname(self.path), exist_ok=True)
             self.f = open(self.path, "w")
-            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                                          "-i", str(self.gpu), "-lms", "50"], stdout=self.f, stderr=subprocess.DEVNULL)
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={load_judge.SAMPLE_FIELDS}",
+                                          "--format=csv,noheader,nounits", "-i", str(self.gpu), "-lms", "50"],
+                                         stdout=self.f, stderr=subprocess.DEVNULL)
         except (OSError, FileNotFoundError):
             self.proc = None
 
     def stop(self):
+        from vkb import load_judge
         if self.proc is None:
             return None
         time.sleep(0.06)
@@ -91,24 +92,10 @@ class ClockSampler:
         except subprocess.TimeoutExpired:
             self.proc.kill()
         self.f.close()
-        sm, mx, reasons = [], [], set()
-        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
-        for line in open(self.path):
-            f = [v.strip() for v in line.split(",")]
-            if len(f) < 9:
-                continue
-            try:
-                sm.append(float(f[1]))
-                mx.append(float(f[2]))
-            except ValueError:
-                continue
-            for n, v in zip(names, f[5:9]):
-                if v.lower() == "active":
-                    reasons.add(n)
-        if not sm:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
-        sm.sort()
-        return {"sm_mhz": sm[len(sm) // 2], "sm_max_mhz": max(mx), "reasons": sorted(reasons), "samples": len(sm)}
+        with open(self.path, encoding="utf-8", errors="replace") as fh:
+            v = load_judge.judge(fh.read())
+        return {"sm_mhz": v.median_clock, "sm_max_mhz": v.max_clock, "reasons": v.reason_names(),
+                "samples": v.busy, "flagged": v.flagged, "judge": load_judge.format_line("timed", v)}
 
 
 # ---- the reference's CPU path ----------------------------------------------------------------------------------------
