@@ -76,7 +76,7 @@ class ClockSampler:
             os.makedirs(os.path.dirname(self.path), exist_ok=True)
             self.f = open(self.path, "w")
             self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={load_judge.SAMPLE_FIELDS}",
-                                          "--format=csv,noheader,nounits", "-i", str(self.gpu), "-lms", "50"],
+                                          "--format=csv,noheader,nounits", "-i", str(self.gpu), "-lms", "20"],
                                          stdout=self.f, stderr=subprocess.DEVNULL)
         except (OSError, FileNotFoundError):
             self.proc = None
