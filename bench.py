@@ -211,14 +211,17 @@ def _copies(nbytes: int, L2: int) -> int:
 
 def prompt_section(torch, vkb, dev, stream, L2, peaks):
     """configs[4] on one GPU: the tcgen05 prompt GEMM against cuBLAS bf16 (torch.matmul, bf16 in and out) at the same
-    shapes, weights cycled over >= 4x L2 for both."""
+    shapes, weights cycled over >= 4x L2 for both; the same shapes with Q8 weights (the Q8 prompt kernel, SURVEY
+    8(f)) as q8_* entries."""
     out = {}
     for N, K in PROMPT_SHAPES:
-        codes, scales = vkb.quantize(0, vkb.synth_normal(0, (N, K), 0.02))
-        q0 = vkb.to_device_packed(vkb.pack(0, codes), dev)
-        s0 = vkb.to_device_f16(scales, dev)
-        nq = _copies(q0.numel() + 2 * s0.numel(), L2)
-        ql, sl = [q0] + [q0.clone() for _ in range(nq - 1)], [s0] + [s0.clone() for _ in range(nq - 1)]
+        sets = {}
+        for fmt in (0, 1):
+            codes, scales = vkb.quantize(fmt, vkb.synth_normal(0, (N, K), 0.02))
+            q0 = vkb.to_device_packed(vkb.pack(fmt, codes), dev)
+            s0 = vkb.to_device_f16(scales, dev)
+            nq = _copies(q0.numel() * q0.element_size() + 2 * s0.numel(), L2)
+            sets[fmt] = ([q0] + [q0.clone() for _ in range(nq - 1)], [s0] + [s0.clone() for _ in range(nq - 1)], nq)
         wb = torch.randn(N, K, device=dev, dtype=torch.bfloat16) * 0.02
         nb = _copies(wb.numel() * 2, L2)
         wl = [wb] + [wb.clone() for _ in range(nb - 1)]
@@ -227,14 +230,16 @@ def prompt_section(torch, vkb, dev, stream, L2, peaks):
             xb = x.to(torch.bfloat16)
             y = torch.empty((M, N), dtype=torch.float16, device=dev)
             yb = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
-            us = _median_us(torch, stream, lambda i: vkb.gemm_tc(ql[i % nq], sl[i % nq], x, y=y))
             us_b = _median_us(torch, stream, lambda i: torch.matmul(xb, wl[i % nb].t(), out=yb), vkb_graph=False)
             fl = 2.0 * M * N * K
-            out[f"q4_{N}x{K}_m{M}"] = {
-                "us": round(us, 2), "tflops": round(fl / us / 1e6, 1), "cublas_bf16_us": round(us_b, 2),
-                "cublas_bf16_tflops": round(fl / us_b / 1e6, 1), "time_vs_cublas_bf16": round(us_b / us, 3),
-                "frac_of_bf16_peak": round(fl / us / 1e6 / float(peaks.get("bf16_tflops", 1590.0)), 3)}
-        del ql, sl, wl
+            for fmt, tag in ((0, "q4"), (1, "q8")):
+                ql, sl, nq = sets[fmt]
+                us = _median_us(torch, stream, lambda i: vkb.gemm_tc(ql[i % nq], sl[i % nq], x, y=y, fmt=fmt))
+                out[f"{tag}_{N}x{K}_m{M}"] = {
+                    "us": round(us, 2), "tflops": round(fl / us / 1e6, 1), "cublas_bf16_us": round(us_b, 2),
+                    "cublas_bf16_tflops": round(fl / us_b / 1e6, 1), "time_vs_cublas_bf16": round(us_b / us, 3),
+                    "frac_of_bf16_peak": round(fl / us / 1e6 / float(peaks.get("bf16_tflops", 1590.0)), 3)}
+        del sets, wl
     return out
 
 

@@ -115,6 +115,15 @@ int vkb_gemm_q4_tc(const void* q, const void* s, const void* x, void* y, int N, 
 int vkb_gemm_q4_tc_f32(const void* q, const void* s, const void* x, float* y, int N, int K, int M,
                        vkb_stream_t stream);
 
+/* Q8 weights (int8 codes [N][K], scales [N][K/32]) on the same tcgen05 kernel: the tc_q8 the reference planned but
+ * never built (its STAGE3.md). Weights are rounded to fp16 as code * scale (one rounding), as in the Q4 kernel (fp16
+ * class). Same shapes and alignment rules as vkb_gemm_q4_tc. vkb_gemm_tc takes the format at run time (Q4 or Q8). */
+int vkb_gemm_q8_tc(const void* q, const void* s, const void* x, void* y, int N, int K, int M, vkb_stream_t stream);
+int vkb_gemm_q8_tc_f32(const void* q, const void* s, const void* x, float* y, int N, int K, int M,
+                       vkb_stream_t stream);
+int vkb_gemm_tc(int fmt, const void* q, const void* s, const void* x, void* y, int out_f32, int N, int K, int M,
+                vkb_stream_t stream);
+
 /* ---- multi-GPU: one process (and one rank) per GPU ---------------------------------------------------------------------
  * No counterpart in the reference, which runs on one GPU: these shard the MoE (by experts) and the prompt GEMM (by
  * weight rows) over the GPUs of one node. A communicator wraps one NCCL rank on the device that is current at vkb_comm_init. Collective entry points must be

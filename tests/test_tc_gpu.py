@@ -123,3 +123,26 @@ def test_tc_pair_kernel_opt_in(cuda):
     assert r.returncode == 0, r.stderr[-2000:]
     line = [l for l in r.stdout.splitlines() if l.startswith("WORST")][-1].split()
     assert float(line[1]) < 1e-5 and int(line[3]) == 0, line
+
+
+@pytest.mark.parametrize("N,K,M", [(512, 256, 16), (1031, 768, 65), (2048, 2048, 511), (12288, 2560, 512),
+                                   (8192, 2048, 64)])
+def test_tc_q8_vs_torch_fp32_and_oracle(cuda, N, K, M):
+    """The Q8 prompt GEMM (vkb_gemm_tc with Q8 weights): against torch fp32 over the fp16-rounded weights (tight) and
+    the CPU oracle of the exact codes with the fp16-class tolerance."""
+    import torch
+    rng = np.random.default_rng(3 * N + K + M)
+    codes, scales = random_codes(rng, O.FMT_Q8, N, K)
+    q, s = device_weights(O.FMT_Q8, codes, scales)
+    x = uniform_x(rng, M, K)
+    y = vkb.gemm_tc(q, s, vkb.to_device_f16(x), out_f32=True, fmt=O.FMT_Q8)
+    yh = vkb.gemm_tc(q, s, vkb.to_device_f16(x), out_f32=False, fmt=O.FMT_Q8)
+    torch.cuda.synchronize()
+    ref = _torch_ref(codes, scales, x)
+    assert ((y - ref).abs().max() / (ref.abs().max() + 1e-12)).item() < 1e-5
+    if N * K <= 2048 * 2048:
+        yo = y.cpu().numpy().astype(np.float64)
+        err = O.check_error(yo, O.ref_value(codes, scales, x), O.ref_scale(codes, scales, x))[0]
+        assert err <= O.TOL_FP16, err
+    assert torch.equal(yh, y.half())
+    assert vkb.device_status() == 0

@@ -50,8 +50,10 @@ constexpr int TC_THREADS = 32 * (TC_WEPI0 + TC_NEPI);
 
 // A packed chunk holds PK K steps (4 or 8): 128 rows of 32 PK code bytes at a pitch of 32 PK + 16 (pitch / 16 odd:
 // the dequantising warps' 16-byte reads are conflict free), then 128 rows of scales at TC_SPITCH.
-__host__ __device__ constexpr int tc_ppitch(int pk) { return 32 * pk + 16; }
-__host__ __device__ constexpr int tc_pchunk(int pk) { return TC_BM * (tc_ppitch(pk) + TC_SPITCH); }
+// Q8 weights (wf = 1) take 64 code bytes per K step instead of 32: pitch 64 PK + 16 (again an odd number of 16-byte
+// units).
+__host__ __device__ constexpr int tc_ppitch(int pk, int wf = 0) { return (wf == 1 ? 64 : 32) * pk + 16; }
+__host__ __device__ constexpr int tc_pchunk(int pk, int wf = 0) { return TC_BM * (tc_ppitch(pk, wf) + TC_SPITCH); }
 
 struct TcArgs {
     void* y;            // [M][ldy], this call's columns from ycol0
@@ -246,6 +248,17 @@ __device__ __forceinline__ void dequant8_to(uint32_t v, uint32_t s2, uint32_t* r
     }
 }
 
+// One Q8 word (4 int8 codes of one row, natural k order) -> 4 fp16 weights code * scale in two registers: the exact
+// code through the offset-binary magic number ((0x6400 | (code + 128)) - 1152), then one fp16 rounding of code * scale
+// (the rounding the Q4 kernel applies, so the prompt GEMM stays in the reference's fp16 class).
+__device__ __forceinline__ void dequant4_q8_to(uint32_t v, uint32_t s2, uint32_t* r) {
+    const uint32_t u = v ^ 0x80808080u;
+    const uint32_t c01 = h2_sub(prmt(u, 0x64646464u, 0x4140u), 0x64806480u);   // exact (c0, c1)
+    const uint32_t c23 = h2_sub(prmt(u, 0x64646464u, 0x4342u), 0x64806480u);   // exact (c2, c3)
+    asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(r[0]) : "r"(c01), "r"(s2));
+    asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(r[1]) : "r"(c23), "r"(s2));
+}
+
 template <typename OutT> __device__ __forceinline__ OutT tc_out(float v);
 template <> __device__ __forceinline__ __half tc_out<__half>(float v) { return __float2half_rn(v); }
 template <> __device__ __forceinline__ float tc_out<float>(float v) { return v; }
@@ -267,12 +280,16 @@ __device__ __noinline__ void tc_push_tile(const TcArgs& a, int row0, int tok0, i
 // streams half of the activations it would stream alone: the shared-memory traffic per MMA halves. The leader's
 // barriers count both CTAs (the peer's dequantising and epilogue warps arrive remotely, the peer's activation loads
 // complete on the leader's barrier); the leader's commits arrive on both CTAs' barriers. No TMA multicast.
-template <typename OutT, int PK, bool P2P, int CG>
+// WF: weight format, 0 = Q4 (the reference's tc_q4), 1 = Q8 (the tc_q8 it planned, SURVEY's next rows): only the packed
+// chunk layout and the dequantisation differ.
+template <typename OutT, int PK, bool P2P, int CG, int WF = 0>
 __global__ void __launch_bounds__(TC_THREADS, 1)
 tc_q4_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap ts,
              const __grid_constant__ CUtensorMap tx, const __grid_constant__ TcArgs a) {
     static_assert(CG == 1 || (CG == 2 && !P2P), "peer stores use the one-CTA kernel");
-    constexpr int PPITCH = tc_ppitch(PK), PCHUNK = tc_pchunk(PK), SCOFF = TC_BM * PPITCH;
+    static_assert(WF == 0 || (WF == 1 && !P2P && CG == 1), "Q8 weights: the one-CTA kernel without peer stores");
+    constexpr int PPITCH = tc_ppitch(PK, WF), PCHUNK = tc_pchunk(PK, WF), SCOFF = TC_BM * PPITCH;
+    constexpr int KSB = WF == 1 ? 64 : 32;   // code bytes per row per K step
     extern __shared__ uint8_t smem_raw[];
     const uint32_t pad = (1024u - (smem_u32(smem_raw) & 1023u)) & 1023u;
     uint8_t* sm = smem_raw + pad;
@@ -320,7 +337,7 @@ tc_q4_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUt
         const int t = tile_of(g / nch), c = g % nch;
         uint8_t* dst = sm + a.p_off + b * PCHUNK;
         mbar_arrive_expect_tx(&pfull[b], (uint32_t)PCHUNK);
-        tma_load_2d(dst, &tq, c * PK * 4, row0_of(t), &pfull[b]);                // PK x 4 x 8 B of codes
+        tma_load_2d(dst, &tq, c * PK * (KSB / 8), row0_of(t), &pfull[b]);        // PK K steps of codes, 8-B units
         tma_load_2d(dst + SCOFF, &ts, c * PK * 2, row0_of(t), &pfull[b]);         // 2 PK (+ pad) fp16 scales
     };
 
@@ -515,33 +532,59 @@ tc_q4_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUt
                 const int ab = sl % a.na;
                 // this group's two K steps of the slot: both loads first, then both conversions, one TMEM store
                 const int sub0 = sc * TC_SLOT + 2 * grp;            // first of the two sub-steps within the chunk
-                const uint32_t pa = prow + pb * PCHUNK + sub0 * 32;
-                const uint4 w0 = lds128(pa), w1 = lds128(pa + 16), w2 = lds128(pa + 32), w3 = lds128(pa + 48);
+                const uint32_t pa = prow + pb * PCHUNK + sub0 * KSB;
+                uint4 w0 = lds128(pa), w1 = lds128(pa + 16), w2 = lds128(pa + 32), w3 = lds128(pa + 48);
                 const uint32_t sa = grp ? sw[sc * TC_SLOT + 2] : sw[sc * TC_SLOT];       // static indices
                 const uint32_t sb = grp ? sw[sc * TC_SLOT + 3] : sw[sc * TC_SLOT + 1];
-                if (sc == PK / TC_SLOT - 1) {                       // this warp's last read of the chunk
+                if (WF == 0 && sc == PK / TC_SLOT - 1) {            // this warp's last read of the chunk
                     __syncwarp();
                     if (lane == 0) mbar_arrive(&pempty[pb]);
                 }
                 uint32_t v[64];
                 const uint32_t a_lo = (sa & 0xFFFFu) * 0x00010001u, a_hi = (sa >> 16) * 0x00010001u;
                 const uint32_t b_lo = (sb & 0xFFFFu) * 0x00010001u, b_hi = (sb >> 16) * 0x00010001u;
-                dequant8_to(w0.x, a_lo, v + 0);
-                dequant8_to(w0.y, a_lo, v + 4);
-                dequant8_to(w0.z, a_lo, v + 8);
-                dequant8_to(w0.w, a_lo, v + 12);
-                dequant8_to(w1.x, a_hi, v + 16);
-                dequant8_to(w1.y, a_hi, v + 20);
-                dequant8_to(w1.z, a_hi, v + 24);
-                dequant8_to(w1.w, a_hi, v + 28);
-                dequant8_to(w2.x, b_lo, v + 32);
-                dequant8_to(w2.y, b_lo, v + 36);
-                dequant8_to(w2.z, b_lo, v + 40);
-                dequant8_to(w2.w, b_lo, v + 44);
-                dequant8_to(w3.x, b_hi, v + 48);
-                dequant8_to(w3.y, b_hi, v + 52);
-                dequant8_to(w3.z, b_hi, v + 56);
-                dequant8_to(w3.w, b_hi, v + 60);
+                if constexpr (WF == 0) {   // Q4: 32 code bytes per K step (w0-w1: step A, w2-w3: step B)
+                    dequant8_to(w0.x, a_lo, v + 0);
+                    dequant8_to(w0.y, a_lo, v + 4);
+                    dequant8_to(w0.z, a_lo, v + 8);
+                    dequant8_to(w0.w, a_lo, v + 12);
+                    dequant8_to(w1.x, a_hi, v + 16);
+                    dequant8_to(w1.y, a_hi, v + 20);
+                    dequant8_to(w1.z, a_hi, v + 24);
+                    dequant8_to(w1.w, a_hi, v + 28);
+                    dequant8_to(w2.x, b_lo, v + 32);
+                    dequant8_to(w2.y, b_lo, v + 36);
+                    dequant8_to(w2.z, b_lo, v + 40);
+                    dequant8_to(w2.w, b_lo, v + 44);
+                    dequant8_to(w3.x, b_hi, v + 48);
+                    dequant8_to(w3.y, b_hi, v + 52);
+                    dequant8_to(w3.z, b_hi, v + 56);
+                    dequant8_to(w3.w, b_hi, v + 60);
+                } else {   // Q8: 64 code bytes per K step; w0-w3 hold step A, step B is loaded after A is converted
+                    const uint4 wa[4] = {w0, w1, w2, w3};
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {   // 16 codes per uint4: groups of 32 = two uint4
+                        const uint32_t s2 = i < 2 ? a_lo : a_hi;
+                        dequant4_q8_to(wa[i].x, s2, v + 8 * i);
+                        dequant4_q8_to(wa[i].y, s2, v + 8 * i + 2);
+                        dequant4_q8_to(wa[i].z, s2, v + 8 * i + 4);
+                        dequant4_q8_to(wa[i].w, s2, v + 8 * i + 6);
+                    }
+                    w0 = lds128(pa + 64); w1 = lds128(pa + 80); w2 = lds128(pa + 96); w3 = lds128(pa + 112);
+                    const uint4 wb[4] = {w0, w1, w2, w3};
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        const uint32_t s2 = i < 2 ? b_lo : b_hi;
+                        dequant4_q8_to(wb[i].x, s2, v + 32 + 8 * i);
+                        dequant4_q8_to(wb[i].y, s2, v + 32 + 8 * i + 2);
+                        dequant4_q8_to(wb[i].z, s2, v + 32 + 8 * i + 4);
+                        dequant4_q8_to(wb[i].w, s2, v + 32 + 8 * i + 6);
+                    }
+                    if (sc == PK / TC_SLOT - 1) {                   // this warp's last read of the chunk
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(&pempty[pb]);
+                    }
+                }
                 if (sl >= a.na && !wait_b(&aempty[ab], ((sl / a.na) - 1) & 1)) { ok = false; break; }
                 tc_fence_after();                                   // the slot's previous MMAs are done
                 tmem_st64(tlane + (uint32_t)(ab * TC_SLOT * TC_ACOLS), v);

@@ -458,7 +458,8 @@ struct TcPlan {
 // 32 KB (an even count: two producers), P chunks of 8 K steps when they fit (else 4), both deepened while shared
 // memory lasts. With cg = 2 the units are CTA pairs (at most `units_max` co-resident), a tile has 256 rows and each
 // CTA's X stages hold half of the tile's tokens.
-static bool plan_tc(int N, int K, int M, int out_bytes, const DeviceInfo& d, TcPlan* p, int cg, int units_max) {
+static bool plan_tc(int N, int K, int M, int out_bytes, const DeviceInfo& d, TcPlan* p, int cg, int units_max,
+                    int wf = 0) {
     TcArgs& a = p->a;
     const int tiles_n = (N + TC_BM * cg - 1) / (TC_BM * cg);
     const int nk = K / TC_BK;
@@ -489,7 +490,7 @@ static bool plan_tc(int N, int K, int M, int out_bytes, const DeviceInfo& d, TcP
     (void)out_bytes;
     for (int pk : {8, 4}) {
         if (nk % pk != 0) continue;
-        const int pchunk = tc_pchunk(pk);
+        const int pchunk = tc_pchunk(pk, wf);
         int nx = 4, np = 2;   // four X stages first: the activations are the fast-consumed stream
         auto bars_bytes = [&]() { return 8 * (2 * np + 2 * nx + 2 * a.na + 2 * a.nacc) + 16; };
         auto total = [&]() { return nx * xk * (NT / cg) * 128 + np * pchunk + bars_bytes() + 1024; };
@@ -517,13 +518,13 @@ static bool plan_tc(int N, int K, int M, int out_bytes, const DeviceInfo& d, TcP
 }
 
 // Opt one prompt-GEMM kernel variant into the device's shared memory, once per device.
-template <typename OutT, int PK, bool P2P, int CG>
+template <typename OutT, int PK, bool P2P, int CG, int WF = 0>
 static int tc_attr(int dev, int smem_optin) {
     static std::once_flag once[kMaxDevices];
     static cudaError_t err[kMaxDevices];
     std::call_once(once[dev], [&] {
-        err[dev] = cudaFuncSetAttribute(tc_q4_kernel<OutT, PK, P2P, CG>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                        smem_optin);
+        err[dev] = cudaFuncSetAttribute(tc_q4_kernel<OutT, PK, P2P, CG, WF>,
+                                        cudaFuncAttributeMaxDynamicSharedMemorySize, smem_optin);
     });
     return err[dev] == cudaSuccess ? 0 : -(int)err[dev];
 }
@@ -557,9 +558,10 @@ static int tc_max_pairs(int dev, int smem) {
 
 template <typename OutT>
 static int tc_entry(const void* q, const void* s, const void* x, void* y, int N, int K, int M, cudaStream_t st,
-                    const TcOut* out = nullptr) {
+                    const TcOut* out = nullptr, int wf = 0) {
     if (!q || !s || !x || !y) return VKB_EINVAL;
     if (N < 1 || M < 1 || K < 256) return VKB_EINVAL;
+    if (wf == 1 && out && out->p2p) return VKB_EUNSUPPORTED;   // peer stores: Q4 weights only
     if (K % 256 != 0) return VKB_EUNSUPPORTED;
     if (!aligned16(q) || !aligned16(s) || !aligned16(x)) return VKB_EUNSUPPORTED;
     int dev = 0;
@@ -570,7 +572,7 @@ static int tc_entry(const void* q, const void* s, const void* x, void* y, int N,
     // activations) is correct but measured slower on B200 at every shape of the sweep (12288x2560 M=512: 38.8 vs
     // 34.6 us; 8192x2048 M=64: 13.8 vs 10.6 us): VKB_TC_CG=2 selects it for experiments.
     static const int cg_force = getenv("VKB_TC_CG") ? atoi(getenv("VKB_TC_CG")) : 0;   // tuning override
-    int cg = cg_force == 2 && N >= 2 * TC_BM ? 2 : 1;
+    int cg = cg_force == 2 && N >= 2 * TC_BM && wf == 0 ? 2 : 1;
     if (out && out->p2p) cg = 1;
     int units_max = d.sm_count;
     if (cg == 2) {
@@ -578,7 +580,7 @@ static int tc_entry(const void* q, const void* s, const void* x, void* y, int N,
         if (units_max < 1) cg = 1, units_max = d.sm_count;
     }
     TcPlan p{};
-    if (!plan_tc(N, K, M, (int)sizeof(OutT), d, &p, cg, units_max)) return VKB_EUNSUPPORTED;
+    if (!plan_tc(N, K, M, (int)sizeof(OutT), d, &p, cg, units_max, wf)) return VKB_EUNSUPPORTED;
     p.a.y = y;
     p.a.ldy = out ? out->ldy : N;
     p.a.ycol0 = out ? out->col0 : 0;
@@ -586,8 +588,8 @@ static int tc_entry(const void* q, const void* s, const void* x, void* y, int N,
     if (p.a.p2p) p.a.pp = *out->p2p;
     if (p.a.p2p && p.grid.x > (unsigned)P2P_MAX_CTAS) return VKB_EUNSUPPORTED;   // one flag pair per CTA
     CUtensorMap tq, ts, tx;
-    int r = get_tmap_2d(&tq, q, (uint64_t)N, (uint64_t)K / 2, CU_TENSOR_MAP_DATA_TYPE_UINT64, 8,
-                        (uint32_t)tc_ppitch(p.pk) / 8, TC_BM, CU_TENSOR_MAP_SWIZZLE_NONE);
+    int r = get_tmap_2d(&tq, q, (uint64_t)N, (uint64_t)(wf == 1 ? K : K / 2), CU_TENSOR_MAP_DATA_TYPE_UINT64, 8,
+                        (uint32_t)tc_ppitch(p.pk, wf) / 8, TC_BM, CU_TENSOR_MAP_SWIZZLE_NONE);
     if (r) return r;
     r = get_tmap_2d(&ts, s, (uint64_t)N, (uint64_t)K / 16, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, TC_SPITCH / 2, TC_BM,
                     CU_TENSOR_MAP_SWIZZLE_NONE);
@@ -604,6 +606,10 @@ static int tc_entry(const void* q, const void* s, const void* x, void* y, int N,
         } else {
             return VKB_EUNSUPPORTED;
         }
+    } else if (wf == 1) {   // Q8 weights
+        kern = p.pk == 8 ? tc_q4_kernel<OutT, 8, false, 1, 1> : tc_q4_kernel<OutT, 4, false, 1, 1>;
+        ra = p.pk == 8 ? tc_attr<OutT, 8, false, 1, 1>(dev, d.smem_optin)
+                       : tc_attr<OutT, 4, false, 1, 1>(dev, d.smem_optin);
     } else if (p.cg == 2) {
         kern = p.pk == 8 ? tc_q4_kernel<OutT, 8, false, 2> : tc_q4_kernel<OutT, 4, false, 2>;
         ra = p.pk == 8 ? tc_attr<OutT, 8, false, 2>(dev, d.smem_optin) : tc_attr<OutT, 4, false, 2>(dev, d.smem_optin);
@@ -638,8 +644,8 @@ static int tc_entry(const void* q, const void* s, const void* x, void* y, int N,
 }
 
 int tc_dispatch(const void* q, const void* s, const void* x, void* y, bool f32, int N, int K, int M, cudaStream_t st,
-                const TcOut* out) {
-    return f32 ? tc_entry<float>(q, s, x, y, N, K, M, st, out) : tc_entry<__half>(q, s, x, y, N, K, M, st, out);
+                const TcOut* out, int wf) {
+    return f32 ? tc_entry<float>(q, s, x, y, N, K, M, st, out, wf) : tc_entry<__half>(q, s, x, y, N, K, M, st, out, wf);
 }
 
 }  // namespace vkb
@@ -703,6 +709,18 @@ int vkb_gemm_q4_tc(const void* q, const void* s, const void* x, void* y, int N, 
 int vkb_gemm_q4_tc_f32(const void* q, const void* s, const void* x, float* y, int N, int K, int M,
                        vkb_stream_t stream) {
     return tc_entry<float>(q, s, x, y, N, K, M, (cudaStream_t)stream);
+}
+int vkb_gemm_q8_tc(const void* q, const void* s, const void* x, void* y, int N, int K, int M, vkb_stream_t stream) {
+    return tc_entry<__half>(q, s, x, y, N, K, M, (cudaStream_t)stream, nullptr, 1);
+}
+int vkb_gemm_q8_tc_f32(const void* q, const void* s, const void* x, float* y, int N, int K, int M,
+                       vkb_stream_t stream) {
+    return tc_entry<float>(q, s, x, y, N, K, M, (cudaStream_t)stream, nullptr, 1);
+}
+int vkb_gemm_tc(int fmt, const void* q, const void* s, const void* x, void* y, int out_f32, int N, int K, int M,
+                vkb_stream_t stream) {
+    if (fmt != VKB_FMT_Q4 && fmt != VKB_FMT_Q8) return VKB_EUNSUPPORTED;
+    return tc_dispatch(q, s, x, y, out_f32 != 0, N, K, M, (cudaStream_t)stream, nullptr, fmt == VKB_FMT_Q8 ? 1 : 0);
 }
 
 int vkb_graph_begin(vkb_stream_t stream) {

@@ -38,8 +38,9 @@ struct TcOut {
     int ldy, col0;
     const P2PArgs* p2p;
 };
+// wf: weight format of the prompt GEMM (0 = Q4, 1 = Q8).
 int tc_dispatch(const void* q, const void* s, const void* x, void* y, bool f32, int N, int K, int M, cudaStream_t st,
-                const TcOut* out = nullptr);
+                const TcOut* out = nullptr, int wf = 0);
 bool pdl_stream_ok(cudaStream_t st);
 
 // Host accessors of the per-translation-unit device status words (read and clear, OR into *bits).

@@ -13,7 +13,8 @@
 //   BAKEOFF_CONTENDER=c  sweep the contenders whose name starts with c only (and allocate only their weights)
 //
 // Contenders: vkb_q4 / vkb_q8 / vkb_q2 (decode GEMV, 1-8 tokens), vkb_q4_f32in (the same with fp32 activations),
-// vkb_glu_q4_f32in (gate + up + SwiGLU, fp32 activations), vkb_tc_q4 (prompt GEMM on tcgen05, any token count),
+// vkb_glu_q4_f32in (gate + up + SwiGLU, fp32 activations), vkb_tc_q4 / vkb_tc_q8 (prompt GEMM on tcgen05, Q4 or Q8
+// weights, any token count),
 // vkb_moe_q4 (MoE, one launch over a device index list), and the controls cublas_fp16 (the reference's
 // cublasGemmEx fp16 x fp16 -> fp32, src/bakeoff.cu:249-253) and cublas_bf16 (bf16 x bf16 -> bf16). Timing follows the
 // reference's time_us (src/bakeoff.cu:283-298: 20 warm-up calls, the median of 5 repetitions of 50 calls), with the 50
@@ -236,7 +237,8 @@ static void run_sweep() {
             const auto p = packed(w, false);
             Set st{fmt, p.size() + w.scale.size() * 2, 0, {}, {}};
             if ((any_gemv && want(gname[fmt])) ||
-                (fmt == VKB_FMT_Q4 && (want("vkb_tc_q4") || (any_gemv && want("vkb_q4_f32in")))))
+                (fmt == VKB_FMT_Q4 && (want("vkb_tc_q4") || (any_gemv && want("vkb_q4_f32in")))) ||
+                (fmt == VKB_FMT_Q8 && want("vkb_tc_q8")))
                 st.c = copies_for(st.bytes);
             for (int i = 0; i < st.c; ++i) {
                 st.q.push_back(dupload(p));
@@ -280,6 +282,12 @@ static void run_sweep() {
                            return VK(vkb_gemm_q4_tc(s4.q[i % s4.c], s4.s[i % s4.c], dx, dyh, sh.N, sh.K, M,
                                                     (vkb_stream_t)g_st), "vkb_gemm_q4_tc");
                        }), s4.bytes, s4.c);
+            const Set& s8 = sets[1];
+            if (want("vkb_tc_q8"))
+                report("vkb_tc_q8", time_us([&](int i) {
+                           return VK(vkb_gemm_q8_tc(s8.q[i % s8.c], s8.s[i % s8.c], dx, dyh, sh.N, sh.K, M,
+                                                    (vkb_stream_t)g_st), "vkb_gemm_q8_tc");
+                       }), s8.bytes, s8.c);
             if (M <= 8)
                 for (const Set& st : sets)
                     if (want(gname[st.fmt]))
@@ -476,7 +484,7 @@ static void check_tables(bool sabotage, std::mt19937& rng) {
             struct XCase { int M, kind; };
             std::vector<XCase> xcases;
             for (int M : {1, 2, 4, 8}) xcases.push_back({M, 0});
-            if (fmt == VKB_FMT_Q4)
+            if (fmt != VKB_FMT_Q2)   // prompt GEMM: Q4 and Q8 weights
                 for (int M : {64, 65, 128, 256, 512}) xcases.push_back({M, 0});
             for (int M : {1, 2, 4, 8}) {
                 xcases.push_back({M, 1});
@@ -511,6 +519,12 @@ static void check_tables(bool sabotage, std::mt19937& rng) {
                     check_one("cublas_fp16", label, w, x, M, true, 2e-3, [&](void* y) {   // the control
                         cublas_f16(dwf, dx, (float*)y, sh.N, sh.K, M);
                         return true;
+                    }, rng);
+                }
+                if (fmt == VKB_FMT_Q8 && xc.kind != 1) {   // the Q8 prompt GEMM (tc_q8, planned by the reference)
+                    check_one("vkb_tc_q8", label, w, x, M, true, 2e-3, [&](void* y) {
+                        return VK(vkb_gemm_q8_tc_f32(dq, ds, dx, (float*)y, sh.N, sh.K, M, (vkb_stream_t)g_st),
+                                  "vkb_gemm_q8_tc");
                     }, rng);
                 }
                 CK(cudaFree(dx));

@@ -97,6 +97,9 @@ def _register_optional(L) -> None:
         "vkb_gemm_q4_tc_rowsplit_p2p": ([vp, vp, vp, vp, vp, i, i, i, vp], i),
         "vkb_moe_ep_p2p": ([vp, i, vp, vp, vp, i, i, vp, vp, i, i, i, i, i, vp], i),
         "vkb_gemv_q4_f32in": ([vp, vp, vp, vp, vp, i, i, i, vp], i),
+        "vkb_gemm_tc": ([i, vp, vp, vp, vp, i, i, i, i, vp], i),
+        "vkb_gemm_q8_tc": ([vp, vp, vp, vp, i, i, i, vp], i),
+        "vkb_gemm_q8_tc_f32": ([vp, vp, vp, vp, i, i, i, vp], i),
         "vkb_gguf_to_vkb_device": ([i, vp, i, i, vp, vp, vp], i),
         "vkb_gguf_bytes": ([i, i, i], ctypes.c_size_t),
         "vkb_gguf_to_vkb": ([i, vp, i, i, vp, vp], i),
@@ -302,16 +305,20 @@ def moe(fmt: int, qpool, spool, idx, x, y=None, E_local: int | None = None, e0: 
     return y
 
 
-def gemm_tc(q, s, x, y=None, out_f32: bool = False, stream=None):
-    """Prompt GEMM on tcgen05 (Q4): y[M][N] = x[M][K] . W[N][K]^T for any M. q: packed Q4 codes, s: fp16 [N][K/32],
-    x: fp16 [M][K]. Returns y (fp16, or fp32 with out_f32)."""
+def gemm_tc(q, s, x, y=None, out_f32: bool = False, stream=None, fmt: int = FMT_Q4):
+    """Prompt GEMM on tcgen05: y[M][N] = x[M][K] . W[N][K]^T for any M. q: packed Q4 codes (or int8 Q8 codes with
+    fmt=FMT_Q8), s: fp16 [N][K/32], x: fp16 [M][K]. Returns y (fp16, or fp32 with out_f32)."""
     torch = _torch()
     M, K = x.shape
     N = s.shape[0]
     if y is None:
         y = torch.empty((M, N), dtype=torch.float32 if out_f32 else torch.float16, device=x.device)
-    fn = lib().vkb_gemm_q4_tc_f32 if out_f32 else lib().vkb_gemm_q4_tc
-    check(fn(_ptr(q), _ptr(s), _ptr(x), _ptr(y), N, K, M, _stream(stream)), "vkb_gemm_q4_tc")
+    if fmt == FMT_Q4:
+        fn = lib().vkb_gemm_q4_tc_f32 if out_f32 else lib().vkb_gemm_q4_tc
+        check(fn(_ptr(q), _ptr(s), _ptr(x), _ptr(y), N, K, M, _stream(stream)), "vkb_gemm_q4_tc")
+    else:
+        check(lib().vkb_gemm_tc(fmt, _ptr(q), _ptr(s), _ptr(x), _ptr(y), int(out_f32), N, K, M, _stream(stream)),
+              "vkb_gemm_tc")
     return y
 
 
