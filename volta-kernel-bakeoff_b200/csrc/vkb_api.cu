@@ -488,8 +488,12 @@ static bool plan_tc(int N, int K, int M, int out_bytes, const DeviceInfo& d, TcP
     int xk = 8;
     while (xk > 1 && (xk * (NT / cg) * 128 > 32768 || nk % xk != 0)) xk /= 2;
     (void)out_bytes;
-    for (int pk : {8, 4}) {
-        if (nk % pk != 0) continue;
+    // Q8 chunks of 8 K steps (74 KB) leave too little room for the activation ring: 4 K steps for Q8 (measured:
+    // 12288x2560 M=512 35.3 vs 52.6 us), 8 for Q4 (either is the same there)
+    static const int pk_force = getenv("VKB_TC_PK") ? atoi(getenv("VKB_TC_PK")) : 0;   // tuning override
+    const int pk_order[2] = {wf == 1 ? 4 : 8, wf == 1 ? 8 : 4};
+    for (int pk : pk_order) {
+        if (nk % pk != 0 || ((pk_force == 4 || pk_force == 8) && pk != pk_force)) continue;
         const int pchunk = tc_pchunk(pk, wf);
         int nx = 4, np = 2;   // four X stages first: the activations are the fast-consumed stream
         auto bars_bytes = [&]() { return 8 * (2 * np + 2 * nx + 2 * a.na + 2 * a.nacc) + 16; };
