@@ -88,7 +88,7 @@ def test_tc_rejects_unsupported(cuda):
     assert L.vkb_gemm_q4_tc(p, p, p, p, 128, 256, 0, vkb._stream()) == vkb.EINVAL
 
 
-_PAIR_SCRIPT = r"""
+_VARIANT_SCRIPT = r"""
 import sys
 import numpy as np
 sys.path[:0] = sys.argv[1:4]
@@ -97,7 +97,8 @@ from oracle import oracle as O
 from gpu_util import device_weights, random_codes, uniform_x
 from test_tc_gpu import _tc, _torch_ref
 worst = 0.0
-for N, K, M in [(384, 1024, 128), (1031, 768, 200), (2048, 2048, 511), (512, 256, 16)]:
+for N, K, M in [(384, 1024, 128), (1031, 768, 200), (2048, 2048, 511), (512, 256, 16), (12288, 2560, 512),
+                (640, 2560, 130)]:
     rng = np.random.default_rng(N + K + M)
     codes, scales = random_codes(rng, O.FMT_Q4, N, K)
     q, s = device_weights(O.FMT_Q4, codes, scales)
@@ -109,17 +110,22 @@ print("WORST", worst, "STATUS", vkb.device_status())
 """
 
 
-def test_tc_pair_kernel_opt_in(cuda):
-    """The CTA-pair prompt kernel (tcgen05 cta_group::2, selected by VKB_TC_CG=2) against torch fp32, in a child
-    process (the override is read once per process)."""
+@pytest.mark.parametrize("env", [{"VKB_TC_CG": "2"}, {"VKB_TC_RB": "2"}, {"VKB_TC_RB": "2", "VKB_TC_NT": "176"},
+                                 {"VKB_TC_RB": "2", "VKB_TC_NT": "48"}, {"VKB_TC_RB": "1", "VKB_TC_NT": "176"},
+                                 {"VKB_TC_RB": "1", "VKB_TC_NT": "80"}],
+                         ids=["pair", "rb2", "rb2_nt176", "rb2_nt48", "rb1_nt176", "rb1_nt80"])
+def test_tc_kernel_variants(cuda, env):
+    """Every prompt-kernel variant the planner can pick, forced by its tuning overrides (read once per process, so in
+    a child process) against torch fp32: the CTA pair (tcgen05 cta_group::2), two 128-row blocks per CTA, and token
+    tiles that are multiples of 16 but not of 32 (one accumulator, two blocks, or two accumulators). A forced value
+    that does not fit a shape leaves that shape to the planner."""
     import os
     import subprocess
     import sys
     root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
-    env = dict(os.environ, VKB_TC_CG="2")
     paths = [root, os.path.join(root, "volta-kernel-bakeoff_b200"), os.path.join(root, "tests")]
-    r = subprocess.run([sys.executable, "-c", _PAIR_SCRIPT] + paths, env=env, capture_output=True, text=True,
-                       timeout=300, cwd=root)
+    r = subprocess.run([sys.executable, "-c", _VARIANT_SCRIPT] + paths, env=dict(os.environ, **env),
+                       capture_output=True, text=True, timeout=300, cwd=root)
     assert r.returncode == 0, r.stderr[-2000:]
     line = [l for l in r.stdout.splitlines() if l.startswith("WORST")][-1].split()
     assert float(line[1]) < 1e-5 and int(line[3]) == 0, line

@@ -108,11 +108,37 @@ __device__ __forceinline__ bool mbar_try_wait_sleep(uint32_t bar_addr, uint32_t 
     return ok != 0;
 }
 
-// wait_parity for roles that are not on the critical issue path (producers, the MMA thread, waiting consumers).
+// Non-blocking test of a phase (returns at once): the fast path of the sleeping waits below.
+__device__ __forceinline__ bool mbar_test_wait(uint32_t bar_addr, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(bar_addr), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+__device__ __forceinline__ bool mbar_test_wait_cl(uint32_t bar_addr, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.test_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(bar_addr), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// wait_parity for roles that are not on the critical issue path (producers, the MMA thread, waiting consumers). A
+// completed phase is tested first (test_wait returns at once; a try_wait with a suspend hint costs ~150 cycles even
+// then), and only an incomplete one sleeps.
 __device__ __forceinline__ bool wait_parity_sleep(uint64_t* bar, uint32_t parity,
                                                   unsigned err = DEV_ERR_WAIT_TIMEOUT) {
     const uint32_t a = smem_u32(bar);
-    if (mbar_try_wait_sleep(a, parity)) return true;
+    if (mbar_test_wait(a, parity) || mbar_try_wait_sleep(a, parity)) return true;
     const uint64_t t0 = globaltimer();
     for (;;) {
         if (mbar_try_wait_sleep(a, parity)) return true;
@@ -169,7 +195,7 @@ __device__ __forceinline__ bool mbar_try_wait_sleep_cl(uint32_t bar_addr, uint32
 __device__ __forceinline__ bool wait_parity_sleep_cl(uint64_t* bar, uint32_t parity,
                                                      unsigned err = DEV_ERR_WAIT_TIMEOUT) {
     const uint32_t a = smem_u32(bar);
-    if (mbar_try_wait_sleep_cl(a, parity)) return true;
+    if (mbar_test_wait_cl(a, parity) || mbar_try_wait_sleep_cl(a, parity)) return true;
     const uint64_t t0 = globaltimer();
     for (;;) {
         if (mbar_try_wait_sleep_cl(a, parity)) return true;

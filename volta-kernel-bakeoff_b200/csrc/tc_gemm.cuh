@@ -58,13 +58,14 @@ __host__ __device__ constexpr int tc_pchunk(int pk, int wf = 0) { return TC_BM *
 struct TcArgs {
     void* y;            // [M][ldy], this call's columns from ycol0
     int M, N, K;
-    int NT;             // tokens per tile (multiple of 32, <= 256)
+    int NT;             // tokens per tile (multiple of 16, <= 256; of 32 for a CTA pair)
     int nk;             // K steps per tile (K / 64)
     int tiles_n;        // row tiles (N / 128 rounded up); tile t: rows (t % tiles_n) * 128, tokens (t / tiles_n) NT
     int tiles;          // all tiles
     int na, nx, np;     // ring depths: A slots (TMEM), X stages, P chunks
-    int nacc;           // TMEM accumulators (2 when NT <= 128)
-    int a_col0;         // first TMEM column of the A ring; accumulator b at column b * 128
+    int nacc;           // TMEM accumulators (2 when NT <= 128 with one row block, else 1)
+    int a_col0;         // first TMEM column of the A ring; accumulator b at column b * 128, its row block r at
+                        // + r round_up(NT, 32)
     int xk;             // K steps per X stage (one 3-D TMA box of xk 128B-swizzled NT x 64 tiles)
     int x_stage;        // bytes of one X stage (xk x NT x 128)
     int x_off, p_off, bar_off;   // shared-memory region offsets (1024-aligned)
@@ -263,6 +264,37 @@ template <typename OutT> __device__ __forceinline__ OutT tc_out(float v);
 template <> __device__ __forceinline__ __half tc_out<__half>(float v) { return __float2half_rn(v); }
 template <> __device__ __forceinline__ float tc_out<float>(float v) { return v; }
 
+// One warp's share of a finished accumulator: the 32-token chunks sub, sub + parts, ... of its TMEM lane quarter
+// (tq_addr: lane quarter and accumulator column; n: this lane's weight row), two TMEM loads in flight, stored straight
+// to y. 32-column loads may run past the tile's tokens (up to the next multiple of 32): still inside the TMEM
+// allocation, and not stored.
+template <typename OutT>
+__device__ __forceinline__ void tc_epi_store(const TcArgs& a, uint32_t tq_addr, int n, int tok0, int sub, int parts) {
+    OutT* y = reinterpret_cast<OutT*>(a.y);
+    const int step = 32 * parts;
+    const int ntok = min(a.NT, a.M - tok0);   // tokens of this tile (NT is a multiple of 16, not of 32)
+    auto put = [&](const uint32_t (&v)[32], int c) {
+        if (n >= a.N) return;
+        OutT* yp = y + (size_t)(tok0 + c) * a.ldy + a.ycol0 + n;
+        const int lim = ntok - c;
+#pragma unroll
+        for (int j = 0; j < 32; ++j, yp += a.ldy)
+            if (j < lim) *yp = tc_out<OutT>(__uint_as_float(v[j]));
+    };
+    uint32_t va[32], vb[32];
+    int c = 32 * sub;
+    if (c < ntok) tmem_ld32_async(tq_addr + (uint32_t)c, va);
+    for (; c < ntok; c += 2 * step) {
+        tmem_wait_ld(va);
+        if (c + step < ntok) tmem_ld32_async(tq_addr + (uint32_t)(c + step), vb);
+        put(va, c);
+        if (c + step >= ntok) break;
+        tmem_wait_ld(vb);
+        if (c + 2 * step < ntok) tmem_ld32_async(tq_addr + (uint32_t)(c + 2 * step), va);
+        put(vb, c + step);
+    }
+}
+
 // Push the finished tile (weight rows row0.., tokens tok0..) from this rank's y to every peer; thread t of nth.
 // Out of line, so that the epilogue's register allocation does not carry it.
 template <typename OutT>
@@ -282,13 +314,23 @@ __device__ __noinline__ void tc_push_tile(const TcArgs& a, int row0, int tok0, i
 // complete on the leader's barrier); the leader's commits arrive on both CTAs' barriers. No TMA multicast.
 // WF: weight format, 0 = Q4 (the reference's tc_q4), 1 = Q8 (the tc_q8 it planned, SURVEY's next rows): only the packed
 // chunk layout and the dequantisation differ.
-template <typename OutT, int PK, bool P2P, int CG, int WF = 0>
+// RB = 2: one CTA holds a 256-row tile as two 128-row blocks, each with its own accumulator (TMEM columns 0 and NT
+// rounded up to 32), and every activation K step feeds the MMAs of both blocks: the activations are streamed from L2
+// once per 256 weight rows instead of once per 128. That stream (re-read once per row tile: N / 128 times the activations) is what bounds
+// the one-block kernel at 512 tokens (measured: the activation and weight streams alone, without MMAs or
+// dequantisation, take two thirds of its time at 12288x2560). A slots hold one K step of both blocks (64 columns);
+// dequantising group g (four warps) converts block g.
+template <typename OutT, int PK, bool P2P, int CG, int WF = 0, int RB = 1>
 __global__ void __launch_bounds__(TC_THREADS, 1)
 tc_q4_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap ts,
              const __grid_constant__ CUtensorMap tx, const __grid_constant__ TcArgs a) {
     static_assert(CG == 1 || (CG == 2 && !P2P), "peer stores use the one-CTA kernel");
     static_assert(WF == 0 || (WF == 1 && !P2P && CG == 1), "Q8 weights: the one-CTA kernel without peer stores");
-    constexpr int PPITCH = tc_ppitch(PK, WF), PCHUNK = tc_pchunk(PK, WF), SCOFF = TC_BM * PPITCH;
+    static_assert(RB == 1 || (RB == 2 && CG == 1 && !P2P && WF == 0), "two row blocks: the one-CTA Q4 kernel");
+    constexpr int BMR = TC_BM * RB;                         // weight rows of a CTA's tile
+    constexpr int SK = RB == 1 ? TC_SLOT : 1;               // K steps per A slot
+    constexpr int SLOT_COLS = RB * SK * TC_ACOLS;           // TMEM columns per A slot (128, or 64 with two blocks)
+    constexpr int PPITCH = tc_ppitch(PK, WF), PCHUNK = RB * tc_pchunk(PK, WF), SCOFF = BMR * PPITCH;
     constexpr int KSB = WF == 1 ? 64 : 32;   // code bytes per row per K step
     extern __shared__ uint8_t smem_raw[];
     const uint32_t pad = (1024u - (smem_u32(smem_raw) & 1023u)) & 1023u;
@@ -305,17 +347,18 @@ tc_q4_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUt
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accempty + a.nacc);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int nk = a.nk, nch = nk / PK, nxs = nk / a.xk, nslots = nk / TC_SLOT;
+    const int nk = a.nk, nch = nk / PK, nxs = nk / a.xk, nslots = nk / SK;
+    const int rbcol = (a.NT + 31) & ~31;   // TMEM columns between the row blocks' accumulators (32-aligned)
     // the CTA's place in its pair (CG = 2) and the pairs of the grid; a "unit" is a CTA (CG = 1) or a pair
     const uint32_t crank = CG == 2 ? cluster_ctarank() : 0u;
     const bool leader = crank == 0;
     const int units = CG == 2 ? (int)cluster_count_x() : (int)gridDim.x;
     const int unit = CG == 2 ? (int)cluster_id_x() : (int)blockIdx.x;
-    // tiles of this unit: t = unit + i * units (a tile: 128 CG weight rows x NT tokens; this CTA's rows start at
+    // tiles of this unit: t = unit + i * units (a tile: 128 RB CG weight rows x NT tokens; this CTA's rows start at
     // row0_of(t), its tokens for the B operand at tok0_of(t) + crank NT / CG)
     const int ntl = unit < a.tiles ? (a.tiles - 1 - unit) / units + 1 : 0;
     auto tile_of = [&](int i) { return unit + i * units; };
-    auto row0_of = [&](int t) { return (t % a.tiles_n) * (TC_BM * CG) + TC_BM * (int)crank; };
+    auto row0_of = [&](int t) { return (t % a.tiles_n) * (BMR * CG) + BMR * (int)crank; };
     auto tok0_of = [&](int t) { return (t / a.tiles_n) * a.NT; };
     // barrier helpers: waits that a peer CTA may have released acquire at cluster scope; arrivals that the MMA
     // issuer waits for go to the leader's barrier; commits of a pair's MMAs arrive in both CTAs
@@ -373,6 +416,54 @@ tc_q4_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUt
     const uint32_t tmem = *tmem_slot;
 
     bool ok = true;
+    // ---- epilogue of one tile, by one participant warp ----
+    // A warp reads TMEM lanes 32 (w % 4).. (weight rows): the `parts` participants of a lane quarter take interleaved
+    // 32-token chunks (sub: this warp's index among them) and store y directly (tc_epi_store; a warp's store covers
+    // 32 consecutive outputs of one token: 64 or 128 contiguous bytes). With `arrive` the warp then
+    // releases the accumulator to the MMA warp. With peer stores, the participants of a tile then push the finished
+    // tile from this rank's y to every peer (p2p_push: 16-byte words) while the MMA warp works on the next tile; every
+    // participant passes the tile's named barrier, also after a failed wait (it then skips the work), so that no
+    // barrier waits for a warp that left.
+    // The epilogue warps empty every tile (with two accumulators, behind the next tile's MMAs); the dequantising
+    // warps, idle by then, join for the CTA's last tile, whose epilogue nothing else overlaps. (Joining every tile
+    // when there is one accumulator was measured slower: the epilogue code inside the dequantising loop, inline or
+    // called, slows that loop by more than the shorter epilogue gains.)
+    bool epi_began = false;
+    auto epi_tile = [&](int i, int sub, int parts, bool arrive) {
+        if (!epi_began) {
+            epi_began = true;
+            pdl_wait();   // y may still be read or written by the previous grid
+            if constexpr (P2P) {   // this rank's copy may now be written; wait until every peer's may be
+                const uint32_t e = p2p_epoch(a.pp);
+                if (warp == TC_WEPI0 && lane == 0) p2p_post_ready(a.pp, e);
+                if (lane == 0 && !p2p_wait_ready(a.pp, e)) ok = false;
+                ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+            }
+        }
+        const int acc = i % a.nacc, t = tile_of(i), row0 = row0_of(t), tok0 = tok0_of(t);
+        const int q = warp & 3;
+        if (ok) ok = __all_sync(0xffffffffu, wait_b(&accfull[acc], (i / a.nacc) & 1));
+        if (ok) {
+            tc_fence_after();
+#pragma unroll
+            for (int rb = 0; rb < RB; ++rb) {   // row block rb: accumulator columns from rb rbcol, rows from 128 rb
+                const uint32_t tq_addr = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(acc * 128 + rb * rbcol);
+                tc_epi_store<OutT>(a, tq_addr, row0 + rb * TC_BM + 32 * q + lane, tok0, sub, parts);
+            }
+            // every TMEM read of this accumulator has completed: the MMA warp may overwrite it
+            if (arrive) {
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) arrive_leader(&accempty[acc]);
+            }
+        }
+        if constexpr (P2P) {   // the tile is complete in this rank's copy: its participants push it to every peer
+            named_sync(2, 128u * (uint32_t)parts);
+            if (ok) tc_push_tile<OutT>(a, row0, tok0, (warp >= TC_WEPI0 ? warp - TC_WEPI0 : warp - TC_WDQ0 + 4) * 32
+                                       + lane, 128 * parts);
+        }
+    };
+
     if (warp == 0) {
         // ===================== P ring producer =====================
         for (int g = a.np; g < total_ch; ++g) {
@@ -418,247 +509,240 @@ tc_q4_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUt
                 if (!wait_b(&xfull[gs % a.nx], (gs / a.nx) & 1, DEV_ERR_DRAIN_TIMEOUT)) break;
     } else if (warp == 1 && leader) {
         // ===================== MMA issuer (the pair leader's, CG = 2) =====================
-        // per slot: wait for its A (TMEM) and the X stages its 4 K steps read, then 16 UMMAs (4 per K step). When the
-        // X ring holds at least two slots of K steps all of a slot's X waits come first and the 16 UMMAs issue back
-        // to back; otherwise (large token tiles, shallow X ring) the waits interleave with the K steps so that each
-        // X stage is released as soon as its own MMAs complete.
-        const uint32_t idesc = umma_idesc_f16(a.NT, TC_BM * CG);
-        const uint32_t xtile = (uint32_t)(a.NT / CG) * 128;   // one K step of this CTA's tokens in a stage
-        const bool hoist = a.nx * a.xk >= 2 * TC_SLOT;
-        int ab = 0, arnd = 0, xb = 0, xrnd = 0, xj = 0;
-        for (int i = 0; i < ntl && ok; ++i) {
-            const int acc = i % a.nacc;
-            if (i >= a.nacc) ok = __all_sync(0xffffffffu, wait_b(&accempty[acc], ((i / a.nacc) - 1) & 1));
-            if (!ok) break;
-            tc_fence_after();
-            const uint32_t td = tmem + (uint32_t)(acc * 128);
-            for (int sl = 0; sl < nslots && ok; ++sl) {
-                ok = __all_sync(0xffffffffu, wait_b(&afull[ab], arnd & 1));
+        // Per slot: wait for its A (TMEM) and the X stages its SK K steps read, then 4 UMMAs per K step and row block
+        // (16 per slot), issued by one elected lane. tcgen05.mma issue blocks while the tensor pipe's queue is full
+        // (it holds about one instruction), so every cycle this warp spends between two UMMAs is tensor-pipe idle
+        // time. Its waits therefore test the phase first (mbarrier.test_wait, in wait_parity_sleep) and sleep in
+        // try_wait only when it is not complete (measured: a sleeping try_wait on a completed phase cost ~150-300
+        // cycles per wait, ~150 cycles per UMMA in all; the test first: 5 % off 12288x2560 at 512 tokens; one lane
+        // running the loop alone, polling or sleeping, was slower still). When the X ring holds at least two slots of K steps all
+        // of a slot's X waits come first and its UMMAs issue back to back; otherwise (large token tiles, shallow X
+        // ring) the waits interleave with the K steps so that each X stage is released as soon as its own MMAs
+        // complete.
+        {
+            auto wait_m = [&](uint64_t* bar, uint32_t par) { return __all_sync(0xffffffffu, wait_b(bar, par)); };
+            const uint32_t idesc = umma_idesc_f16(a.NT, TC_BM * CG);
+            const uint32_t xtile = (uint32_t)(a.NT / CG) * 128;   // one K step of this CTA's tokens in a stage
+            const bool hoist = a.nx * a.xk >= 2 * SK;
+            // K step j of the slot at ta (X at sb, K step it of the tile): row block rb's A at slot column
+            // (j RB + rb) 32, its accumulator at td + rb rbcol
+            auto issue_k = [&](uint32_t td, uint32_t ta, uint32_t sb, int j, int it) {
+#pragma unroll
+                for (int kk = 0; kk < TC_BK / 16; ++kk) {   // 16 k: 8 TMEM columns of A, 32 B of a B row
+#pragma unroll
+                    for (int rb = 0; rb < RB; ++rb) {
+                        const uint32_t tdr = td + (uint32_t)(rb * rbcol);
+                        const uint32_t tar = ta + (uint32_t)((j * RB + rb) * TC_ACOLS + 8 * kk);
+                        if constexpr (CG == 2)
+                            umma_f16_ts_cg2(tdr, tar, umma_desc_sw128(sb + 32 * kk), idesc, (it | kk) != 0);
+                        else
+                            umma_f16_ts(tdr, tar, umma_desc_sw128(sb + 32 * kk), idesc, (it | kk) != 0);
+                    }
+                }
+            };
+            int ab = 0, arnd = 0, xb = 0, xrnd = 0, xj = 0;
+            for (int i = 0; i < ntl && ok; ++i) {
+                const int acc = i % a.nacc;
+                if (i >= a.nacc) ok = wait_m(&accempty[acc], ((i / a.nacc) - 1) & 1);
                 if (!ok) break;
                 tc_fence_after();
-                const uint32_t ta = tmem + (uint32_t)(a.a_col0 + ab * TC_SLOT * TC_ACOLS);
-                if (hoist) {
-                    uint32_t sb[TC_SLOT];
-                    int rel[TC_SLOT];   // X stage to release after K step j (-1: none)
-#pragma unroll
-                    for (int j = 0; j < TC_SLOT; ++j) {
-                        if (xj == 0 && ok) ok = __all_sync(0xffffffffu, wait_b(&xfull[xb], xrnd & 1));
-                        sb[j] = smem_u32(sm + a.x_off + xb * a.x_stage) + xj * xtile;
-                        rel[j] = xj + 1 == a.xk ? xb : -1;
-                        if (++xj == a.xk) {
-                            xj = 0;
-                            if (++xb == a.nx) { xb = 0; ++xrnd; }
-                        }
-                    }
+                const uint32_t td = tmem + (uint32_t)(acc * 128);
+                for (int sl = 0; sl < nslots && ok; ++sl) {
+                    ok = wait_m(&afull[ab], arnd & 1);
                     if (!ok) break;
-                    if (elect_one()) {
+                    tc_fence_after();
+                    const uint32_t ta = tmem + (uint32_t)(a.a_col0 + ab * SLOT_COLS);
+                    if (hoist) {
+                        uint32_t sb[SK];
+                        int rel[SK];   // X stage to release after K step j (-1: none)
 #pragma unroll
-                        for (int j = 0; j < TC_SLOT; ++j) {
-                            const int it = sl * TC_SLOT + j;
-#pragma unroll
-                            for (int kk = 0; kk < TC_BK / 16; ++kk) {   // 16 k: 8 TMEM columns of A, 32 B of a B row
-                                if constexpr (CG == 2)
-                                    umma_f16_ts_cg2(td, ta + (uint32_t)(j * TC_ACOLS + 8 * kk),
-                                                    umma_desc_sw128(sb[j] + 32 * kk), idesc, (it | kk) != 0);
-                                else
-                                    umma_f16_ts(td, ta + (uint32_t)(j * TC_ACOLS + 8 * kk),
-                                                umma_desc_sw128(sb[j] + 32 * kk), idesc, (it | kk) != 0);
+                        for (int j = 0; j < SK; ++j) {
+                            if (xj == 0 && ok) ok = wait_m(&xfull[xb], xrnd & 1);
+                            sb[j] = smem_u32(sm + a.x_off + xb * a.x_stage) + xj * xtile;
+                            rel[j] = xj + 1 == a.xk ? xb : -1;
+                            if (++xj == a.xk) {
+                                xj = 0;
+                                if (++xb == a.nx) { xb = 0; ++xrnd; }
                             }
-                            if (rel[j] >= 0) commit(&xempty[rel[j]]);   // free the stage after these MMAs
                         }
-                        commit(&aempty[ab]);
-                    }
-                    __syncwarp();
-                } else {
-#pragma unroll
-                    for (int j = 0; j < TC_SLOT; ++j) {
-                        if (xj == 0) {
-                            ok = __all_sync(0xffffffffu, wait_b(&xfull[xb], xrnd & 1));
-                            if (!ok) break;
-                        }
-                        const int it = sl * TC_SLOT + j;
-                        const uint32_t sb = smem_u32(sm + a.x_off + xb * a.x_stage) + xj * xtile;
-                        const bool last_x = xj + 1 == a.xk;
+                        if (!ok) break;
+                        tc_fence_after();
                         if (elect_one()) {
 #pragma unroll
-                            for (int kk = 0; kk < TC_BK / 16; ++kk) {
-                                if constexpr (CG == 2)
-                                    umma_f16_ts_cg2(td, ta + (uint32_t)(j * TC_ACOLS + 8 * kk),
-                                                    umma_desc_sw128(sb + 32 * kk), idesc, (it | kk) != 0);
-                                else
-                                    umma_f16_ts(td, ta + (uint32_t)(j * TC_ACOLS + 8 * kk),
-                                                umma_desc_sw128(sb + 32 * kk), idesc, (it | kk) != 0);
+                            for (int j = 0; j < SK; ++j) {
+                                issue_k(td, ta, sb[j], j, sl * SK + j);
+                                if (rel[j] >= 0) commit(&xempty[rel[j]]);   // free the stage after these MMAs
                             }
-                            if (last_x) commit(&xempty[xb]);
-                            if (j == TC_SLOT - 1) commit(&aempty[ab]);
+                            commit(&aempty[ab]);
                         }
                         __syncwarp();
-                        if (last_x) {
-                            xj = 0;
-                            if (++xb == a.nx) { xb = 0; ++xrnd; }
-                        } else {
-                            ++xj;
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < SK; ++j) {
+                            if (xj == 0) {
+                                ok = wait_m(&xfull[xb], xrnd & 1);
+                                if (!ok) break;
+                                tc_fence_after();
+                            }
+                            const uint32_t sb = smem_u32(sm + a.x_off + xb * a.x_stage) + xj * xtile;
+                            const bool last_x = xj + 1 == a.xk;
+                            if (elect_one()) {
+                                issue_k(td, ta, sb, j, sl * SK + j);
+                                if (last_x) commit(&xempty[xb]);
+                                if (j == SK - 1) commit(&aempty[ab]);
+                            }
+                            __syncwarp();
+                            if (last_x) {
+                                xj = 0;
+                                if (++xb == a.nx) { xb = 0; ++xrnd; }
+                            } else {
+                                ++xj;
+                            }
                         }
+                        if (!ok) break;
                     }
-                    if (!ok) break;
+                    if (++ab == a.na) { ab = 0; ++arnd; }
                 }
-                if (++ab == a.na) { ab = 0; ++arnd; }
+                if (!ok) break;
+                if (elect_one()) commit(&accfull[acc]);   // the tile's MMAs are done: its accumulator is final
+                __syncwarp();
             }
-            if (!ok) break;
-            if (elect_one()) commit(&accfull[acc]);   // the tile's MMAs are done: its accumulator is final
-            __syncwarp();
         }
     } else if (warp >= TC_WDQ0 && warp < TC_WEPI0) {
-        // ===================== dequantise (two groups, half a slot each) =====================
+        // ===================== dequantise (two groups: half a slot each, or one row block each) ==============
         const int dw = warp - TC_WDQ0;            // 0..7
-        const int grp = dw >> 2;                  // K steps 2 grp, 2 grp + 1 of every slot
+        const int grp = dw >> 2;                  // RB = 1: K steps 2 grp, 2 grp + 1 of every slot; RB = 2: block grp
         const int qtr = warp & 3;                 // TMEM lane quarter this warp may access
-        const int r = qtr * 32 + lane;            // weight row of the tile = TMEM lane
-        const uint32_t prow = smem_u32(sm + a.p_off) + r * PPITCH;
-        const uint32_t srow = smem_u32(sm + a.p_off) + SCOFF + r * TC_SPITCH;
-        const uint32_t tlane = tmem + ((uint32_t)(32 * qtr) << 16) + (uint32_t)(a.a_col0 + 2 * grp * TC_ACOLS);
-        for (int g = 0; g < total_ch && ok; ++g) {   // chunk g of the CTA's stream (tile g / nch)
-            const int pb = g % a.np;
-            if (!wait_parity_sleep(&pfull[pb], (g / a.np) & 1)) { ok = false; break; }
-            uint32_t sw[PK];                                          // scales of the chunk's 2 PK groups
+        if constexpr (RB == 2) {
+            // one K step per slot; group grp converts row block grp (tile row 128 grp + TMEM lane)
+            const int r = grp * TC_BM + qtr * 32 + lane;
+            const uint32_t prow = smem_u32(sm + a.p_off) + r * PPITCH;
+            const uint32_t srow = smem_u32(sm + a.p_off) + SCOFF + r * TC_SPITCH;
+            const uint32_t tlane = tmem + ((uint32_t)(32 * qtr) << 16) + (uint32_t)(a.a_col0 + grp * TC_ACOLS);
+            for (int g = 0; g < total_ch && ok; ++g) {   // chunk g of the CTA's stream (tile g / nch)
+                const int pb = g % a.np;
+                if (!wait_parity_sleep(&pfull[pb], (g / a.np) & 1)) { ok = false; break; }
+                uint32_t sw[PK];                                      // scales of the chunk's 2 PK groups
 #pragma unroll
-            for (int q4 = 0; q4 < PK / 4; ++q4) {
-                const uint4 t = lds128(srow + pb * PCHUNK + 16 * q4);
-                sw[4 * q4] = t.x; sw[4 * q4 + 1] = t.y; sw[4 * q4 + 2] = t.z; sw[4 * q4 + 3] = t.w;
-            }
-#pragma unroll
-            for (int sc = 0; sc < PK / TC_SLOT; ++sc) {            // slots of this chunk
-                const int sl = g * (PK / TC_SLOT) + sc;             // slot of the CTA's stream
-                const int ab = sl % a.na;
-                // this group's two K steps of the slot: both loads first, then both conversions, one TMEM store
-                const int sub0 = sc * TC_SLOT + 2 * grp;            // first of the two sub-steps within the chunk
-                const uint32_t pa = prow + pb * PCHUNK + sub0 * KSB;
-                uint4 w0 = lds128(pa), w1 = lds128(pa + 16), w2 = lds128(pa + 32), w3 = lds128(pa + 48);
-                const uint32_t sa = grp ? sw[sc * TC_SLOT + 2] : sw[sc * TC_SLOT];       // static indices
-                const uint32_t sb = grp ? sw[sc * TC_SLOT + 3] : sw[sc * TC_SLOT + 1];
-                if (WF == 0 && sc == PK / TC_SLOT - 1) {            // this warp's last read of the chunk
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(&pempty[pb]);
+                for (int q4 = 0; q4 < PK / 4; ++q4) {
+                    const uint4 t = lds128(srow + pb * PCHUNK + 16 * q4);
+                    sw[4 * q4] = t.x; sw[4 * q4 + 1] = t.y; sw[4 * q4 + 2] = t.z; sw[4 * q4 + 3] = t.w;
                 }
-                uint32_t v[64];
-                const uint32_t a_lo = (sa & 0xFFFFu) * 0x00010001u, a_hi = (sa >> 16) * 0x00010001u;
-                const uint32_t b_lo = (sb & 0xFFFFu) * 0x00010001u, b_hi = (sb >> 16) * 0x00010001u;
-                if constexpr (WF == 0) {   // Q4: 32 code bytes per K step (w0-w1: step A, w2-w3: step B)
-                    dequant8_to(w0.x, a_lo, v + 0);
-                    dequant8_to(w0.y, a_lo, v + 4);
-                    dequant8_to(w0.z, a_lo, v + 8);
-                    dequant8_to(w0.w, a_lo, v + 12);
-                    dequant8_to(w1.x, a_hi, v + 16);
-                    dequant8_to(w1.y, a_hi, v + 20);
-                    dequant8_to(w1.z, a_hi, v + 24);
-                    dequant8_to(w1.w, a_hi, v + 28);
-                    dequant8_to(w2.x, b_lo, v + 32);
-                    dequant8_to(w2.y, b_lo, v + 36);
-                    dequant8_to(w2.z, b_lo, v + 40);
-                    dequant8_to(w2.w, b_lo, v + 44);
-                    dequant8_to(w3.x, b_hi, v + 48);
-                    dequant8_to(w3.y, b_hi, v + 52);
-                    dequant8_to(w3.z, b_hi, v + 56);
-                    dequant8_to(w3.w, b_hi, v + 60);
-                } else {   // Q8: 64 code bytes per K step; w0-w3 hold step A, step B is loaded after A is converted
-                    const uint4 wa[4] = {w0, w1, w2, w3};
 #pragma unroll
-                    for (int i = 0; i < 4; ++i) {   // 16 codes per uint4: groups of 32 = two uint4
-                        const uint32_t s2 = i < 2 ? a_lo : a_hi;
-                        dequant4_q8_to(wa[i].x, s2, v + 8 * i);
-                        dequant4_q8_to(wa[i].y, s2, v + 8 * i + 2);
-                        dequant4_q8_to(wa[i].z, s2, v + 8 * i + 4);
-                        dequant4_q8_to(wa[i].w, s2, v + 8 * i + 6);
-                    }
-                    w0 = lds128(pa + 64); w1 = lds128(pa + 80); w2 = lds128(pa + 96); w3 = lds128(pa + 112);
-                    const uint4 wb[4] = {w0, w1, w2, w3};
-#pragma unroll
-                    for (int i = 0; i < 4; ++i) {
-                        const uint32_t s2 = i < 2 ? b_lo : b_hi;
-                        dequant4_q8_to(wb[i].x, s2, v + 32 + 8 * i);
-                        dequant4_q8_to(wb[i].y, s2, v + 32 + 8 * i + 2);
-                        dequant4_q8_to(wb[i].z, s2, v + 32 + 8 * i + 4);
-                        dequant4_q8_to(wb[i].w, s2, v + 32 + 8 * i + 6);
-                    }
-                    if (sc == PK / TC_SLOT - 1) {                   // this warp's last read of the chunk
+                for (int sc = 0; sc < PK; ++sc) {                     // K step sc of the chunk = one slot
+                    const int sl = g * PK + sc, ab = sl % a.na;
+                    const uint32_t pa = prow + pb * PCHUNK + sc * KSB;
+                    const uint4 w0 = lds128(pa), w1 = lds128(pa + 16);
+                    if (sc == PK - 1) {                               // this warp's last read of the chunk
                         __syncwarp();
                         if (lane == 0) mbar_arrive(&pempty[pb]);
                     }
+                    const uint32_t lo = (sw[sc] & 0xFFFFu) * 0x00010001u, hi = (sw[sc] >> 16) * 0x00010001u;
+                    uint32_t v[32];
+                    dequant8_to(w0.x, lo, v + 0);
+                    dequant8_to(w0.y, lo, v + 4);
+                    dequant8_to(w0.z, lo, v + 8);
+                    dequant8_to(w0.w, lo, v + 12);
+                    dequant8_to(w1.x, hi, v + 16);
+                    dequant8_to(w1.y, hi, v + 20);
+                    dequant8_to(w1.z, hi, v + 24);
+                    dequant8_to(w1.w, hi, v + 28);
+                    if (sl >= a.na && !wait_b(&aempty[ab], ((sl / a.na) - 1) & 1)) { ok = false; break; }
+                    tc_fence_after();                                 // the slot's previous MMAs are done
+                    tmem_st32(tlane + (uint32_t)(ab * SLOT_COLS), v);
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) arrive_leader(&afull[ab]);
                 }
-                if (sl >= a.na && !wait_b(&aempty[ab], ((sl / a.na) - 1) & 1)) { ok = false; break; }
-                tc_fence_after();                                   // the slot's previous MMAs are done
-                tmem_st64(tlane + (uint32_t)(ab * TC_SLOT * TC_ACOLS), v);
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) arrive_leader(&afull[ab]);
+            }
+        } else {
+            const int r = qtr * 32 + lane;            // weight row of the tile = TMEM lane
+            const uint32_t prow = smem_u32(sm + a.p_off) + r * PPITCH;
+            const uint32_t srow = smem_u32(sm + a.p_off) + SCOFF + r * TC_SPITCH;
+            const uint32_t tlane = tmem + ((uint32_t)(32 * qtr) << 16) + (uint32_t)(a.a_col0 + 2 * grp * TC_ACOLS);
+            for (int g = 0; g < total_ch && ok; ++g) {   // chunk g of the CTA's stream (tile g / nch)
+                const int pb = g % a.np;
+                if (!wait_parity_sleep(&pfull[pb], (g / a.np) & 1)) { ok = false; break; }
+                uint32_t sw[PK];                                          // scales of the chunk's 2 PK groups
+#pragma unroll
+                for (int q4 = 0; q4 < PK / 4; ++q4) {
+                    const uint4 t = lds128(srow + pb * PCHUNK + 16 * q4);
+                    sw[4 * q4] = t.x; sw[4 * q4 + 1] = t.y; sw[4 * q4 + 2] = t.z; sw[4 * q4 + 3] = t.w;
+                }
+#pragma unroll
+                for (int sc = 0; sc < PK / TC_SLOT; ++sc) {            // slots of this chunk
+                    const int sl = g * (PK / TC_SLOT) + sc;             // slot of the CTA's stream
+                    const int ab = sl % a.na;
+                    // this group's two K steps of the slot: both loads first, then both conversions, one TMEM store
+                    const int sub0 = sc * TC_SLOT + 2 * grp;            // first of the two sub-steps within the chunk
+                    const uint32_t pa = prow + pb * PCHUNK + sub0 * KSB;
+                    uint4 w0 = lds128(pa), w1 = lds128(pa + 16), w2 = lds128(pa + 32), w3 = lds128(pa + 48);
+                    const uint32_t sa = grp ? sw[sc * TC_SLOT + 2] : sw[sc * TC_SLOT];       // static indices
+                    const uint32_t sb = grp ? sw[sc * TC_SLOT + 3] : sw[sc * TC_SLOT + 1];
+                    if (WF == 0 && sc == PK / TC_SLOT - 1) {            // this warp's last read of the chunk
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(&pempty[pb]);
+                    }
+                    uint32_t v[64];
+                    const uint32_t a_lo = (sa & 0xFFFFu) * 0x00010001u, a_hi = (sa >> 16) * 0x00010001u;
+                    const uint32_t b_lo = (sb & 0xFFFFu) * 0x00010001u, b_hi = (sb >> 16) * 0x00010001u;
+                    if constexpr (WF == 0) {   // Q4: 32 code bytes per K step (w0-w1: step A, w2-w3: step B)
+                        dequant8_to(w0.x, a_lo, v + 0);
+                        dequant8_to(w0.y, a_lo, v + 4);
+                        dequant8_to(w0.z, a_lo, v + 8);
+                        dequant8_to(w0.w, a_lo, v + 12);
+                        dequant8_to(w1.x, a_hi, v + 16);
+                        dequant8_to(w1.y, a_hi, v + 20);
+                        dequant8_to(w1.z, a_hi, v + 24);
+                        dequant8_to(w1.w, a_hi, v + 28);
+                        dequant8_to(w2.x, b_lo, v + 32);
+                        dequant8_to(w2.y, b_lo, v + 36);
+                        dequant8_to(w2.z, b_lo, v + 40);
+                        dequant8_to(w2.w, b_lo, v + 44);
+                        dequant8_to(w3.x, b_hi, v + 48);
+                        dequant8_to(w3.y, b_hi, v + 52);
+                        dequant8_to(w3.z, b_hi, v + 56);
+                        dequant8_to(w3.w, b_hi, v + 60);
+                    } else {   // Q8: 64 code bytes per K step; w0-w3 hold step A, step B is loaded after A is converted
+                        const uint4 wa[4] = {w0, w1, w2, w3};
+#pragma unroll
+                        for (int i = 0; i < 4; ++i) {   // 16 codes per uint4: groups of 32 = two uint4
+                            const uint32_t s2 = i < 2 ? a_lo : a_hi;
+                            dequant4_q8_to(wa[i].x, s2, v + 8 * i);
+                            dequant4_q8_to(wa[i].y, s2, v + 8 * i + 2);
+                            dequant4_q8_to(wa[i].z, s2, v + 8 * i + 4);
+                            dequant4_q8_to(wa[i].w, s2, v + 8 * i + 6);
+                        }
+                        w0 = lds128(pa + 64); w1 = lds128(pa + 80); w2 = lds128(pa + 96); w3 = lds128(pa + 112);
+                        const uint4 wb[4] = {w0, w1, w2, w3};
+#pragma unroll
+                        for (int i = 0; i < 4; ++i) {
+                            const uint32_t s2 = i < 2 ? b_lo : b_hi;
+                            dequant4_q8_to(wb[i].x, s2, v + 32 + 8 * i);
+                            dequant4_q8_to(wb[i].y, s2, v + 32 + 8 * i + 2);
+                            dequant4_q8_to(wb[i].z, s2, v + 32 + 8 * i + 4);
+                            dequant4_q8_to(wb[i].w, s2, v + 32 + 8 * i + 6);
+                        }
+                        if (sc == PK / TC_SLOT - 1) {                   // this warp's last read of the chunk
+                            __syncwarp();
+                            if (lane == 0) mbar_arrive(&pempty[pb]);
+                        }
+                    }
+                    if (sl >= a.na && !wait_b(&aempty[ab], ((sl / a.na) - 1) & 1)) { ok = false; break; }
+                    tc_fence_after();                                   // the slot's previous MMAs are done
+                    tmem_st64(tlane + (uint32_t)(ab * TC_SLOT * TC_ACOLS), v);
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) arrive_leader(&afull[ab]);
+                }
             }
         }
     }
     // ===================== epilogue =====================
-    // Epilogue warps (12-15) empty every accumulator; the dequantising warps, idle by then, join for the CTA's last
-    // tile, whose epilogue nothing else overlaps. A warp reads TMEM lanes 32 (w % 4).. (weight rows): the participants
-    // of a lane quarter take interleaved 32-token chunks, two TMEM loads in flight, and store y directly (a warp's
-    // store covers 32 consecutive outputs of one token: 64 or 128 contiguous bytes). With peer stores, the
-    // participants of a tile then push the finished tile from this rank's y to every peer (p2p_push: 16-byte words)
-    // while the MMA warp works on the next tile.
-    if (warp >= TC_WDQ0) {
-        const bool epi = warp >= TC_WEPI0;
-        const int q = warp & 3;
-        const int sub = epi ? 0 : 1 + ((warp - TC_WDQ0) >> 2);   // participant index within the lane quarter
-        pdl_wait();   // y may still be read or written by the previous grid
-        uint32_t p2p_e = 0;
-        if constexpr (P2P) {   // this rank's copy may now be written; wait until every peer's may be
-            p2p_e = p2p_epoch(a.pp);
-            if (warp == TC_WEPI0 && lane == 0) p2p_post_ready(a.pp, p2p_e);
-            if (lane == 0 && !p2p_wait_ready(a.pp, p2p_e)) ok = false;
-            ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
-        }
-        OutT* y = reinterpret_cast<OutT*>(a.y);
-        // With peer stores every participant of a tile passes the tile's named barrier, also after a failed wait (it
-        // then skips the work), so that no barrier waits for a warp that left the loop.
-        for (int i = epi ? 0 : ntl - 1; i < ntl && (ok || P2P); ++i) {
-            const int acc = i % a.nacc, t = tile_of(i), row0 = row0_of(t), tok0 = tok0_of(t);
-            const bool last = i == ntl - 1;
-            const int parts = last ? 3 : 1;
-            if (ok) ok = __all_sync(0xffffffffu, wait_b(&accfull[acc], (i / a.nacc) & 1));
-            if (ok) {
-                tc_fence_after();
-                const uint32_t tq_addr = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(acc * 128);
-                const int n = row0 + 32 * q + lane;
-                const int step = 32 * parts;
-                auto put = [&](const uint32_t (&v)[32], int c) {
-                    if (n >= a.N) return;
-                    OutT* yp = y + (size_t)(tok0 + c) * a.ldy + a.ycol0 + n;
-                    const int lim = a.M - (tok0 + c);
-#pragma unroll
-                    for (int j = 0; j < 32; ++j, yp += a.ldy)
-                        if (j < lim) *yp = tc_out<OutT>(__uint_as_float(v[j]));
-                };
-                uint32_t va[32], vb[32];
-                int c = 32 * sub;
-                if (c < a.NT) tmem_ld32_async(tq_addr + (uint32_t)c, va);
-                for (; c < a.NT; c += 2 * step) {
-                    tmem_wait_ld(va);
-                    if (c + step < a.NT) tmem_ld32_async(tq_addr + (uint32_t)(c + step), vb);
-                    put(va, c);
-                    if (c + step >= a.NT) break;
-                    tmem_wait_ld(vb);
-                    if (c + 2 * step < a.NT) tmem_ld32_async(tq_addr + (uint32_t)(c + 2 * step), va);
-                    put(vb, c + step);
-                }
-                // every TMEM read of this accumulator has completed: the MMA warp may overwrite it
-                if (epi) {
-                    tc_fence_before();
-                    __syncwarp();
-                    if (lane == 0) arrive_leader(&accempty[acc]);
-                }
-            }
-            if constexpr (P2P) {   // the tile is complete in this rank's copy: its participants push it to every peer
-                named_sync(2, 128u * (uint32_t)parts);
-                if (ok) tc_push_tile<OutT>(a, row0, tok0, (epi ? warp - TC_WEPI0 : warp - TC_WDQ0 + 4) * 32 + lane,
-                                           128 * parts);
-            }
-        }
+    if (warp >= TC_WEPI0) {   // every tile
+        for (int i = 0; i < ntl && (ok || P2P); ++i) epi_tile(i, 0, i == ntl - 1 ? 3 : 1, true);
+    } else if (warp >= TC_WDQ0 && ntl > 0 && (ok || P2P)) {   // the last tile
+        epi_tile(ntl - 1, 1 + ((warp - TC_WDQ0) >> 2), 3, false);
     }
     // teardown: every MMA has completed (the epilogue waited on each accumulator) before TMEM is released
     if (warp == 1 && !ok && ntl > 0) wait_b(&accfull[(ntl - 1) % a.nacc], ((ntl - 1) / a.nacc) & 1,

@@ -448,53 +448,73 @@ struct TcPlan {
     TcArgs a;
     int pk;     // K steps per packed chunk (kernel template argument)
     int cg;     // CTAs per tile: 1, or 2 (a cluster pair on 256-row tiles, tcgen05 cta_group::2)
+    int rb;     // 128-row blocks per CTA tile: 1, or 2 (two accumulators sharing every activation stage)
     int smem;
     dim3 grid;
 };
 
-// Token tile NT (a multiple of 32, <= 256): the persistent grid (one CTA per SM) walks ceil(tiles / grid) tiles per
-// CTA; a K step costs 4 UMMAs of (32 + 0.41 NT) cycles (measured, A in TMEM) or the dequantisation floor, and a
-// single-buffered accumulator (NT > 128) exposes the epilogue once per extra tile. Ring depths: X stages of up to
-// 32 KB (an even count: two producers), P chunks of 8 K steps when they fit (else 4), both deepened while shared
-// memory lasts. With cg = 2 the units are CTA pairs (at most `units_max` co-resident), a tile has 256 rows and each
-// CTA's X stages hold half of the tile's tokens.
+// Tile shape: rb row blocks of 128 weight rows x NT tokens (NT <= 256, a multiple of 16 above 128 tokens, else of
+// 32; any multiple of 16 when forced); the persistent grid (one CTA per SM) walks ceil(tiles / grid) tiles per CTA.
+// A K step costs 4 UMMAs per row block of (32 + 0.41 NT) cycles (measured in the kernel, A in TMEM) or the
+// dequantisation floor, and a single-buffered accumulator exposes the epilogue once per extra tile. One block: two accumulators when NT <= 128 (the epilogue overlaps the next tile), A
+// slots of 4 K steps (128 TMEM columns). Two blocks (VKB_TC_RB=2 only: it halves the activation stream, but measured
+// slower at every shape of the sweep, e.g. 12288x2560 at 512 tokens 34.0 vs 32.7 us, 8192x2048 24.5 vs 16.2 us):
+// one accumulator per block, A slots of one K step for both blocks (64 columns) in the rest. Ring depths: X stages of
+// up to 32 KB (an even count: two producers), P chunks of 8 K steps when they fit (else 4; 4 with two blocks), both
+// deepened while shared memory lasts. With cg = 2 the units are CTA pairs (at most `units_max` co-resident), a tile
+// has 256 rows and each CTA's X stages hold half of the tile's tokens.
 static bool plan_tc(int N, int K, int M, int out_bytes, const DeviceInfo& d, TcPlan* p, int cg, int units_max,
-                    int wf = 0) {
+                    int wf = 0, bool allow_rb2 = false) {
     TcArgs& a = p->a;
-    const int tiles_n = (N + TC_BM * cg - 1) / (TC_BM * cg);
     const int nk = K / TC_BK;
-    int NT = 0;
+    int NT = 0, RB = 1;
     double best = 1e300;
     const int nt_max = round_up(M, 32) < 256 ? round_up(M, 32) : 256;
-    static const int nt_force = getenv("VKB_TC_NT") ? atoi(getenv("VKB_TC_NT")) : 0;   // tuning override
-    for (int nt = nt_max; nt >= 32; nt -= 32) {
-        if (nt_force > 0 && nt != nt_force && nt_force <= nt_max) continue;
-        const long tiles = (long)tiles_n * ((M + nt - 1) / nt);
-        const long grid = tiles < units_max ? tiles : units_max;
-        const long per_cta = (tiles + grid - 1) / grid;
-        const double umma = 4.0 * (32.0 + 0.41 * nt);
-        const double step = umma > 180.0 ? umma : 180.0;
-        const double epi = nt <= 128 ? 0.0 : 1500.0 + 10.0 * nt;
-        const double t = (double)per_cta * nk * step + (double)(per_cta - 1) * epi + 6000.0;
-        if (t < best * 0.999) { best = t; NT = nt; }
+    static const int nt_force = getenv("VKB_TC_NT") ? atoi(getenv("VKB_TC_NT")) : 0;   // tuning overrides
+    static const int rb_force = getenv("VKB_TC_RB") ? atoi(getenv("VKB_TC_RB")) : 0;
+    const int rb = rb_force == 2 && allow_rb2 && cg == 1 && wf == 0 ? 2 : 1;
+    for (int pass = 0; pass < 2 && NT == 0; ++pass) {   // pass 1: without the NT override (it does not fit)
+        // steps of 16 above 128 tokens (512 = 3 x 176 wastes 3 % of the MMAs, 3 x 192 11 %; measured 1 % faster),
+        // of 32 below (48-token tiles were slower than 64 at 6144x2048 x 128 tokens: more passes over the weights)
+        for (int nt = nt_max; nt >= 32; nt -= ((pass == 0 && nt_force > 0) || nt > 128) && cg == 1 ? 16 : 32) {
+            if (pass == 0 && nt_force > 0 && nt != nt_force) continue;
+            if (rb == 2 && round_up(round_up(nt, 32) + nt, 64) > 384) continue;   // two accumulators, two A slots
+            const long tiles = (long)((N + TC_BM * rb * cg - 1) / (TC_BM * rb * cg)) * ((M + nt - 1) / nt);
+            const long grid = tiles < units_max ? tiles : units_max;
+            const long per_cta = (tiles + grid - 1) / grid;
+            const double umma = 4.0 * rb * (32.0 + 0.41 * nt);
+            const double step = umma > 180.0 * rb ? umma : 180.0 * rb;
+            const double epi = nt <= 128 && rb == 1 ? 0.0 : 1500.0 + 10.0 * nt * rb;
+            const double t = (double)per_cta * nk * step + (double)(per_cta - 1) * epi + 6000.0;
+            if (t < best * 0.999) { best = t; NT = nt; RB = rb; }
+        }
     }
+    if (NT == 0) return false;
+    p->rb = RB;
     a.M = M; a.N = N; a.K = K; a.NT = NT; a.nk = nk;
-    a.tiles_n = tiles_n;
-    a.tiles = tiles_n * ((M + NT - 1) / NT);
-    a.na = 2;
-    a.nacc = NT <= 128 ? 2 : 1;   // TMEM: accumulators at columns 0 / 128, A ring of two 128-column slots from 256
-    a.a_col0 = 256;
+    a.tiles_n = (N + TC_BM * RB * cg - 1) / (TC_BM * RB * cg);
+    a.tiles = a.tiles_n * ((M + NT - 1) / NT);
+    if (RB == 1) {
+        a.na = 2;
+        a.nacc = NT <= 128 ? 2 : 1;   // TMEM: accumulators at columns 0 / 128, A ring of two 128-column slots from 256
+        a.a_col0 = 256;
+    } else {
+        a.nacc = 1;   // TMEM: block accumulators at columns 0 and round_up(NT, 32), A ring of 64-column slots after
+        a.a_col0 = round_up(round_up(NT, 32) + NT, 64);
+        a.na = (512 - a.a_col0) / 64 < 4 ? (512 - a.a_col0) / 64 : 4;
+    }
     a.tmem_cols = 512;
     int xk = 8;
     while (xk > 1 && (xk * (NT / cg) * 128 > 32768 || nk % xk != 0)) xk /= 2;
     (void)out_bytes;
     // Q8 chunks of 8 K steps (74 KB) leave too little room for the activation ring: 4 K steps for Q8 (measured:
-    // 12288x2560 M=512 35.3 vs 52.6 us), 8 for Q4 (either is the same there)
+    // 12288x2560 M=512 35.3 vs 52.6 us), 8 for Q4 (either is the same there); 256-row chunks: 4
     static const int pk_force = getenv("VKB_TC_PK") ? atoi(getenv("VKB_TC_PK")) : 0;   // tuning override
-    const int pk_order[2] = {wf == 1 ? 4 : 8, wf == 1 ? 8 : 4};
+    const int pk_order[2] = {wf == 1 || RB == 2 ? 4 : 8, wf == 1 || RB == 2 ? 8 : 4};
     for (int pk : pk_order) {
-        if (nk % pk != 0 || ((pk_force == 4 || pk_force == 8) && pk != pk_force)) continue;
-        const int pchunk = tc_pchunk(pk, wf);
+        if (nk % pk != 0 || ((pk_force == 4 || pk_force == 8) && pk != pk_force && RB == 1)) continue;
+        if (RB == 2 && pk != 4) continue;
+        const int pchunk = RB * tc_pchunk(pk, wf);
         int nx = 4, np = 2;   // four X stages first: the activations are the fast-consumed stream
         auto bars_bytes = [&]() { return 8 * (2 * np + 2 * nx + 2 * a.na + 2 * a.nacc) + 16; };
         auto total = [&]() { return nx * xk * (NT / cg) * 128 + np * pchunk + bars_bytes() + 1024; };
@@ -522,12 +542,12 @@ static bool plan_tc(int N, int K, int M, int out_bytes, const DeviceInfo& d, TcP
 }
 
 // Opt one prompt-GEMM kernel variant into the device's shared memory, once per device.
-template <typename OutT, int PK, bool P2P, int CG, int WF = 0>
+template <typename OutT, int PK, bool P2P, int CG, int WF = 0, int RB = 1>
 static int tc_attr(int dev, int smem_optin) {
     static std::once_flag once[kMaxDevices];
     static cudaError_t err[kMaxDevices];
     std::call_once(once[dev], [&] {
-        err[dev] = cudaFuncSetAttribute(tc_q4_kernel<OutT, PK, P2P, CG, WF>,
+        err[dev] = cudaFuncSetAttribute(tc_q4_kernel<OutT, PK, P2P, CG, WF, RB>,
                                         cudaFuncAttributeMaxDynamicSharedMemorySize, smem_optin);
     });
     return err[dev] == cudaSuccess ? 0 : -(int)err[dev];
@@ -584,7 +604,8 @@ static int tc_entry(const void* q, const void* s, const void* x, void* y, int N,
         if (units_max < 1) cg = 1, units_max = d.sm_count;
     }
     TcPlan p{};
-    if (!plan_tc(N, K, M, (int)sizeof(OutT), d, &p, cg, units_max, wf)) return VKB_EUNSUPPORTED;
+    const bool p2p = out && out->p2p;
+    if (!plan_tc(N, K, M, (int)sizeof(OutT), d, &p, cg, units_max, wf, !p2p)) return VKB_EUNSUPPORTED;
     p.a.y = y;
     p.a.ldy = out ? out->ldy : N;
     p.a.ycol0 = out ? out->col0 : 0;
@@ -593,10 +614,10 @@ static int tc_entry(const void* q, const void* s, const void* x, void* y, int N,
     if (p.a.p2p && p.grid.x > (unsigned)P2P_MAX_CTAS) return VKB_EUNSUPPORTED;   // one flag pair per CTA
     CUtensorMap tq, ts, tx;
     int r = get_tmap_2d(&tq, q, (uint64_t)N, (uint64_t)(wf == 1 ? K : K / 2), CU_TENSOR_MAP_DATA_TYPE_UINT64, 8,
-                        (uint32_t)tc_ppitch(p.pk, wf) / 8, TC_BM, CU_TENSOR_MAP_SWIZZLE_NONE);
+                        (uint32_t)tc_ppitch(p.pk, wf) / 8, TC_BM * p.rb, CU_TENSOR_MAP_SWIZZLE_NONE);
     if (r) return r;
-    r = get_tmap_2d(&ts, s, (uint64_t)N, (uint64_t)K / 16, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, TC_SPITCH / 2, TC_BM,
-                    CU_TENSOR_MAP_SWIZZLE_NONE);
+    r = get_tmap_2d(&ts, s, (uint64_t)N, (uint64_t)K / 16, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, TC_SPITCH / 2,
+                    TC_BM * p.rb, CU_TENSOR_MAP_SWIZZLE_NONE);
     if (r) return r;
     r = get_tmap_x3d(&tx, x, M, K, p.a.NT / p.cg, p.a.xk);   // a CTA's share of a tile's tokens
     if (r) return r;
@@ -610,6 +631,9 @@ static int tc_entry(const void* q, const void* s, const void* x, void* y, int N,
         } else {
             return VKB_EUNSUPPORTED;
         }
+    } else if (p.rb == 2) {   // 256-row tiles in one CTA (Q4, chunks of 4 K steps)
+        kern = tc_q4_kernel<OutT, 4, false, 1, 0, 2>;
+        ra = tc_attr<OutT, 4, false, 1, 0, 2>(dev, d.smem_optin);
     } else if (wf == 1) {   // Q8 weights
         kern = p.pk == 8 ? tc_q4_kernel<OutT, 8, false, 1, 1> : tc_q4_kernel<OutT, 4, false, 1, 1>;
         ra = p.pk == 8 ? tc_attr<OutT, 8, false, 1, 1>(dev, d.smem_optin)
