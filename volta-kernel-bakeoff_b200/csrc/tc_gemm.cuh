@@ -314,12 +314,13 @@ __device__ __noinline__ void tc_push_tile(const TcArgs& a, int row0, int tok0, i
 // complete on the leader's barrier); the leader's commits arrive on both CTAs' barriers. No TMA multicast.
 // WF: weight format, 0 = Q4 (the reference's tc_q4), 1 = Q8 (the tc_q8 it planned, SURVEY's next rows): only the packed
 // chunk layout and the dequantisation differ.
-// RB = 2: one CTA holds a 256-row tile as two 128-row blocks, each with its own accumulator (TMEM columns 0 and NT
-// rounded up to 32), and every activation K step feeds the MMAs of both blocks: the activations are streamed from L2
-// once per 256 weight rows instead of once per 128. That stream (re-read once per row tile: N / 128 times the activations) is what bounds
-// the one-block kernel at 512 tokens (measured: the activation and weight streams alone, without MMAs or
-// dequantisation, take two thirds of its time at 12288x2560). A slots hold one K step of both blocks (64 columns);
-// dequantising group g (four warps) converts block g.
+// RB = 2 (opt-in, VKB_TC_RB=2): one CTA holds a 256-row tile as two 128-row blocks, each with its own accumulator
+// (TMEM columns 0 and NT rounded up to 32), and every activation K step feeds the MMAs of both blocks: the activations
+// are streamed from L2 once per 256 weight rows instead of once per 128 (that stream, N / 128 times the activations,
+// takes two thirds of the one-block kernel's time at 12288x2560 x 512 tokens when its MMAs and dequantisation are
+// compiled out). A slots hold one K step of both blocks (64 columns); dequantising group g (four warps) converts block
+// g. Measured slower than one block at every shape (the MMA issue loop and the 2-slot A ring bound it first), so the
+// planner never picks it.
 template <typename OutT, int PK, bool P2P, int CG, int WF = 0, int RB = 1>
 __global__ void __launch_bounds__(TC_THREADS, 1)
 tc_q4_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap ts,
@@ -510,15 +511,15 @@ tc_q4_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUt
     } else if (warp == 1 && leader) {
         // ===================== MMA issuer (the pair leader's, CG = 2) =====================
         // Per slot: wait for its A (TMEM) and the X stages its SK K steps read, then 4 UMMAs per K step and row block
-        // (16 per slot), issued by one elected lane. tcgen05.mma issue blocks while the tensor pipe's queue is full
-        // (it holds about one instruction), so every cycle this warp spends between two UMMAs is tensor-pipe idle
-        // time. Its waits therefore test the phase first (mbarrier.test_wait, in wait_parity_sleep) and sleep in
-        // try_wait only when it is not complete (measured: a sleeping try_wait on a completed phase cost ~150-300
-        // cycles per wait, ~150 cycles per UMMA in all; the test first: 5 % off 12288x2560 at 512 tokens; one lane
-        // running the loop alone, polling or sleeping, was slower still). When the X ring holds at least two slots of K steps all
-        // of a slot's X waits come first and its UMMAs issue back to back; otherwise (large token tiles, shallow X
-        // ring) the waits interleave with the K steps so that each X stage is released as soon as its own MMAs
-        // complete.
+        // (16 per slot with one block), issued by one elected lane, the warp reconverged after each issue block.
+        // tcgen05.mma issue blocks while the tensor pipe's queue is full (it holds about one instruction), so every
+        // cycle this warp spends between two UMMAs is tensor-pipe idle time. Its waits therefore test the phase first
+        // (mbarrier.test_wait, in wait_parity_sleep) and sleep in try_wait only when it is not complete (measured: a
+        // sleeping try_wait on a completed phase cost ~150-300 cycles per wait, ~150 cycles per UMMA in all; testing
+        // first took 5 % off 12288x2560 at 512 tokens; one lane running the loop alone, or issuing without elect.sync
+        // and __syncwarp, was 4-30 % slower). When the X ring holds at least two slots of K steps all of a slot's X
+        // waits come first and its UMMAs issue back to back; otherwise (large token tiles, shallow X ring) the waits
+        // interleave with the K steps so that each X stage is released as soon as its own MMAs complete.
         {
             auto wait_m = [&](uint64_t* bar, uint32_t par) { return __all_sync(0xffffffffu, wait_b(bar, par)); };
             const uint32_t idesc = umma_idesc_f16(a.NT, TC_BM * CG);
