@@ -170,7 +170,11 @@ static int round_up(int v, int m) { return (v + m - 1) / m * m; }
 
 // Stage: 16 rows x KS values, up to 1.5 KB of codes per row (one TMA box each for codes and scales, rows padded so
 // the fragment reads are conflict free); ring as deep as fits, preferring a footprint that lets a second CTA (the
-// next call, under PDL) share the SM.
+// next call, under PDL) share the SM when that still leaves at least 4 stages. The two-CTA footprint pays only while
+// the previous call's CTA can share the SM as well: after a one-CTA call its shallow ring streams the weights without
+// the head start. Measured on B200 (bench.py, the configs[1] graph of 48 different calls): minimum 3 stages 1385 GB/s,
+// 4 stages 1487 GB/s, one CTA always 1622 GB/s; one shape repeated (8192x2048 Q4, 1 token): 4.7 / 4.7 / 5.8 us. 4 keeps the
+// repeated-call time and takes part of the chain gain.
 // glu: gate/up tile pairs over a [2N][K] table (N output rows, 2 ceil(N / 16) tiles, the gate hand-over slots after
 // the reduction region).
 static bool plan_qmv(int fmt, int N, int K, int xrows, int moe_slots, int E_local, const DeviceInfo& d, QmvPlan* p,
@@ -193,12 +197,13 @@ static bool plan_qmv(int fmt, int N, int K, int xrows, int moe_slots, int E_loca
     auto fixed_for = [&](int nstage) { return 8 * qmv_nbars(nstage) + xbytes + redbytes + moebytes + slack; };
     const int pair_budget = d.smem_per_sm / 2 - 1024;   // two CTAs per SM
     const int solo_budget = d.smem_optin;
+    static const int pair_min = getenv("VKB_QMV_PAIRMIN") ? atoi(getenv("VKB_QMV_PAIRMIN")) : 4;   // tuning override
     int nstage = 0, budget = pair_budget;
     for (int pass = 0; pass < 2; ++pass) {
         budget = pass == 0 ? pair_budget : solo_budget;
         nstage = 16;
         while (nstage >= 2 && nstage * stage_bytes + fixed_for(nstage) > budget) --nstage;
-        if (nstage >= 3 || (pass == 1 && nstage >= 2)) break;
+        if (nstage >= pair_min || (pass == 1 && nstage >= 2)) break;
     }
     if (nstage < 2) return false;
     QmvArgs& a = p->a;
