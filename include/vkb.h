@@ -208,6 +208,22 @@ int vkb_set_pdl(int enable);
 /* Library version, e.g. 100 for 0.1.0. */
 int vkb_version(void);
 
+/* ---- plan inspection -------------------------------------------------------------------------------------------------
+ * The launch plan the library would use for a shape on a device with `sm_count` SMs and the given shared-memory
+ * limits (bytes: per block with opt-in, per SM). Host only: no CUDA call, no device needed (tuning overrides in the
+ * environment apply). Fills info[0 .. VKB_PLAN_INFO_LEN - 1]; returns 0, VKB_EUNSUPPORTED when the pipelined kernel
+ * does not take the shape, or VKB_EINVAL.
+ *   kind 0, decode GEMV (fmt Q4 / Q8 / Q2, M = 1-8 tokens) and kind 2, gate + up over the stacked [2N][K] Q4 table:
+ *     info = {smem, ring stages, stages per row tile, K values per stage, warp groups, stage bytes, grid, code pitch,
+ *             scale pitch, row tiles}
+ *   kind 1, prompt GEMM (fmt Q4 / Q8, any M), one CTA per tile:
+ *     info = {smem, tokens per tile NT, 128-row blocks per tile, TMEM accumulators, A slots, first A column, TMEM
+ *             columns, X stages, K steps per X stage, P chunks, K steps per P chunk, grid, tiles, X stage bytes,
+ *             row tiles, CTAs per tile} */
+#define VKB_PLAN_INFO_LEN 16
+int vkb_plan_describe(int kind, int fmt, int N, int K, int M, int sm_count, int smem_optin, int smem_per_sm,
+                      int* info);
+
 #ifdef __cplusplus
 }
 #endif

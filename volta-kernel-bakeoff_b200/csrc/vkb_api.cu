@@ -820,4 +820,35 @@ int vkb_set_pdl(int enable) {
 
 int vkb_version(void) { return 100; }
 
+int vkb_plan_describe(int kind, int fmt, int N, int K, int M, int sm_count, int smem_optin, int smem_per_sm,
+                      int* info) {
+    if (!info || N < 1 || K < 1 || M < 1 || sm_count < 1 || smem_optin < 1 || smem_per_sm < 1) return VKB_EINVAL;
+    for (int i = 0; i < VKB_PLAN_INFO_LEN; ++i) info[i] = 0;
+    const DeviceInfo d{sm_count, smem_optin, smem_per_sm, 10};
+    if (kind == 0 || kind == 2) {   // decode GEMV / gate + up over [2N][K] (the pipelined kernel's shapes only)
+        if (fmt < VKB_FMT_Q4 || fmt > VKB_FMT_Q2 || (kind == 2 && fmt != VKB_FMT_Q4)) return VKB_EINVAL;
+        if (M > QMV_MAXTOK) return VKB_EUNSUPPORTED;
+        if (K % 256 != 0) return VKB_EUNSUPPORTED;
+        QmvPlan p{};
+        if (!plan_qmv(fmt, N, K, M, 0, 0, d, &p, kind == 2)) return VKB_EUNSUPPORTED;
+        const QmvArgs& a = p.a;
+        const int v[] = {p.smem, a.nstage, a.nchunks, a.KS, a.wg, a.stage_bytes,
+                         a.tilesN < sm_count ? a.tilesN : sm_count, a.cpitch, a.spitch, a.tilesN};
+        for (int i = 0; i < (int)(sizeof(v) / sizeof(v[0])); ++i) info[i] = v[i];
+        return 0;
+    }
+    if (kind == 1) {   // prompt GEMM, one CTA per tile (the planner's default kernel family)
+        if (fmt != VKB_FMT_Q4 && fmt != VKB_FMT_Q8) return VKB_EINVAL;
+        if (K < 256 || K % 256 != 0) return VKB_EUNSUPPORTED;
+        TcPlan p{};
+        if (!plan_tc(N, K, M, 2, d, &p, 1, sm_count, fmt == VKB_FMT_Q8 ? 1 : 0, true)) return VKB_EUNSUPPORTED;
+        const TcArgs& a = p.a;
+        const int v[] = {p.smem, a.NT, p.rb, a.nacc, a.na, a.a_col0, a.tmem_cols, a.nx, a.xk, a.np, p.pk,
+                         (int)p.grid.x, a.tiles, a.x_stage, a.tiles_n, p.cg};
+        for (int i = 0; i < (int)(sizeof(v) / sizeof(v[0])); ++i) info[i] = v[i];
+        return 0;
+    }
+    return VKB_EINVAL;
+}
+
 }  // extern "C"

@@ -110,12 +110,37 @@ def _register_optional(L) -> None:
         "vkb_graph_end": ([vp, ctypes.POINTER(vp)], i),
         "vkb_graph_launch": ([vp, vp], i),
         "vkb_graph_destroy": ([vp], i),
+        "vkb_plan_describe": ([i, i, i, i, i, i, i, i, vp], i),
     }
     for name, (args, res) in opt.items():
         if hasattr(L, name):
             f = getattr(L, name)
             f.argtypes = args
             f.restype = res
+
+
+# B200: 148 SMs, 227 KB of shared memory per block (opt-in), 228 KB per SM
+B200_LIMITS = {"sm_count": 148, "smem_optin": 232448, "smem_per_sm": 233472}
+PLAN_GEMV, PLAN_TC, PLAN_GLU = 0, 1, 2
+_PLAN_FIELDS = {
+    PLAN_GEMV: ("smem", "nstage", "nchunks", "KS", "wg", "stage_bytes", "grid", "cpitch", "spitch", "tiles"),
+    PLAN_GLU: ("smem", "nstage", "nchunks", "KS", "wg", "stage_bytes", "grid", "cpitch", "spitch", "tiles"),
+    PLAN_TC: ("smem", "NT", "rb", "nacc", "na", "a_col0", "tmem_cols", "nx", "xk", "np", "pk", "grid", "tiles",
+              "x_stage", "tiles_n", "cg"),
+}
+
+
+def plan(kind: int, fmt: int, N: int, K: int, M: int, sm_count: int = 148, smem_optin: int = 232448,
+         smem_per_sm: int = 233472) -> dict | None:
+    """The launch plan the library would use (vkb_plan_describe; host only, no device needed): a dict of named
+    fields, or None when the pipelined kernel does not take the shape."""
+    info = (ctypes.c_int * 16)()
+    rc = lib().vkb_plan_describe(kind, fmt, N, K, M, sm_count, smem_optin, smem_per_sm, ctypes.cast(info,
+                                                                                                     ctypes.c_void_p))
+    if rc == EUNSUPPORTED:
+        return None
+    check(rc, "vkb_plan_describe")
+    return dict(zip(_PLAN_FIELDS[kind], info))
 
 
 def strerror(code: int) -> str:
