@@ -30,6 +30,14 @@ def test_library_exports_every_declared_symbol():
     assert not missing, missing
 
 
+def test_every_declared_symbol_has_a_binding():
+    """vkb.lib() sets argument and result types for every entry point the headers declare (a ctypes call without them
+    would pass 64-bit pointers as C ints)."""
+    L = vkb.lib()
+    unbound = [n for n in _declared_symbols() if getattr(L, n).argtypes is None]
+    assert not unbound, unbound
+
+
 def test_strerror_and_version():
     assert vkb.lib().vkb_version() >= 100
     assert "unsupported" in vkb.strerror(vkb.EUNSUPPORTED)

@@ -57,6 +57,7 @@ def lib() -> ctypes.CDLL:
     L.vkb_device_status.restype = i
     L.vkb_set_pdl.argtypes = [i]
     L.vkb_set_pdl.restype = i
+    L.vkb_version.argtypes = []
     L.vkb_version.restype = i
     L.vkb_quantize.argtypes = [i, vp, i, i, vp, vp]
     L.vkb_quantize.restype = i
