@@ -212,7 +212,8 @@ int vkb_version(void);
  * The launch plan the library would use for a shape on a device with `sm_count` SMs and the given shared-memory
  * limits (bytes: per block with opt-in, per SM). Host only: no CUDA call, no device needed (tuning overrides in the
  * environment apply). Fills info[0 .. VKB_PLAN_INFO_LEN - 1]; returns 0, VKB_EUNSUPPORTED when the pipelined kernel
- * does not take the shape, or VKB_EINVAL.
+ * does not take the shape, or VKB_EINVAL. No counterpart in the reference, whose launchers fix their tiles at
+ * compile time (src/stage2.cuh:217-229).
  *   kind 0, decode GEMV (fmt Q4 / Q8 / Q2, M = 1-8 tokens) and kind 2, gate + up over the stacked [2N][K] Q4 table:
  *     info = {smem, ring stages, stages per row tile, K values per stage, warp groups, stage bytes, grid, code pitch,
  *             scale pitch, row tiles}
