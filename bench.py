@@ -12,18 +12,24 @@ fairness rule, src/bakeoff.cu:16-18, :314, with 96 MB raised to 4x B200's L2).
 
 Metric: aggregate decode-GEMV HBM throughput in GB/s = algorithmic bytes (packed codes + fp16 scales + x + y) of the
 step / step time, and the reference's own µs per call for each case (time_us: 5 batches of 50 back-to-back calls,
-median), including configs[0] (Q4_0 8192x2048, 1 token).
+median), including configs[0] (Q4_0 8192x2048, 1 token), with cuBLAS bf16 on the same GPU beside every case.
 
 Multi-GPU: the dense GEMV does not shard (replicas only): every rank runs the whole step on its own GPU; value sums the
-ranks' bytes over the slowest rank's time (weak scaling).
+ranks' bytes over the slowest rank's time (weak scaling). The paths that do shard -- the expert-parallel MoE
+(configs[2]/[3]) and the row-split prompt GEMM -- are timed beside their one-GPU time in "sharded", each
+case with its parity against the one-GPU kernel (bit for bit, NCCL and fused combines); a mismatch makes the run exit
+non-zero after the JSON line.
 
-Extra fields of the same JSON line: "prompt_gemm" (configs[4]: the tcgen05 Q4 prompt GEMM at 64 and 512 tokens against
-cuBLAS bf16 on the same GPU), "moe" (configs[2]/[3] one-launch MoE, µs per call), and with N > 1 GPUs "sharded": the
-expert-parallel MoE and the row-split prompt GEMM across the ranks (max over ranks).
+Extra fields of the same JSON line: "prompt_gemm" (configs[4] against cuBLAS bf16), "moe" (configs[2]/[3]),
+"f32in_and_glu" (the reference's fp32-in and gate/up entries) and, on one GPU, "reference_kernels": the reference's
+own kernels rebuilt for sm_100a (baseline/) timed on the same GPU and weights as ours (baseline/time_ref_kernels.py, in a
+child process).
 
 The reference arm (--impl reference) times the reference's own CPU path, ref_value (src/bakeoff.cu:221-227, compiled
-from the reference source into oracle/_ref/ by oracle/Makefile), on all host cores over a bounded sample of each
-step's outputs, scaled to the full step.
+from the reference source into oracle/_ref/ by oracle/Makefile), on all host cores over the step's outputs -- all of
+them when the run's budget allows, else the same leading rows of every case, reported unscaled. Its inputs are built
+without libvkb.so (oracle/_ref's input generator and the numpy quantiser). Our arm's cpu_baseline is the same
+procedure.
 """
 from __future__ import annotations
 
@@ -68,13 +74,14 @@ class ClockSampler:
     def __init__(self, gpu_index: int):
         self.gpu = gpu_index
         self.proc = None
-        self.path = os.path.join(ROOT, "gpurun_out", f"clocks_gpu{gpu_index}.csv")
+        self.path = None
 
     def start(self):
+        import tempfile
         from vkb import load_judge
         try:
-            os.makedirs(os.path.dirname(self.path), exist_ok=True)
-            self.f = open(self.path, "w")
+            fd, self.path = tempfile.mkstemp(prefix=f"vkb_clocks_gpu{self.gpu}_", suffix=".csv")
+            self.f = os.fdopen(fd, "w")
             self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={load_judge.SAMPLE_FIELDS}",
                                           "--format=csv,noheader,nounits", "-i", str(self.gpu), "-lms", "20"],
                                          stdout=self.f, stderr=subprocess.DEVNULL)
@@ -94,42 +101,52 @@ class ClockSampler:
         self.f.close()
         with open(self.path, encoding="utf-8", errors="replace") as fh:
             v = load_judge.judge(fh.read())
+        os.unlink(self.path)
         return {"sm_mhz": v.median_clock, "sm_max_mhz": v.max_clock, "reasons": v.reason_names(),
                 "samples": v.busy, "flagged": v.flagged, "judge": load_judge.format_line("timed", v)}
 
 
 # ---- the reference's CPU path ----------------------------------------------------------------------------------------
 
-def cpu_reference_step(cases, frac: float, threads: int):
-    """Times the reference's ref_value (oracle/_ref) over the first frac of every case's output rows, all threads;
-    returns (seconds for the full step, scaled; kind; sample description). Falls back to the numpy oracle port when the
-    reference library is not built."""
-    import numpy as np
+def cpu_reference(cases, threads: int, frac: float):
+    """One step of the reference's CPU path: its ref_value (oracle/_ref, src/bakeoff.cu:221-227) over the leading
+    `frac` of every case's output rows (all of them at frac = 1), on `threads` host threads. Returns (seconds,
+    algorithmic bytes of the outputs computed). Falls back to the numpy oracle port when the reference library is not
+    built."""
     from oracle import refbind
     L = refbind.load()
-    t_total = 0.0
+    t_total, nbytes = 0.0, 0.0
     for c in cases:
-        rows = max(16, int(c["N"] * frac))
+        rows = c["N"] if frac >= 1.0 else max(16, int(c["N"] * frac))
+        t0 = time.perf_counter()
         if L is not None:
-            t0 = time.perf_counter()
             refbind.gemv_mt(c["codes"][:rows], c["scales"][:rows], c["x"], 0, rows, threads)
-            dt = time.perf_counter() - t0
         else:
             from oracle import oracle as O
-            t0 = time.perf_counter()
             O.ref_value(c["codes"][:rows], c["scales"][:rows], c["x"])
-            dt = time.perf_counter() - t0
-        t_total += dt * c["N"] / rows
-    kind = "reference" if L is not None else "port"
-    sample = f"first {frac:.3g} of the output rows of each of the {len(cases)} step cases, scaled to the full step"
-    return t_total, kind, sample
+        t_total += time.perf_counter() - t0
+        nbytes += case_bytes(c["bw"], rows, c["K"], c["M"])
+    return t_total, nbytes
 
 
-def cpu_frac_for(cases, threads: int, budget_s: float) -> float:
-    """The sampled row fraction that makes one CPU step take about budget_s (from a tiny calibration sample)."""
-    f0 = 1.0 / 1024
-    t0, _, _ = cpu_reference_step(cases, f0, threads)   # t0 is already scaled to the full step
-    return max(1.0 / 4096, min(0.25, budget_s / max(t0, 1e-9)))
+def cpu_plan(cases, threads: int, steps: int, budget_s: float) -> float:
+    """The output-row fraction per step that keeps `steps` CPU steps within about budget_s (1.0 when the full step
+    fits), from a timed 1/64 sample."""
+    t, _ = cpu_reference(cases, threads, 1.0 / 64)
+    full = t * 64
+    return 1.0 if full * steps <= budget_s else max(1.0 / 4096, budget_s / steps / full)
+
+
+def cpu_kind() -> str:
+    from oracle import refbind
+    return "reference" if refbind.load() is not None else "port"
+
+
+def cpu_sample_text(frac: float, ncases: int) -> str:
+    if frac >= 1.0:
+        return f"every output of the {ncases} step cases (the full step, nothing scaled)"
+    return (f"the first {frac:.3g} of the output rows of each of the {ncases} step cases per step; value = those "
+            f"outputs' algorithmic bytes / their time, unscaled")
 
 
 def gpu_index(local_rank: int) -> int:
@@ -141,17 +158,35 @@ def gpu_index(local_rank: int) -> int:
     return local_rank
 
 
-def host_cases(for_cpu: bool = True):
-    """Host-side weights/activations of the 48 step cases (codes int8, fp16 scales and x as uint16 bits)."""
-    import vkb
+def host_cases(source: str = "vkb"):
+    """Host-side weights/activations of the 48 step cases (codes int8, fp16 scales and x as uint16 bits). source
+    "vkb": the library's host functions (our arm); "oracle": oracle/_ref's input generator and the numpy quantiser (the
+    reference arm, which loads no libvkb.so) -- the same bits (tests/test_oracle.py)."""
+    import numpy as np
+    if source == "vkb":
+        import vkb
+        normal, quantize, f16 = vkb.synth_normal, vkb.quantize, vkb.to_f16_bits
+    else:
+        from oracle import oracle as O
+        from oracle import refbind
+        normal, quantize = refbind.synth_normal, O.quantize
+        f16 = lambda a: np.ascontiguousarray(a, dtype=np.float32).astype(np.float16).view(np.uint16)  # noqa: E731
     cases = []
     for fname, fmt, bw in FORMATS:
         for N, K in SHAPES:
-            codes, scales = vkb.quantize(fmt, vkb.synth_normal(0, (N, K), 0.02))
+            codes, scales = quantize(fmt, normal(0, (N, K), 0.02))
             for M in TOKENS:
-                x = vkb.to_f16_bits(vkb.synth_normal(1 + M, (M, K), 1.0))
+                x = f16(normal(1 + M, (M, K), 1.0))
                 cases.append(dict(fname=fname, fmt=fmt, bw=bw, N=N, K=K, M=M, codes=codes, scales=scales, x=x))
     return cases
+
+
+def bench_config():
+    """The workload's config, identical in both arms."""
+    return {"workload": "configs[1]: dense quantised GEMV sweep, 48 calls per step",
+            "tables": [f"{n}x{k}" for n, k in SHAPES], "tokens": TOKENS, "formats": [f[0] for f in FORMATS],
+            "step_bytes": step_bytes(),
+            "l2": "inputs larger than L2: every call reads a different copy; each table's copies cycle >= 4x L2"}
 
 
 # ---- extra sections: prompt GEMM, MoE, sharded paths -------------------------------------------------------------
@@ -211,8 +246,8 @@ def _copies(nbytes: int, L2: int) -> int:
 
 def prompt_section(torch, vkb, dev, stream, L2, peaks):
     """configs[4] on one GPU: the tcgen05 prompt GEMM against cuBLAS bf16 (torch.matmul, bf16 in and out) at the same
-    shapes, weights cycled over >= 4x L2 for both; the same shapes with Q8 weights (the Q8 prompt kernel, SURVEY
-    8(f)) as q8_* entries."""
+    shapes, weights cycled over >= 4x L2 for both; the same shapes with Q8 weights (the Q8 prompt kernel the reference
+    planned but never built) as q8_* entries."""
     out = {}
     for N, K in PROMPT_SHAPES:
         sets = {}
@@ -243,48 +278,32 @@ def prompt_section(torch, vkb, dev, stream, L2, peaks):
     return out
 
 
-def moe_section(torch, vkb, dev, stream, L2, comm=None, rank=0, world=1):
+def moe_section(torch, vkb, dev, stream, L2):
+    """configs[2]/[3] on one GPU: one-launch MoE over a device index list, T tokens x k distinct experts."""
     import numpy as np
-    """configs[2]/[3]: one-launch MoE over a device index list, T tokens x k distinct experts. With a communicator,
-    the experts are split over the ranks (vkb_moe_ep: own slots + zeros, in-place all-reduce)."""
-    from vkb import dist as D
     out = {}
     for name, E, k, N, K, Ts in MOE_CASES:
-        e0, el = D.expert_range(E, world, rank) if comm is not None else (0, E)
-        codes, scales = vkb.quantize(0, vkb.synth_normal(7, (el * N, K), 0.02))
-        q0 = vkb.to_device_packed(vkb.pack(0, codes), dev).view(el, N, -1)
-        s0 = vkb.to_device_f16(scales, dev).view(el, N, K // 32)
+        codes, scales = vkb.quantize(0, vkb.synth_normal(7, (E * N, K), 0.02))
+        q0 = vkb.to_device_packed(vkb.pack(0, codes), dev).view(E, N, -1)
+        s0 = vkb.to_device_f16(scales, dev).view(E, N, K // 32)
         per_expert = N * K * 0.5625
-        n = _copies(int(el * per_expert), L2)
+        n = _copies(int(E * per_expert), L2)
         ql, sl = [q0] + [q0.clone() for _ in range(n - 1)], [s0] + [s0.clone() for _ in range(n - 1)]
         for T in Ts:
             idx_np = vkb.synth_topk(11 + T, T, E, k)
             idx = torch.from_numpy(idx_np).to(dev)
             x = vkb.to_device_f16(vkb.to_f16_bits(vkb.synth_normal(13, (T, K), 1.0)), dev)
             y = torch.empty((T, k, N), dtype=torch.float16, device=dev)
-            us_p2p = None
-            if comm is None:
-                us = _median_us(torch, stream, lambda i: vkb.moe(0, ql[i % n], sl[i % n], idx, x, y=y))
-            else:
-                us = _median_us(torch, stream, lambda i: comm.moe_ep(ql[i % n], sl[i % n], idx, x, E_local=el,
-                                                                      e0=e0, y=y), graph=False)
-                ysym = comm.alloc((T, k, N), torch.float16)
-                us_p2p = _median_us(torch, stream, lambda i: comm.moe_ep_p2p(ql[i % n], sl[i % n], idx, x, E_local=el,
-                                                                              e0=e0, y_sym=ysym))
-                torch.cuda.synchronize()
-                ysym.free()
+            us = _median_us(torch, stream, lambda i: vkb.moe(0, ql[i % n], sl[i % n], idx, x, y=y))
             U = len(np.unique(idx_np))
             nbytes = U * per_expert + idx_np.nbytes + T * K * 2 + T * k * N * 2
-            out[f"{name}_t{T}"] = {"us": round(us, 2), "distinct_experts": U,
-                                   "GBps": round(nbytes / us / 1e3, 1) if comm is None else None}
-            if us_p2p is not None:
-                out[f"{name}_t{T}"]["us_p2p"] = round(us_p2p, 2)
+            out[f"{name}_t{T}"] = {"us": round(us, 2), "distinct_experts": U, "GBps": round(nbytes / us / 1e3, 1)}
         del ql, sl
     return out
 
 
 def glu_section(torch, vkb, dev, stream, L2):
-    """SURVEY 8(f) row 1, the reference's like-for-like decode entries: Q4 decode with fp32 activations (rounded to
+    """The reference's like-for-like decode entries (fused_q4_v3_fp32in, gate_up_glu_fp32in): Q4 decode with fp32 activations (rounded to
     fp16 inside the kernel) on configs[0]'s table, and gate + up + SwiGLU (Qwen3-1.7B's MLP, gate and up 6144x2048
     stacked) with fp32 activations, one kernel; weights cycled over >= 4x L2. GB/s: packed weights + activations +
     outputs per call."""
@@ -316,32 +335,122 @@ def glu_section(torch, vkb, dev, stream, L2):
     return out
 
 
-def rowsplit_section(torch, vkb, dev, stream, L2, comm, rank, world):
-    """configs[4] with the weight rows split over the ranks (vkb_gemm_q4_tc_rowsplit: local tcgen05 GEMM, in-place
-    all-gather, permute)."""
+def _fp64_err(torch, codes, scales, x_bits, y, rows, dev) -> float:
+    """The reference's error metric, max |y - ref| / sum |x w| (src/bakeoff.cu:565-583), on the output rows `rows` of
+    every token, with ref computed in float64 by torch on the device from the host codes and scales (a sampled
+    slice: the -m gpu tests hold the full oracle comparisons)."""
+    import numpy as np
+    c = torch.from_numpy(np.ascontiguousarray(codes[rows])).to(dev).double()
+    sc = torch.from_numpy(np.ascontiguousarray(scales[rows]).view(np.float16).astype(np.float64)).to(dev)
+    w = c * sc.repeat_interleave(32, dim=1)
+    x = torch.from_numpy(np.ascontiguousarray(x_bits).view(np.float16).astype(np.float64)).to(dev)
+    ref = x @ w.t()
+    mag = x.abs() @ w.abs().t()
+    got = y[:, rows].double()
+    return float(((got - ref).abs() / (mag + 1e-12)).max())
+
+
+def sharded_section(torch, vkb, dev, stream, L2, comm, rank, world):
+    """The paths that shard, each case on `world` GPUs beside the same problem on one GPU (every rank times the whole
+    problem on its own GPU; all times max over ranks):
+      MoE expert parallel (configs[2]/[3]): vkb_moe_ep (own slots + zeros, NCCL all-reduce) and vkb_moe_ep_p2p (the
+        combine fused into the kernel, peer stores);
+      prompt row split: vkb_gemm_q4_tc_rowsplit (NCCL all-gather + permute) and _p2p (the all-gather fused
+        into the tcgen05 epilogue).
+    parity: both results equal the one-GPU kernel's bit for bit on every rank (the combines only add zeros or move
+    values); err_fp64: the reference's error metric on a sampled slice against a float64 product."""
+    import numpy as np
     from vkb import dist as D
-    out = {}
+    moe, rows = {}, {}
+    for name, E, k, N, K, Ts in MOE_CASES:
+        codes, scales = vkb.quantize(0, vkb.synth_normal(7, (E * N, K), 0.02))
+        qf = vkb.to_device_packed(vkb.pack(0, codes), dev).view(E, N, -1)
+        sf = vkb.to_device_f16(scales, dev).view(E, N, K // 32)
+        e0, el = D.expert_range(E, world, rank)
+        q0, s0 = qf[e0:e0 + el].contiguous(), sf[e0:e0 + el].contiguous()
+        n = _copies(int(el * N * K * 0.5625), L2)
+        ql, sl = [q0] + [q0.clone() for _ in range(n - 1)], [s0] + [s0.clone() for _ in range(n - 1)]
+        nf = _copies(int(E * N * K * 0.5625), L2)
+        qfl, sfl = [qf] + [qf.clone() for _ in range(nf - 1)], [sf] + [sf.clone() for _ in range(nf - 1)]
+        for T in Ts:
+            idx_np = vkb.synth_topk(11 + T, T, E, k)
+            idx = torch.from_numpy(idx_np).to(dev)
+            x_bits = vkb.to_f16_bits(vkb.synth_normal(13, (T, K), 1.0))
+            x = vkb.to_device_f16(x_bits, dev)
+            y = torch.empty((T, k, N), dtype=torch.float16, device=dev)
+            y1 = torch.empty((T, k, N), dtype=torch.float16, device=dev)
+            ysym = comm.alloc((T, k, N), torch.float16)
+            # parity first, on weight copy 0
+            y_one = vkb.moe(0, qf, sf, idx, x)
+            y_nccl = comm.moe_ep(q0, s0, idx, x, E_local=el, e0=e0)
+            comm.moe_ep_p2p(q0, s0, idx, x, E_local=el, e0=e0, y_sym=ysym)
+            torch.cuda.synchronize()
+            same = bool(torch.equal(y_one, y_nccl)) and bool(torch.equal(y_one, ysym.tensor()))
+            # fp64 slice: slots of token 0, output rows 0..63 of each slot's expert
+            err = 0.0
+            for j in range(k):
+                e = int(idx_np[0, j])
+                err = max(err, _fp64_err(torch, codes[e * N:(e + 1) * N], scales[e * N:(e + 1) * N], x_bits[:1],
+                                         y_nccl[0, j:j + 1], np.arange(min(64, N)), dev))
+            us1 = _median_us(torch, stream, lambda i: vkb.moe(0, qfl[i % nf], sfl[i % nf], idx, x, y=y1))
+            us = _median_us(torch, stream, lambda i: comm.moe_ep(ql[i % n], sl[i % n], idx, x, E_local=el, e0=e0,
+                                                                  y=y), graph=False)
+            us_p2p = _median_us(torch, stream, lambda i: comm.moe_ep_p2p(ql[i % n], sl[i % n], idx, x, E_local=el,
+                                                                          e0=e0, y_sym=ysym))
+            torch.cuda.synchronize()
+            ysym.free()
+            moe[f"{name}_t{T}"] = {"us_1gpu": us1, "us": us, "us_p2p": us_p2p, "parity": same, "err_fp64": err}
+        del ql, sl, qfl, sfl
     for N, K in PROMPT_SHAPES:
+        codes, scales = vkb.quantize(0, vkb.synth_normal(0, (N, K), 0.02))
+        qf = vkb.to_device_packed(vkb.pack(0, codes), dev)
+        sf = vkb.to_device_f16(scales, dev)
         n0, nl = D.row_range(N, world, rank)
-        codes, scales = vkb.quantize(0, vkb.synth_normal(0, (N, K), 0.02)[n0:n0 + nl])
-        q0 = vkb.to_device_packed(vkb.pack(0, codes), dev)
-        s0 = vkb.to_device_f16(scales, dev)
+        q0, s0 = qf[n0:n0 + nl].contiguous(), sf[n0:n0 + nl].contiguous()
         nq = _copies(q0.numel() + 2 * s0.numel(), L2)
         ql, sl = [q0] + [q0.clone() for _ in range(nq - 1)], [s0] + [s0.clone() for _ in range(nq - 1)]
+        nf = _copies(qf.numel() + 2 * sf.numel(), L2)
+        qfl, sfl = [qf] + [qf.clone() for _ in range(nf - 1)], [sf] + [sf.clone() for _ in range(nf - 1)]
         for M in PROMPT_TOKENS:
-            x = vkb.to_device_f16(vkb.to_f16_bits(vkb.synth_normal(5, (M, K), 1.0)), dev)
+            x_bits = vkb.to_f16_bits(vkb.synth_normal(5, (M, K), 1.0))
+            x = vkb.to_device_f16(x_bits, dev)
             y = torch.empty((M, N), dtype=torch.float16, device=dev)
+            y1 = torch.empty((M, N), dtype=torch.float16, device=dev)
             work = torch.empty(vkb.lib().vkb_gemm_rowsplit_work_bytes(M, N, 0), dtype=torch.uint8, device=dev)
+            ysym = comm.alloc((M, N), torch.float16)
+            y_one = vkb.gemm_tc(qf, sf, x)
+            y_nccl = comm.gemm_rowsplit(q0, s0, x, N, work=work)
+            comm.gemm_rowsplit_p2p(q0, s0, x, N, ysym)
+            torch.cuda.synchronize()
+            same = bool(torch.equal(y_one, y_nccl)) and bool(torch.equal(y_one, ysym.tensor()))
+            sample = np.unique(np.linspace(0, N - 1, 97).astype(np.int64))   # rows of every rank's block
+            err = _fp64_err(torch, codes, scales, x_bits[:8], y_nccl[:8], sample, dev)
+            us1 = _median_us(torch, stream, lambda i: vkb.gemm_tc(qfl[i % nf], sfl[i % nf], x, y=y1))
             us = _median_us(torch, stream, lambda i: comm.gemm_rowsplit(ql[i % nq], sl[i % nq], x, N, y=y, work=work),
                             graph=False)
-            ysym = comm.alloc((M, N), torch.float16)
             us_p2p = _median_us(torch, stream, lambda i: comm.gemm_rowsplit_p2p(ql[i % nq], sl[i % nq], x, N, ysym))
             torch.cuda.synchronize()
             ysym.free()
-            out[f"q4_{N}x{K}_m{M}"] = {"us": us, "us_p2p": us_p2p, "flop": 2.0 * M * N * K,
-                                       "allgather_bytes": M * N * 2}
-        del ql, sl
-    return out
+            rows[f"q4_{N}x{K}_m{M}"] = {"us_1gpu": us1, "us": us, "us_p2p": us_p2p, "parity": same, "err_fp64": err,
+                                        "flop": 2.0 * M * N * K, "allgather_bytes": M * N * 2}
+        del ql, sl, qfl, sfl
+    return moe, rows
+
+
+def reference_kernels_section(timeout_s: float = 600.0):
+    """The reference's own kernels rebuilt for sm_100a, timed on this GPU beside ours and cuBLAS bf16
+    (baseline/time_ref_kernels.py) in a child process: the reference's error handling exits its process."""
+    script = os.path.join(ROOT, "baseline", "time_ref_kernels.py")
+    try:
+        r = subprocess.run([sys.executable, script], capture_output=True, text=True, timeout=timeout_s,
+                           env=dict(os.environ, CUDA_VISIBLE_DEVICES=os.environ.get("CUDA_VISIBLE_DEVICES", "0")
+                                    .split(",")[0]))
+    except subprocess.TimeoutExpired:
+        return {"unavailable": f"timed out after {timeout_s:.0f} s"}
+    lines = [ln for ln in r.stdout.splitlines() if ln.startswith("{")]
+    if r.returncode != 0 or not lines:
+        return {"unavailable": f"exit {r.returncode}: {(r.stderr or r.stdout).strip()[-300:]}"}
+    return json.loads(lines[-1])
 
 
 # ---- our arm ---------------------------------------------------------------------------------------------------------
@@ -520,29 +629,34 @@ def run_ours(args, rank: int, world: int, local_rank: int, dist):
     prompt = prompt_section(torch, vkb, dev, stream, L2, peaks)
     moe1 = moe_section(torch, vkb, dev, stream, L2)
     glu1 = glu_section(torch, vkb, dev, stream, L2)
-    sharded = None
+    sharded, parity_ok = None, True
     if dist is not None:
         from vkb import dist as D
         comm = D.Comm.from_torch()
-        moe_ep = moe_section(torch, vkb, dev, stream, L2, comm, rank, world)
-        rows = rowsplit_section(torch, vkb, dev, stream, L2, comm, rank, world)
+        moe_ep, rows = sharded_section(torch, vkb, dev, stream, L2, comm, rank, world)
         for d in (moe_ep, rows):
             for v in d.values():
-                for key in ("us", "us_p2p"):
-                    if key in v:
-                        v[key] = round(_max_over_ranks(torch, dist, dev, v[key]), 2)
+                for key in ("us_1gpu", "us", "us_p2p", "err_fp64"):
+                    v[key] = round(_max_over_ranks(torch, dist, dev, v[key]), 3 if key != "err_fp64" else 9)
+                v["parity"] = _max_over_ranks(torch, dist, dev, 0.0 if v["parity"] else 1.0) == 0.0   # every rank
+                parity_ok &= v["parity"]
+                v["speedup_vs_1gpu"] = round(v["us_1gpu"] / v["us"], 3)
+                v["speedup_p2p_vs_1gpu"] = round(v["us_1gpu"] / v["us_p2p"], 3)
                 if "flop" in v:   # throughput of the max-over-ranks time
                     fl = v.pop("flop")
                     v["tflops"] = round(fl / v["us"] / 1e6, 1)
                     v["tflops_p2p"] = round(fl / v["us_p2p"] / 1e6, 1)
         torch.cuda.synchronize()
         comm.close()
-        sharded = {"gpus": world, "moe_expert_parallel": moe_ep, "prompt_row_split": rows,
-                   "timing": "median of 5 x 50 calls, device events, max over ranks; us: NCCL combine, launched directly; "
-                             "us_p2p: combine fused into the kernel (peer stores), the 50 calls in one CUDA graph"}
+        sharded = {"gpus": world, "parity": parity_ok, "moe_expert_parallel": moe_ep, "prompt_row_split": rows,
+                   "timing": "median of 5 x 50 calls, device events, max over ranks; us_1gpu: the whole problem on one "
+                             "GPU (full weights); us: NCCL combine, launched directly; us_p2p: combine fused into the "
+                             "kernel (peer stores), the 50 calls in one CUDA graph",
+                   "parity_how": "bit-identical to the one-GPU kernel on the same inputs, NCCL and fused combines, "
+                                 "every rank; err_fp64: max |y - ref| / sum |x w| on a sampled slice, ref in float64"}
 
     if rank != 0:
-        return None
+        return None, parity_ok
     peak = float(peaks.get("hbm_gbs", 6650.0))
     traffic = None
     tf = os.path.join(ROOT, "profiles", "qmv_dram_traffic.json")
@@ -552,13 +666,18 @@ def run_ours(args, rank: int, world: int, local_rank: int, dist):
         except (OSError, ValueError):
             traffic = None
 
-    cpu = None
+    cpu, refk = None, None
     if world == 1:
+        # the reference's kernels on this GPU (a child process), cuBLAS bf16 beside every decode case
+        refk = reference_kernels_section()
+        for key, rec in (refk.get("decode") or {}).items():
+            if key in table:
+                table[key]["cublas_bf16_us"] = rec.get("cublas_bf16_us")
         threads = os.cpu_count() or 1
-        frac = cpu_frac_for(cases, threads, budget_s=10.0)
-        t_cpu, kind, sample = cpu_reference_step(cases, frac, threads)
-        cpu = {"value": round(sbytes / t_cpu / 1e9, 4), "unit": "GB/s", "cores": threads, "kind": kind,
-               "sample": sample, "s_per_step": round(t_cpu, 3)}
+        frac = cpu_plan(cases, threads, 1, budget_s=20.0)
+        t_cpu, nb = cpu_reference(cases, threads, frac)
+        cpu = {"value": round(nb / t_cpu / 1e9, 4), "unit": "GB/s", "cores": threads, "kind": cpu_kind(),
+               "sample": cpu_sample_text(frac, len(cases)), "s_per_step": round(t_cpu, 3)}
 
     return {
         "metric": METRIC,
@@ -573,15 +692,10 @@ def run_ours(args, rank: int, world: int, local_rank: int, dist):
         "vs_baseline": None,
         "dtype": "f16 x int{4,8,2} codes -> f32",
         "data": "synthetic: weights N(0,0.02) seed 0 quantised per 32 (Q4_0/Q8_0/2-bit), x fp16 N(0,1)",
-        "config": {
-            "workload": "configs[1]: dense quantised GEMV sweep, 48 calls per step",
-            "tables": [f"{n}x{k}" for n, k in SHAPES], "tokens": TOKENS, "formats": [f[0] for f in FORMATS],
-            "parallelism": f"replicas x{world}" if world > 1 else "1 GPU",
-            "l2": "inputs larger than L2: every call reads a different copy; each table's copies cycle >= 4x L2",
-            "launch": "one CUDA graph per step (48 vkb_gemv calls captured with vkb_graph_begin/end, programmatic "
-                      "dependent launch between them)",
-            "step_bytes": sbytes,
-        },
+        "config": bench_config(),
+        "parallelism": f"replicas x{world}" if world > 1 else "1 GPU",
+        "launch": "one CUDA graph per step (48 vkb_gemv calls captured with vkb_graph_begin/end, programmatic "
+                  "dependent launch between them)",
         "roofline": {"bound": "hbm", "achieved": round(per_gpu, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(per_gpu / peak, 4), "traffic": traffic,
                      "peak_source": "MEASURED_PEAKS.json hbm_gbs (of measured)" if peaks else "fallback 6650"},
@@ -597,28 +711,31 @@ def run_ours(args, rank: int, world: int, local_rank: int, dist):
         "prompt_gemm": prompt,
         "moe": moe1,
         "f32in_and_glu": glu1,
+        "reference_kernels": refk,
         "sharded": sharded,
-    }
+    }, parity_ok
 
 
 # ---- the reference arm -----------------------------------------------------------------------------------------------
 
 def run_reference(args, rank: int, world: int):
+    """The reference's CPU path on this box's host cores (rank 0 only; the other ranks exit without work): every step
+    runs the reference's ref_value over the step's outputs -- all of them when steps + warm-up fit the budget (the
+    default run: 25 full steps), else the same leading rows of every case; value and ms_per_step are those outputs'
+    bytes and time, unscaled. Inputs from the oracle (no libvkb.so)."""
     if rank != 0:
         return None
-    cases = host_cases()
+    cases = host_cases(source="oracle")
     threads = os.cpu_count() or 1
-    # every step is a bounded sample of the step's outputs: the whole run takes about 90 s of CPU time
-    frac = cpu_frac_for(cases, threads, budget_s=90.0 / max(1, args.steps + args.warmup))
+    frac = cpu_plan(cases, threads, args.steps + args.warmup, budget_s=150.0)
     for _ in range(args.warmup):
-        cpu_reference_step(cases, frac, threads)
-    t = 0.0
-    kind = sample = None
+        cpu_reference(cases, threads, frac)
+    t, nb = 0.0, 0.0
     for _ in range(args.steps):
-        dt, kind, sample = cpu_reference_step(cases, frac, threads)
+        dt, b = cpu_reference(cases, threads, frac)
         t += dt
-    sbytes = step_bytes()
-    value = sbytes * args.steps / t / 1e9
+        nb += b
+    value = nb / t / 1e9
     return {
         "impl": "reference",
         "metric": METRIC,
@@ -633,10 +750,10 @@ def run_reference(args, rank: int, world: int):
         "vs_baseline": None,
         "dtype": "f64 (the reference's ref_value: double sums of fp16 x * int code * fp16 scale)",
         "data": "synthetic: weights N(0,0.02) seed 0 quantised per 32 (Q4_0/Q8_0/2-bit), x fp16 N(0,1)",
-        "config": {"workload": "configs[1]: dense quantised GEMV sweep, 48 calls per step",
-                   "tables": [f"{n}x{k}" for n, k in SHAPES], "tokens": TOKENS, "formats": [f[0] for f in FORMATS],
-                   "parallelism": "host CPU, rank 0 only"},
-        "cpu_baseline": {"value": round(value, 4), "unit": "GB/s", "cores": threads, "kind": kind, "sample": sample},
+        "config": bench_config(),
+        "parallelism": "host CPU, rank 0 only",
+        "cpu_baseline": {"value": round(value, 4), "unit": "GB/s", "cores": threads, "kind": cpu_kind(),
+                         "sample": cpu_sample_text(frac, len(cases))},
         "e2e": {"value": round(value, 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
 
@@ -654,6 +771,7 @@ def main():
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     dist = None
+    parity_ok = True
     if args.impl == "reference":
         res = run_reference(args, rank, world)
     else:
@@ -664,12 +782,14 @@ def main():
             tdist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
                                      device_id=torch.device("cuda", local_rank))
             dist = tdist
-        res = run_ours(args, rank, world, local_rank, dist)
+        res, parity_ok = run_ours(args, rank, world, local_rank, dist)
         if dist is not None:
             dist.barrier()
             dist.destroy_process_group()
     if res is not None:
         print(json.dumps(res), flush=True)
+    if not parity_ok:   # a sharded result differs from the one-GPU kernel's
+        sys.exit(1)
 
 
 if __name__ == "__main__":

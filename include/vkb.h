@@ -157,23 +157,31 @@ int vkb_gemm_q4_tc_rowsplit_f32(vkb_comm_t* comm, const void* q_local, const voi
 /* vkb_gemm_q4_tc_rowsplit (fp16 y) with no workspace argument and no allocation: the workspace is a static device
  * array of the library, 16 MiB per device, looked up once per device. No counterpart in the reference. M * N * 2 must
  * not exceed VKB_ROWSPLIT_NOALLOC_MAX_BYTES (VKB_EUNSUPPORTED otherwise, nothing launched). Calls that overlap in time
- * on one device (other streams, host threads or communicators) share the array and race: serialise them. */
+ * on one device (other streams, host threads or communicators) share the array and race: serialise them. If the
+ * array's lookup fails on one rank, that rank still joins the all-gather (through y) and returns the lookup error.
+ * In every row-split entry point a null pointer on one rank is refused before the collective only when that rank has
+ * neither y nor a workspace to join it with; with either, it joins and returns VKB_EINVAL. */
 #define VKB_ROWSPLIT_NOALLOC_MAX_BYTES (16u << 20)
 int vkb_gemm_q4_tc_rowsplit_noalloc(vkb_comm_t* comm, const void* q_local, const void* s_local, const void* x, void* y,
                                     int N, int K, int M, vkb_stream_t stream);
 
 /* ---- multi-GPU, fused: the exchange inside the kernel (peer stores over NVLink, no NCCL call) --------------------
  * Symmetric device buffers: collective, the same `bytes` on every rank; each rank's buffer is mapped into every peer
- * (CUDA IPC, exchanged over the communicator) and followed by an 8448-byte flags block. Freed by vkb_comm_free
- * (collective) or vkb_comm_destroy. At most 8 ranks.
- * The fused calls below write every rank's copy of a symmetric y. Every rank makes the same fused calls on a buffer in
- * the same order; each call is numbered by an epoch kept in the buffer's flags (device memory, so the calls may be
- * captured in a CUDA graph and replayed): a rank's copy is written only after that rank started the call, and each
- * rank's kernel ends only when every rank's part has arrived. A call refused on one rank only (an argument error
- * there) leaves the other ranks' kernels waiting until their bounded waits give up: their calls end with the
- * peer-timeout bit (4) in vkb_device_status instead of a result. */
+ * (CUDA IPC, exchanged over the communicator). The first allocation also makes the communicator's flags block (8448
+ * bytes, mapped the same way). Freed by vkb_comm_free (collective) or vkb_comm_destroy. At most 8 ranks.
+ * The fused calls below write every rank's copy of a symmetric y. Every rank makes the same fused calls on the
+ * communicator in the same order; each call is numbered by an epoch kept in the flags block (device memory, so the
+ * calls may be captured in a CUDA graph and replayed): a rank's copy is written only after that rank started the
+ * call, and each rank's kernel ends only when every rank's part has arrived or is known to be missing.
+ * A call refused on one rank only, after the checks every rank shares (a pointer that is not a symmetric buffer, an
+ * unaligned operand, a failed launch there), returns its error code on that rank and still takes part in the call's
+ * numbering with a small kernel; the other ranks' kernels then end at once with bit 8 (a peer's part is missing) in
+ * vkb_device_status, and the next call is exact again. A rank whose own waits give up marks its part missing the same
+ * way. vkb_comm_epoch: the number of the last fused call completed on this rank (0 before the first; read from device
+ * memory: synchronise the streams of the fused calls first). */
 int vkb_comm_alloc(vkb_comm_t* comm, size_t bytes, void** ptr);
 int vkb_comm_free(vkb_comm_t* comm, void* ptr);
+int vkb_comm_epoch(const vkb_comm_t* comm, unsigned int* epoch);
 /* Row split with the all-gather fused into the GEMM: the tcgen05 epilogue stores this rank's columns of y straight
  * into every rank's copy of y_sym (>= M x N fp16). Same operands and result as vkb_gemm_q4_tc_rowsplit. */
 int vkb_gemm_q4_tc_rowsplit_p2p(vkb_comm_t* comm, const void* q_local, const void* s_local, const void* x, void* y_sym,
@@ -201,7 +209,8 @@ int vkb_graph_destroy(void* graph_exec);
 /* Human-readable text of a return code. */
 const char* vkb_strerror(int code);
 /* Synchronises the current device, returns (and clears) the device-side status bits that kernels raise when a bounded
- * wait gives up (1 = pipeline wait timeout, 2 = drain timeout, 4 = peer timeout). 0 = healthy. */
+ * wait gives up (1 = pipeline wait timeout, 2 = drain timeout, 4 = peer timeout) or a peer rank reports its part of a
+ * fused multi-GPU call missing (8). 0 = healthy. */
 int vkb_device_status(unsigned int* bits);
 /* Enable (1) or disable (0) programmatic dependent launch for later calls on this host thread; returns the old value. */
 int vkb_set_pdl(int enable);

@@ -130,4 +130,21 @@ double ref_gemv_mt(int N, int K, int M, const int8_t* codes, const uint16_t* sca
     return s;
 }
 
+// The benchmark's synthetic weights and activations without libvkb.so (bench.py's reference arm loads only this
+// library): n normal draws from std::mt19937(seed), Box-Muller on pairs of 32-bit draws u = (r + 0.5) / 2^32 computed
+// in double, times stddev, rounded to float -- the definition the benchmark states for its inputs (BASELINE: fp32
+// N(0, 0.02) weights and fp16 N(0, 1) activations from a seed). tests/test_oracle.py pins it bit for bit against the
+// library's vkb_synth_normal.
+void oracle_synth_normal(unsigned seed, size_t n, float stddev, float* out) {
+    std::mt19937 rng(seed);
+    const double two_pi = 6.283185307179586476925286766559;
+    for (size_t i = 0; i < n; i += 2) {
+        const double u1 = ((double)rng() + 0.5) / 4294967296.0;
+        const double u2 = ((double)rng() + 0.5) / 4294967296.0;
+        const double r = std::sqrt(-2.0 * std::log(u1));
+        out[i] = (float)(r * std::cos(two_pi * u2) * stddev);
+        if (i + 1 < n) out[i + 1] = (float)(r * std::sin(two_pi * u2) * stddev);
+    }
+}
+
 }  // extern "C"

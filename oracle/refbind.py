@@ -36,6 +36,7 @@ def load():
         L.ref_q2_values.argtypes = [i, i, vp, vp, vp, vp, vp]
         L.ref_gemv_mt.restype = ctypes.c_double
         L.ref_gemv_mt.argtypes = [i, i, i, vp, vp, vp, i, i, i, vp]
+        L.oracle_synth_normal.argtypes = [u, ctypes.c_size_t, ctypes.c_float, vp]
         _lib = L
     return _lib
 
@@ -114,6 +115,13 @@ def q2_values(codes, scales, x):
     L.ref_q2_values(N, K, _p(np.ascontiguousarray(codes)), _p(np.ascontiguousarray(scales)),
                     _p(np.ascontiguousarray(x)), _p(val), _p(mag))
     return val, mag
+
+
+def synth_normal(seed: int, shape, std: float) -> np.ndarray:
+    """The benchmark's seeded normal draws (mt19937 + Box-Muller), float32, without libvkb.so."""
+    out = np.empty(int(np.prod(shape)), np.float32)
+    load().oracle_synth_normal(seed, out.size, std, _p(out))
+    return out.reshape(shape)
 
 
 def gemv_mt(codes, scales, x, row0: int, nrows: int, threads: int, out=None) -> float:

@@ -2,8 +2,9 @@
 the combine fused into the kernel) and the row-split prompt GEMM (vkb_gemm_q4_tc_rowsplit, and
 vkb_gemm_q4_tc_rowsplit_p2p with the all-gather fused into the epilogue, called directly and replayed from a CUDA
 graph) against the one-GPU calls on the same inputs -- bit-identical, since every slot / row is computed by the same
-kernel code and the combines only add zeros or move values -- and against the oracle. Skipped with fewer than two
-GPUs."""
+kernel code and the combines only add zeros or move values -- and against the oracle; and a fused call refused on one
+rank only, which must leave its peers with a status bit rather than a silent partial result. Skipped with fewer than
+two GPUs."""
 import datetime
 import os
 import socket
@@ -18,13 +19,6 @@ def _free_port():
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
         return s.getsockname()[1]
-
-
-def _raw_u32(torch, ptr: int, nbytes: int):
-    """uint32 words of device memory at ptr (a view, no copy)."""
-    iface = {"shape": (nbytes,), "typestr": "|u1", "data": (ptr, False), "version": 3}
-    holder = type("_CudaArray", (), {"__cuda_array_interface__": iface})()
-    return torch.as_tensor(holder, device="cuda").view(torch.int32)
 
 
 def _rank_main(rank, world, port, q):
@@ -105,12 +99,14 @@ def _rank_main(rank, world, port, q):
                 out.append((f"rowsplit_p2p N{N} K{K} M{M} call{i}", bool(torch.equal(y_one, snaps[i])), 0.0, 1.0))
             ysym.free()
             # the same call captured once in a CUDA graph and replayed: the epochs live in device memory, so every
-            # replay is a new call (the buffer's epoch word, in the flags after the 256-byte aligned data, counts the replays)
+            # replay is a new call
             if (N, K, M) == (1024, 2048, 64):
                 ysym = comm.alloc((M, N), torch.float16)
                 yv = ysym.tensor()
                 xg = torch.empty_like(xs[0])
                 stream = torch.cuda.current_stream()
+                torch.cuda.synchronize()
+                epoch0 = comm.epoch()
                 g = vkb.Graph(stream)
                 with g:
                     comm.gemm_rowsplit_p2p(qloc, sloc, xg, N, ysym)
@@ -121,10 +117,8 @@ def _rank_main(rank, world, port, q):
                     snaps.append(yv.clone())
                 torch.cuda.synchronize()
                 del g
-                data_bytes = (M * N * 2 + 255) // 256 * 256
-                flags = _raw_u32(torch, ysym.ptr.value, data_bytes + 2058 * 4)[data_bytes // 4:]
-                # the EPOCH word follows READY [8 ranks][256 CTAs], DONE [8 ranks] and the CTA count
-                out.append(("rowsplit_p2p graph epochs", int(flags[2057].item()) == len(xs), 0.0, 1.0))
+                # the communicator's epoch (device memory) counts the replays: each one is a new call
+                out.append(("rowsplit_p2p graph epochs", comm.epoch() == epoch0 + len(xs), 0.0, 1.0))
                 for i, x in enumerate(xs):
                     y_one = vkb.gemm_tc(qfull, sfull, x)
                     torch.cuda.synchronize()
@@ -157,6 +151,45 @@ def _rank_main(rank, world, port, q):
                     dist.barrier()           # every rank compared before the next call's fill
                 ysym.free()
         status = vkb.device_status()
+        # ---- a fused call refused by the last rank only (y is not a symmetric buffer there): that rank returns
+        # VKB_EINVAL and takes part in the call's numbering with its abstain kernel; every other rank's kernel ends at
+        # once (well inside the 2 s bounded waits) with bit 8, a peer's part missing, not with a silent result; the
+        # epochs stay aligned and the next call on every rank is bit-exact again ----
+        import time
+        N, K, M = 1024, 2048, 64
+        codes = rng.integers(-8, 8, size=(N, K)).astype(np.int8)
+        scales = rng.uniform(0.004, 0.02, size=(N, K // 32)).astype(np.float16).view(np.uint16)
+        qfull = vkb.to_device_packed(O.pack(O.FMT_Q4, codes), dev)
+        sfull = vkb.to_device_f16(scales, dev)
+        n0, nl = D.row_range(N, world, rank)
+        qloc, sloc = qfull[n0:n0 + nl].contiguous(), sfull[n0:n0 + nl].contiguous()
+        x = vkb.to_device_f16(rng.uniform(-1, 1, size=(M, K)).astype(np.float16).view(np.uint16), dev)
+        ysym = comm.alloc((M, N), torch.float16)
+        plain = torch.empty((M, N), dtype=torch.float16, device=dev)
+        torch.cuda.synchronize()
+        epoch0 = comm.epoch()
+        dist.barrier()
+        refuser = rank == world - 1
+        t0 = time.perf_counter()
+        target = vkb._ptr(plain) if refuser else ysym.ptr
+        rc = vkb.lib().vkb_gemm_q4_tc_rowsplit_p2p(comm._h, vkb._ptr(qloc), vkb._ptr(sloc), vkb._ptr(x), target, N, K,
+                                                   M, vkb._stream())
+        torch.cuda.synchronize()
+        dt = time.perf_counter() - t0
+        bits = vkb.device_status()
+        out.append(("refusal: return code", rc == (vkb.EINVAL if refuser else 0), 0.0, 1.0))
+        out.append(("refusal: status bits", bits == (0 if refuser else 8), 0.0, 1.0))
+        out.append(("refusal: no timeout", dt < 1.0, 0.0, 1.0))
+        out.append(("refusal: epochs aligned", comm.epoch() == epoch0 + 1, 0.0, 1.0))
+        dist.barrier()
+        comm.gemm_rowsplit_p2p(qloc, sloc, x, N, ysym)
+        y_next = ysym.tensor().clone()
+        y_one = vkb.gemm_tc(qfull, sfull, x)
+        torch.cuda.synchronize()
+        out.append(("refusal: next call exact", bool(torch.equal(y_one, y_next)), 0.0, 1.0))
+        out.append(("refusal: next call status", vkb.device_status() == 0, 0.0, 1.0))
+        dist.barrier()
+        ysym.free()
         comm.close()
         dist.barrier()
         dist.destroy_process_group()

@@ -110,3 +110,21 @@ def test_gguf_blocks_values(fmt):
     assert blocks.size == 5 * 3 * (18 if fmt == O.FMT_Q4 else 34)
     want = codes.astype(np.float64) * np.repeat(scales.view(np.float16).astype(np.float64), 32, axis=1)
     assert np.array_equal(O.gguf_values(fmt, blocks, 5, 96), want)
+
+
+def test_oracle_inputs_match_the_library():
+    """bench.py's reference arm builds the benchmark's inputs without libvkb.so: the oracle's normal draws, numpy
+    quantiser and fp16 rounding must equal the library's bit for bit (full configs[0] table, and odd lengths)."""
+    if refbind.load() is None:
+        pytest.skip("oracle/_ref/libvkbref.so not built")
+    import vkb
+    for seed, shape, std in ((0, (8192, 2048), 0.02), (3, (4, 2048), 1.0), (5, (7,), 1.0)):
+        a, b = refbind.synth_normal(seed, shape, std), vkb.synth_normal(seed, shape, std)
+        assert a.dtype == b.dtype == np.float32 and np.array_equal(a.view(np.uint32), b.view(np.uint32))
+    w = refbind.synth_normal(0, (512, 2048), 0.02)
+    for fmt in (O.FMT_Q4, O.FMT_Q8, O.FMT_Q2):
+        c0, s0 = O.quantize(fmt, w)
+        c1, s1 = vkb.quantize(fmt, w)
+        assert np.array_equal(c0, c1) and np.array_equal(s0, s1), fmt
+    x = refbind.synth_normal(2, (8, 2048), 1.0)
+    assert np.array_equal(x.astype(np.float16).view(np.uint16), vkb.to_f16_bits(x))

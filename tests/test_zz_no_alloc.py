@@ -1,8 +1,9 @@
 """vkb_gemm_q4_tc_rowsplit_noalloc: the row-split prompt GEMM with its workspace in the library's static device array
-(no allocation on the call path). On one GPU with a one-rank communicator: two calls in a row (different shapes, then
-the first again) against vkb_gemm_q4_tc_rowsplit with a caller-owned workspace and against vkb_gemm_q4_tc -- bit for
-bit -- and a shape past the array's size refused with nothing written. This file is collected last on purpose: it
-must pass after every other test as well as alone."""
+(no allocation on the call path). On one GPU with a one-rank communicator: rounds of calls in a row (different
+shapes, then the first again) against vkb_gemm_q4_tc_rowsplit with a caller-owned workspace and against
+vkb_gemm_q4_tc -- bit for bit --, the device's free memory unchanged across a whole round once the first round has
+done the one-time set-up, and a shape past the array's size refused with nothing written. This file is collected last
+on purpose: it must pass after every other test as well as alone."""
 import ctypes
 
 import numpy as np
@@ -45,14 +46,23 @@ def test_two_calls_in_a_row_match(comm, cuda):
             q, s, codes, scales = _weights(rng, N, K, cuda)
             x_np = rng.uniform(-1, 1, size=(M, K)).astype(np.float16).view(np.uint16)
             made[(N, K, M)] = (q, s, vkb.to_device_f16(x_np, cuda), codes, scales, x_np)
-    outs = []
-    for N, K, M in cases:                      # back to back on one stream, no synchronisation in between
-        q, s, x, *_ = made[(N, K, M)]
-        y = torch.full((M, N), float("nan"), dtype=torch.float16, device=cuda)
-        assert _noalloc(comm, q, s, x, y, N, K, M) == 0
-        outs.append(y)
+    ys = [torch.full((M, N), float("nan"), dtype=torch.float16, device=cuda) for N, K, M in cases]
+
+    def round_of_calls():                      # back to back on one stream, no synchronisation in between
+        for (N, K, M), y in zip(cases, ys):
+            q, s, x, *_ = made[(N, K, M)]
+            y.fill_(float("nan"))
+            assert _noalloc(comm, q, s, x, y, N, K, M) == 0
+
+    round_of_calls()   # first round: the one-time symbol lookup, and the first launch of each kernel (lazy loading)
     torch.cuda.synchronize()
-    for (N, K, M), y in zip(cases, outs):
+    free0, _ = torch.cuda.mem_get_info()
+    torch0 = torch.cuda.memory_allocated()
+    round_of_calls()   # second round: the entry point's calls allocate nothing on the device
+    torch.cuda.synchronize()
+    free1, _ = torch.cuda.mem_get_info()
+    assert free1 == free0 and torch.cuda.memory_allocated() == torch0, (free0, free1)
+    for (N, K, M), y in zip(cases, ys):
         q, s, x, codes, scales, x_np = made[(N, K, M)]
         y_ws = comm.gemm_rowsplit(q, s, x, N)          # caller-owned workspace
         y_one = vkb.gemm_tc(q, s, x)                   # single-GPU entry point

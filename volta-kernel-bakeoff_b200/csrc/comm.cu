@@ -26,8 +26,7 @@
 #include "ptx.cuh"
 #include "vkb_internal.h"
 
-// A symmetric buffer: the same size on every rank, this rank's allocation plus every peer's mapped by CUDA IPC; the
-// data is followed by the flags block of the peer-store protocol (p2p.cuh).
+// A symmetric buffer: the same size on every rank, this rank's allocation plus every peer's mapped by CUDA IPC.
 struct SymBuf {
     void* base;
     size_t data_bytes;
@@ -38,6 +37,7 @@ struct vkb_comm {
     ncclComm_t nc;
     int rank, size, dev;
     std::vector<SymBuf> sym;
+    SymBuf flags;   // the peer-store protocol's flags block (p2p.cuh), one per communicator: made by the first alloc
 };
 
 namespace vkb {
@@ -89,13 +89,25 @@ static int launch_permute(const void* work, void* y, int M, int nl, int G, cudaS
     return e == cudaSuccess ? 0 : -(int)e;
 }
 
+// The all-gather of a row-split call, joined without computing anything (a rank-local failure after the checks every
+// rank shares): buf (M * N elements, any contents) sends this rank's block and receives the peers', so that no peer is
+// left waiting in the collective. Returns the collective's own status.
+static int rowsplit_join(vkb_comm_t* c, void* buf, bool f32, int N, int M, cudaStream_t st) {
+    const size_t chunk = (size_t)M * (N / c->size);
+    uint8_t* mine = static_cast<uint8_t*>(buf) + (size_t)c->rank * chunk * (f32 ? 4 : 2);
+    return nccl_rc(ncclAllGather(mine, buf, chunk, f32 ? ncclFloat : ncclHalf, c->nc, st));
+}
+
 static int rowsplit(vkb_comm_t* c, const void* q, const void* s, const void* x, void* y, void* work, bool f32, int N,
                     int K, int M, cudaStream_t st) {
     if (!c) return VKB_ENOCOMM;
-    if (!q || !s || !x || !y || !work) return VKB_EINVAL;
     // shape checks (equal on every rank): a failure here returns before any rank reaches the collective
     if (N < 1 || M < 1 || K < 256) return VKB_EINVAL;
     if (N % c->size != 0 || K % 256 != 0) return VKB_EUNSUPPORTED;
+    if (!q || !s || !x || !y || !work) {   // this rank only: join the collective with whichever buffer it has
+        if (work || y) rowsplit_join(c, work ? work : y, f32, N, M, st);
+        return VKB_EINVAL;                 // (with neither, the peers' all-gather waits: a caller error)
+    }
     const int nl = N / c->size;
     const size_t esz = f32 ? 4 : 2;
     const size_t chunk = (size_t)M * nl;                    // elements per rank
@@ -146,16 +158,31 @@ static SymBuf* find_sym(vkb_comm_t* c, const void* p, size_t need) {
     return nullptr;
 }
 
-// The kernels' view of a symmetric buffer: every rank's copy and its flags block.
-static P2PArgs p2p_args(const vkb_comm_t* c, const SymBuf& b) {
+// The kernels' view of a symmetric buffer (every rank's copy; null: none) and of the communicator's flags block.
+static P2PArgs p2p_args(const vkb_comm_t* c, const SymBuf* b) {
     P2PArgs pp{};
     for (int r = 0; r < c->size; ++r) {
-        pp.peer_base[r] = b.peer[r];
-        pp.peer_flags[r] = reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(b.peer[r]) + b.data_bytes);
+        pp.peer_base[r] = b ? b->peer[r] : nullptr;
+        pp.peer_flags[r] = static_cast<uint32_t*>(c->flags.peer[r]);
     }
     pp.rank = c->rank;
     pp.size = c->size;
     return pp;
+}
+
+// One fused call on a rank that refused it on the host after the checks every rank shares (a pointer that is not a
+// symmetric buffer, an unaligned operand, a failed launch): the epoch protocol's part of the call (p2p_abstain), so
+// that the peers' kernels finish at once with DEV_ERR_PEER_FAILED instead of waiting out their bounded waits, and the
+// ranks' call numbering stays aligned. Nothing is written but flags.
+__global__ void __launch_bounds__(256) p2p_abstain_kernel(P2PArgs pp) {
+    pdl_wait();
+    p2p_abstain(pp);
+}
+
+static void abstain(const vkb_comm_t* c, cudaStream_t st) {
+    if (!c->flags.base) return;   // no symmetric buffer yet on this communicator: no peer can be in a fused call
+    p2p_abstain_kernel<<<1, 256, 0, st>>>(p2p_args(c, nullptr));
+    cudaGetLastError();   // a failed launch here leaves the peers to their bounded waits; the caller has its error
 }
 
 static int sym_free_one(vkb_comm_t* c, SymBuf& b) {
@@ -168,6 +195,53 @@ static int sym_free_one(vkb_comm_t* c, SymBuf& b) {
     const cudaError_t e = cudaFree(b.base);
     if (e != cudaSuccess && rc == 0) rc = -(int)e;
     return rc;
+}
+
+// Collective: `bytes` (rounded up to 256) of zeroed device memory on every rank, every rank's allocation mapped into
+// every peer by CUDA IPC (handles exchanged over the communicator). Every rank that reaches the exchange with valid
+// arguments joins it, also after a local failure, and the call then returns that failure.
+static int sym_alloc(vkb_comm_t* comm, size_t bytes, SymBuf* out) {
+    SymBuf b{};
+    b.data_bytes = (bytes + 255) / 256 * 256;
+    cudaError_t e = cudaMalloc(&b.base, b.data_bytes);
+    if (e != cudaSuccess) b.base = nullptr;
+    if (e == cudaSuccess) e = cudaMemset(b.base, 0, b.data_bytes);
+    cudaIpcMemHandle_t h;
+    if (e == cudaSuccess) e = cudaIpcGetMemHandle(&h, b.base);
+    void* dh = nullptr;
+    if (cudaMalloc(&dh, sizeof(h) * comm->size) != cudaSuccess) dh = nullptr;
+    int rc = e == cudaSuccess ? 0 : -(int)e;
+    if (rc == 0 && !dh) rc = -(int)cudaErrorMemoryAllocation;
+    std::vector<cudaIpcMemHandle_t> all(comm->size);
+    if (rc == 0) {
+        e = cudaMemcpy(static_cast<uint8_t*>(dh) + comm->rank * sizeof(h), &h, sizeof(h), cudaMemcpyHostToDevice);
+        rc = e == cudaSuccess ? 0 : -(int)e;
+    }
+    if (dh) {   // the collective runs on every rank that got its exchange buffer
+        const int rn = nccl_rc(ncclAllGather(static_cast<uint8_t*>(dh) + comm->rank * sizeof(h), dh, sizeof(h),
+                                             ncclUint8, comm->nc, nullptr));
+        if (!rc) rc = rn;
+        e = cudaStreamSynchronize(nullptr);
+        if (!rc && e != cudaSuccess) rc = -(int)e;
+        if (!rc) {
+            e = cudaMemcpy(all.data(), dh, sizeof(h) * comm->size, cudaMemcpyDeviceToHost);
+            if (e != cudaSuccess) rc = -(int)e;
+        }
+        cudaFree(dh);
+    }
+    for (int r = 0; r < comm->size && rc == 0; ++r) {
+        if (r == comm->rank) { b.peer[r] = b.base; continue; }
+        e = cudaIpcOpenMemHandle(&b.peer[r], all[r], cudaIpcMemLazyEnablePeerAccess);
+        if (e != cudaSuccess) rc = -(int)e;
+    }
+    if (rc) {
+        for (int r = 0; r < comm->size; ++r)
+            if (r != comm->rank && b.peer[r]) cudaIpcCloseMemHandle(b.peer[r]);
+        if (b.base) cudaFree(b.base);
+        return rc;
+    }
+    *out = b;
+    return 0;
 }
 
 }  // namespace vkb
@@ -197,7 +271,7 @@ int vkb_comm_init(vkb_comm_t** comm, int rank, int nranks, const void* id) {
     ncclComm_t nc = nullptr;
     const int rc = nccl_rc(ncclCommInitRank(&nc, nranks, u, rank));
     if (rc) return rc;
-    vkb_comm* c = new (std::nothrow) vkb_comm{nc, rank, nranks, dev};
+    vkb_comm* c = new (std::nothrow) vkb_comm{nc, rank, nranks, dev, {}, {}};
     if (!c) {
         ncclCommDestroy(nc);
         return VKB_EINVAL;
@@ -232,6 +306,10 @@ int vkb_comm_destroy(vkb_comm_t* comm) {
         const int r = sym_free_one(comm, b);
         if (r && !rc) rc = r;
     }
+    if (comm->flags.base) {
+        const int r = sym_free_one(comm, comm->flags);
+        if (r && !rc) rc = r;
+    }
     const int r = nccl_rc(ncclCommDestroy(comm->nc));
     delete comm;
     return rc ? rc : r;
@@ -241,46 +319,11 @@ int vkb_comm_alloc(vkb_comm_t* comm, size_t bytes, void** ptr) {
     if (!comm || !ptr || bytes == 0) return VKB_EINVAL;
     *ptr = nullptr;
     if (comm->size > P2P_MAX_RANKS) return VKB_EUNSUPPORTED;
+    if (!comm->flags.base) {   // the communicator's flags block comes with its first symmetric buffer (collective)
+        if (int rc = sym_alloc(comm, P2P_FLAG_BYTES, &comm->flags)) return rc;
+    }
     SymBuf b{};
-    b.data_bytes = (bytes + 255) / 256 * 256;
-    cudaError_t e = cudaMalloc(&b.base, b.data_bytes + P2P_FLAG_BYTES);
-    if (e != cudaSuccess) return -(int)e;
-    e = cudaMemset(b.base, 0, b.data_bytes + P2P_FLAG_BYTES);
-    cudaIpcMemHandle_t h;
-    if (e == cudaSuccess) e = cudaIpcGetMemHandle(&h, b.base);
-    // every rank's handle to every rank, through the communicator
-    void* dh = nullptr;
-    if (e == cudaSuccess) e = cudaMalloc(&dh, sizeof(h) * comm->size);
-    int rc = e == cudaSuccess ? 0 : -(int)e;
-    std::vector<cudaIpcMemHandle_t> all(comm->size);
-    if (rc == 0) {
-        e = cudaMemcpy(static_cast<uint8_t*>(dh) + comm->rank * sizeof(h), &h, sizeof(h), cudaMemcpyHostToDevice);
-        rc = e == cudaSuccess ? 0 : -(int)e;
-    }
-    // the collective runs on every rank that reached this point with valid arguments
-    if (dh) {
-        const int rn = nccl_rc(ncclAllGather(static_cast<uint8_t*>(dh) + comm->rank * sizeof(h), dh, sizeof(h),
-                                             ncclUint8, comm->nc, nullptr));
-        if (!rc) rc = rn;
-        e = cudaStreamSynchronize(nullptr);
-        if (!rc && e != cudaSuccess) rc = -(int)e;
-        if (!rc) {
-            e = cudaMemcpy(all.data(), dh, sizeof(h) * comm->size, cudaMemcpyDeviceToHost);
-            if (e != cudaSuccess) rc = -(int)e;
-        }
-        cudaFree(dh);
-    }
-    for (int r = 0; r < comm->size && rc == 0; ++r) {
-        if (r == comm->rank) { b.peer[r] = b.base; continue; }
-        e = cudaIpcOpenMemHandle(&b.peer[r], all[r], cudaIpcMemLazyEnablePeerAccess);
-        if (e != cudaSuccess) rc = -(int)e;
-    }
-    if (rc) {
-        for (int r = 0; r < comm->size; ++r)
-            if (r != comm->rank && b.peer[r]) cudaIpcCloseMemHandle(b.peer[r]);
-        if (b.base) cudaFree(b.base);
-        return rc;
-    }
+    if (int rc = sym_alloc(comm, bytes, &b)) return rc;
     comm->sym.push_back(b);
     *ptr = b.base;
     return 0;
@@ -326,13 +369,18 @@ int vkb_moe_ep_p2p(vkb_comm_t* comm, int fmt, const void* qpool, const void* spo
                    int topk, const void* x, void* y_sym, int out_f32, int E_local, int e0, int N, int K,
                    vkb_stream_t stream) {
     if (!comm) return VKB_ENOCOMM;
-    if (!idx || !y_sym || T < 1 || topk < 1 || N < 1) return VKB_EINVAL;
+    if (T < 1 || topk < 1 || N < 1) return VKB_EINVAL;               // equal on every rank
     if (comm->size > P2P_MAX_RANKS) return VKB_EUNSUPPORTED;
-    SymBuf* b = find_sym(comm, y_sym, (size_t)T * topk * N * (out_f32 ? 4 : 2));
-    if (!b) return VKB_EINVAL;   // y must come from vkb_comm_alloc and hold T*topk x N outputs
-    const P2PArgs pp = p2p_args(comm, *b);
-    return qmv_dispatch(fmt, qpool, spool, x, y_sym, out_f32 != 0, idx, N, K, T, topk, E_local, e0, 0,
-                        (cudaStream_t)stream, &pp);
+    const cudaStream_t st = (cudaStream_t)stream;
+    // past this point a refusal is this rank's alone: it still takes its part in the call's epoch protocol
+    SymBuf* b = idx ? find_sym(comm, y_sym, (size_t)T * topk * N * (out_f32 ? 4 : 2)) : nullptr;
+    int rc = VKB_EINVAL;   // y must come from vkb_comm_alloc and hold T*topk x N outputs
+    if (b) {
+        const P2PArgs pp = p2p_args(comm, b);
+        rc = qmv_dispatch(fmt, qpool, spool, x, y_sym, out_f32 != 0, idx, N, K, T, topk, E_local, e0, 0, st, &pp);
+    }
+    if (rc != 0) abstain(comm, st);
+    return rc;
 }
 
 size_t vkb_gemm_rowsplit_work_bytes(int M, int N, int out_f32) {
@@ -348,27 +396,49 @@ int vkb_gemm_q4_tc_rowsplit(vkb_comm_t* comm, const void* q_local, const void* s
 int vkb_gemm_q4_tc_rowsplit_noalloc(vkb_comm_t* comm, const void* q_local, const void* s_local, const void* x, void* y,
                                     int N, int K, int M, vkb_stream_t stream) {
     if (!comm) return VKB_ENOCOMM;
-    if (N < 1 || M < 1) return VKB_EINVAL;
+    if (N < 1 || M < 1 || K < 256) return VKB_EINVAL;                                  // equal on every rank
     if ((size_t)M * (size_t)N * 2 > kRowsplitScratchBytes) return VKB_EUNSUPPORTED;   // equal on every rank
+    if (N % comm->size != 0 || K % 256 != 0) return VKB_EUNSUPPORTED;                 // equal on every rank
     int dev = 0;
-    if (int r = current_device(&dev)) return r;
     void* work = nullptr;
-    if (int r = rowsplit_scratch(dev, &work)) return r;
+    int r = current_device(&dev);
+    if (r == 0) r = rowsplit_scratch(dev, &work);
+    if (r != 0) {   // this rank only: join the peers' all-gather through y, then report the lookup failure
+        if (y) rowsplit_join(comm, y, false, N, M, (cudaStream_t)stream);
+        return r;
+    }
     return rowsplit(comm, q_local, s_local, x, y, work, false, N, K, M, (cudaStream_t)stream);
 }
 
 int vkb_gemm_q4_tc_rowsplit_p2p(vkb_comm_t* comm, const void* q_local, const void* s_local, const void* x, void* y_sym,
                                 int N, int K, int M, vkb_stream_t stream) {
     if (!comm) return VKB_ENOCOMM;
-    if (!q_local || !s_local || !x || !y_sym) return VKB_EINVAL;
-    if (N < 1 || M < 1 || K < 256) return VKB_EINVAL;
+    if (N < 1 || M < 1 || K < 256) return VKB_EINVAL;                                        // equal on every rank
     if (N % comm->size != 0 || K % 256 != 0 || comm->size > P2P_MAX_RANKS) return VKB_EUNSUPPORTED;
-    SymBuf* b = find_sym(comm, y_sym, (size_t)M * N * 2);
-    if (!b) return VKB_EINVAL;   // y must come from vkb_comm_alloc and hold M x N fp16
-    const P2PArgs pp = p2p_args(comm, *b);
-    const int nl = N / comm->size;
-    TcOut out{N, comm->rank * nl, &pp};
-    return tc_dispatch(q_local, s_local, x, y_sym, false, nl, K, M, (cudaStream_t)stream, &out);
+    const cudaStream_t st = (cudaStream_t)stream;
+    // past this point a refusal is this rank's alone: it still takes its part in the call's epoch protocol
+    SymBuf* b = (q_local && s_local && x) ? find_sym(comm, y_sym, (size_t)M * N * 2) : nullptr;
+    int rc = VKB_EINVAL;   // y must come from vkb_comm_alloc and hold M x N fp16
+    if (b) {
+        const P2PArgs pp = p2p_args(comm, b);
+        const int nl = N / comm->size;
+        TcOut out{N, comm->rank * nl, &pp};
+        rc = tc_dispatch(q_local, s_local, x, y_sym, false, nl, K, M, st, &out);
+    }
+    if (rc != 0) abstain(comm, st);
+    return rc;
+}
+
+int vkb_comm_epoch(const vkb_comm_t* comm, unsigned int* epoch) {
+    if (!comm || !epoch) return VKB_EINVAL;
+    *epoch = 0;
+    if (!comm->flags.base) return 0;
+    uint32_t v = 0;
+    const cudaError_t e = cudaMemcpy(&v, static_cast<const uint32_t*>(comm->flags.base) + P2P_EPOCH, sizeof(v),
+                                     cudaMemcpyDeviceToHost);
+    if (e != cudaSuccess) return -(int)e;
+    *epoch = v;
+    return 0;
 }
 
 int vkb_gemm_q4_tc_rowsplit_f32(vkb_comm_t* comm, const void* q_local, const void* s_local, const void* x, float* y,

@@ -17,7 +17,12 @@
 namespace vkb {
 
 // Status bits a kernel can raise (read and cleared by vkb_device_status()).
-enum : unsigned { DEV_ERR_WAIT_TIMEOUT = 1u, DEV_ERR_DRAIN_TIMEOUT = 2u, DEV_ERR_PEER_TIMEOUT = 4u };
+enum : unsigned {
+    DEV_ERR_WAIT_TIMEOUT = 1u,    // a pipeline wait (mbarrier) gave up
+    DEV_ERR_DRAIN_TIMEOUT = 2u,   // waiting for this CTA's own copies in flight gave up
+    DEV_ERR_PEER_TIMEOUT = 4u,    // a wait on a peer rank's flag gave up
+    DEV_ERR_PEER_FAILED = 8u,     // a peer rank reported its part of a fused call missing
+};
 
 }  // namespace vkb
 

@@ -308,7 +308,9 @@ __device__ __forceinline__ int moe_route(const QmvArgs& a, MoeTables tb) {
 // system-scope fence in p2p_finish releases the stores of every consumer thread (the producer warp stores nothing).
 // Kept out of line, so that the tile loop's register allocation does not carry it.
 template <typename OutT>
-__device__ __noinline__ void qmv_moe_push(const QmvArgs& a, MoeTables tb, int w0, int w1, bool ok) {
+__device__ __noinline__ void qmv_moe_push(const QmvArgs& a, MoeTables tb, int w0, int w1, bool ok,
+                                          volatile int* cta_failed) {
+    if (threadIdx.x == 0) *cta_failed = 0;   // (set to 1 below by any consumer thread that gave up or skipped)
     named_sync(1, QMV_NW * 32);
     bool rd = ok;
     if ((threadIdx.x & 31) == 0 && rd) rd = p2p_wait_ready(a.pp, p2p_epoch(a.pp));
@@ -327,8 +329,9 @@ __device__ __noinline__ void qmv_moe_push(const QmvArgs& a, MoeTables tb, int w0
                      [&](int r) { return (size_t)tb.slots[first + r] * rowp + off0; }, threadIdx.x, QMV_NW * 32);
         }
     }
+    if (!rd) *cta_failed = 1;
     named_sync(1, QMV_NW * 32);
-    if (threadIdx.x == 0) p2p_finish(a.pp);
+    if (threadIdx.x == 0) p2p_finish(a.pp, *cta_failed == 0);
 }
 
 // ---- the kernel ---------------------------------------------------------------------------------------------------
@@ -341,10 +344,11 @@ __device__ __noinline__ void qmv_moe_push(const QmvArgs& a, MoeTables tb, int w0
 // slot's last completed phase, which is all an mbarrier parity wait can tell apart.
 //
 // Barrier block layout (uint64 slots from bar_off): full[nstage], empty[nstage], xfull[2], xempty[2],
-// redfull[2 * QMV_MAXWG], redfree[2 * QMV_MAXWG], gfull[2], gfree[2]. The reduction region holds 2 * QMV_NW * 32
+// redfull[2 * QMV_MAXWG], redfree[2 * QMV_MAXWG], gfull[2], gfree[2], and one word of CTA state (the MoE peer-store
+// failure flag). The reduction region holds 2 * QMV_NW * 32
 // float4 (plus 2 x 32 float4 of gate hand-over slots for QMV_GLU).
 constexpr int QMV_MAXWG = 4;
-__host__ __device__ constexpr int qmv_nbars(int nstage) { return 2 * nstage + 4 + 4 * QMV_MAXWG + 4; }
+__host__ __device__ constexpr int qmv_nbars(int nstage) { return 2 * nstage + 4 + 4 * QMV_MAXWG + 4 + 1; }
 
 // XF32: the activations arrive as fp32 (the reference's fp32-in decode entry). After the dependency wait the consumer
 // warps read them from global memory (16-byte loads), round them to fp16 (round to nearest even, the reference's
@@ -373,6 +377,7 @@ qmv_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUten
     uint64_t* redfree = redfull + 2 * QMV_MAXWG;
     uint64_t* gfull = redfree + 2 * QMV_MAXWG;   // QMV_GLU: gate sums handed over in slot 0 / 1
     uint64_t* gfree = gfull + 2;                 // QMV_GLU: the up reducer has taken them
+    volatile int* cta_state = reinterpret_cast<volatile int*>(gfree + 2);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int KG = a.K / 32;
@@ -682,7 +687,7 @@ qmv_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUten
     // release the rest of the CTA's segments (also those this group had no tile in)
     if (ok) ok = enter_upto(last_seg - first_seg);
     leave();
-    if constexpr (MODE == QMV_MOE_P2P) qmv_moe_push<OutT>(a, tb, w0, w1, ok);
+    if constexpr (MODE == QMV_MOE_P2P) qmv_moe_push<OutT>(a, tb, w0, w1, ok, cta_state);
 }
 
 }  // namespace vkb

@@ -312,7 +312,7 @@ __device__ __noinline__ void tc_push_tile(const TcArgs& a, int row0, int tok0, i
 // streams half of the activations it would stream alone: the shared-memory traffic per MMA halves. The leader's
 // barriers count both CTAs (the peer's dequantising and epilogue warps arrive remotely, the peer's activation loads
 // complete on the leader's barrier); the leader's commits arrive on both CTAs' barriers. No TMA multicast.
-// WF: weight format, 0 = Q4 (the reference's tc_q4), 1 = Q8 (the tc_q8 it planned, SURVEY's next rows): only the packed
+// WF: weight format, 0 = Q4 (the reference's tc_q4), 1 = Q8 (the tc_q8 it planned but never built): only the packed
 // chunk layout and the dequantisation differ.
 // RB = 2 (opt-in, VKB_TC_RB=2): one CTA holds a 256-row tile as two 128-row blocks, each with its own accumulator
 // (TMEM columns 0 and NT rounded up to 32), and every activation K step feeds the MMAs of both blocks: the activations
@@ -385,8 +385,12 @@ tc_q4_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUt
         tma_load_2d(dst + SCOFF, &ts, c * PK * 2, row0_of(t), &pfull[b]);         // 2 PK (+ pad) fp16 scales
     };
 
+    // peer stores: some thread of this CTA gave up a wait (its part of the call is missing); the word after the TMEM
+    // address in the barrier block
+    volatile int* cta_failed = reinterpret_cast<volatile int*>(tmem_slot + 1);
     pdl_trigger();
     if (threadIdx.x == 0) {
+        *cta_failed = 0;
         for (int i = 0; i < a.np; ++i) {
             mbar_init(&pfull[i], 1);
             mbar_init(&pempty[i], TC_NDQ);
@@ -748,6 +752,7 @@ tc_q4_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUt
     // teardown: every MMA has completed (the epilogue waited on each accumulator) before TMEM is released
     if (warp == 1 && !ok && ntl > 0) wait_b(&accfull[(ntl - 1) % a.nacc], ((ntl - 1) / a.nacc) & 1,
                                             DEV_ERR_DRAIN_TIMEOUT);
+    if (P2P && !ok) *cta_failed = 1;
     tc_fence_before();
     // a pair leaves together: no remote arrive, pair load or MMA touches a CTA that has released its TMEM or exited
     if constexpr (CG == 2) cluster_sync();
@@ -758,7 +763,7 @@ tc_q4_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUt
     }
     // every store of this CTA precedes the barrier above; thread 0's system-scope fence in p2p_finish releases them
     // all (cumulativity), so no per-thread fence is needed
-    if (P2P && threadIdx.x == 0) p2p_finish(a.pp);
+    if (P2P && threadIdx.x == 0) p2p_finish(a.pp, *cta_failed == 0);
 }
 
 }  // namespace vkb

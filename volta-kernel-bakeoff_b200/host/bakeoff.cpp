@@ -684,7 +684,7 @@ static void check_odd_rows(bool sabotage, std::mt19937& rng) {
 // Qwen3-1.7B's MLP gate + up + SwiGLU (gate and up 6144x2048, stacked), the reference's check (src/bakeoff.cu:370-406):
 // the stacked product against the double reference on 256 sampled outputs (both halves; 1e-4 here, the exact-code
 // class -- the reference's own kernel is fp16-class, 2e-3) and out against silu(gate) * up recomputed in double from
-// that product (1e-5).
+// that product (1e-5), one row per token count: max_err_rel is the product's error, worst_m the SwiGLU error.
 static void check_glu(bool sabotage, std::mt19937& rng) {
     const int N = 6144, K = 2048;
     const Weights w = make_weights(VKB_FMT_Q4, 2 * N, K, rng);
@@ -719,8 +719,13 @@ static void check_glu(bool sabotage, std::mt19937& rng) {
             const double e = std::fabs(out[(size_t)m * N + n] - want) / (std::fabs(want) + 1e-6);
             if (e > glu.err) { glu.err = e; glu.m = m; glu.n = n; }
         }
-        verdict("vkb_glu_q4_f32in_stack", "qwen3_1p7b_mlp_gate_up", M, mm, ran && mm.err <= 1e-4);
-        verdict("vkb_glu_q4_f32in_swiglu", "qwen3_1p7b_mlp_gate_up", M, glu, ran && glu.err <= 1e-5);
+        // one verdict for both parts, in the reference's columns (src/bakeoff.cu:401-403): max_err_rel = the stacked
+        // product's error, worst_m = the SwiGLU error, worst_n = 0
+        const bool ok = ran && mm.err <= 1e-4 && glu.err <= 1e-5;
+        g_failures += !ok;
+        printf("check,vkb_glu_q4_f32in,qwen3_1p7b_mlp_gate_up,%d,%.3g,%.3g,0,%s\n", M, mm.err, glu.err,
+               ok ? "ok" : "FAIL");
+        fflush(stdout);
         CK(cudaFree(dxf));
         CK(cudaFree(dxh));
         CK(cudaFree(dys));

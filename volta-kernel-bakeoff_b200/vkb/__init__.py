@@ -95,6 +95,7 @@ def _register_optional(L) -> None:
         "vkb_gemm_q4_tc_rowsplit_noalloc": ([vp, vp, vp, vp, vp, i, i, i, vp], i),
         "vkb_comm_alloc": ([vp, ctypes.c_size_t, ctypes.POINTER(vp)], i),
         "vkb_comm_free": ([vp, vp], i),
+        "vkb_comm_epoch": ([vp, ctypes.POINTER(ctypes.c_uint)], i),
         "vkb_gemm_q4_tc_rowsplit_p2p": ([vp, vp, vp, vp, vp, i, i, i, vp], i),
         "vkb_moe_ep_p2p": ([vp, i, vp, vp, vp, i, i, vp, vp, i, i, i, i, i, vp], i),
         "vkb_gemv_q4_f32in": ([vp, vp, vp, vp, vp, i, i, i, vp], i),

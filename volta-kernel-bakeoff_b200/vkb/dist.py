@@ -118,6 +118,12 @@ class Comm:
         check(rc, "vkb_moe_ep_p2p")
         return y_sym
 
+    def epoch(self) -> int:
+        """The number of the last fused (peer-store) call completed on this rank (vkb_comm_epoch; synchronise first)."""
+        e = ctypes.c_uint(0)
+        check(lib().vkb_comm_epoch(self._h, ctypes.byref(e)), "vkb_comm_epoch")
+        return e.value
+
     def alloc(self, shape, dtype):
         """A symmetric tensor (collective: same shape on every rank): this rank's buffer, mapped into every peer, for
         the fused peer-store calls. Freed with free()."""
