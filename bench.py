@@ -68,15 +68,52 @@ def step_bytes() -> float:
 # ---- clocks ----------------------------------------------------------------------------------------------------------
 
 class ClockSampler:
-    """nvidia-smi samples of the SM clock, clock-event reasons, utilisation, temperature and ECC during the timed
-    region, judged by vkb.load_judge (the B200 counterpart of the reference's bench/load_flag.py)."""
+    """Clock samples during the timed region -- SM clock, max clock, power, clock-event reasons, utilization,
+    temperature, uncorrected ECC, in nvidia-smi's CSV columns -- judged by vkb.load_judge (the B200 counterpart of the
+    reference's bench/load_flag.py). NVML is polled from a thread every 0.2 ms while the timed work runs (the timed
+    region of a default run is a few milliseconds, shorter than nvidia-smi's sampling period); without NVML it falls
+    back to nvidia-smi every 20 ms."""
 
     def __init__(self, gpu_index: int):
         self.gpu = gpu_index
         self.proc = None
+        self.thread = None
+        self.rows = []
         self.path = None
 
+    def _poll(self, handle, nv):
+        def field(fn, fmt):
+            try:
+                return fmt(fn())
+            except Exception:
+                return "[N/A]"
+        while not self.stop_flag:
+            self.rows.append(",".join([
+                str(self.gpu),
+                field(lambda: nv.nvmlDeviceGetClockInfo(handle, nv.NVML_CLOCK_SM), str),
+                field(lambda: nv.nvmlDeviceGetMaxClockInfo(handle, nv.NVML_CLOCK_SM), str),
+                field(lambda: nv.nvmlDeviceGetPowerUsage(handle) / 1000.0, lambda w: f"{w:.1f}"),
+                field(lambda: nv.nvmlDeviceGetCurrentClocksEventReasons(handle), lambda b: f"0x{b:016x}"),
+                "-", "-", "-", "-",
+                field(lambda: nv.nvmlDeviceGetUtilizationRates(handle).gpu, str),
+                field(lambda: nv.nvmlDeviceGetTemperature(handle, nv.NVML_TEMPERATURE_GPU), str),
+                field(lambda: nv.nvmlDeviceGetTotalEccErrors(handle, nv.NVML_MEMORY_ERROR_TYPE_UNCORRECTED,
+                                                             nv.NVML_VOLATILE_ECC), str),
+            ]))
+            time.sleep(0.0002)
+
     def start(self):
+        import threading
+        self.stop_flag = False
+        try:
+            import pynvml as nv
+            nv.nvmlInit()
+            handle = nv.nvmlDeviceGetHandleByIndex(self.gpu)
+            self.thread = threading.Thread(target=self._poll, args=(handle, nv), daemon=True)
+            self.thread.start()
+            return
+        except Exception:
+            self.thread = None
         import tempfile
         from vkb import load_judge
         try:
@@ -90,20 +127,27 @@ class ClockSampler:
 
     def stop(self):
         from vkb import load_judge
-        if self.proc is None:
+        if self.thread is not None:
+            self.stop_flag = True
+            self.thread.join(timeout=5)
+            text, how = "\n".join(self.rows) + "\n", f"NVML every 0.2 ms inside the timed region, {len(self.rows)} samples"
+            v = load_judge.judge(text, assume_busy=True)
+        elif self.proc is not None:
+            time.sleep(0.06)
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+            self.f.close()
+            with open(self.path, encoding="utf-8", errors="replace") as fh:
+                v = load_judge.judge(fh.read())
+            os.unlink(self.path)
+            how = "nvidia-smi every 20 ms"
+        else:
             return None
-        time.sleep(0.06)
-        self.proc.terminate()
-        try:
-            self.proc.wait(timeout=5)
-        except subprocess.TimeoutExpired:
-            self.proc.kill()
-        self.f.close()
-        with open(self.path, encoding="utf-8", errors="replace") as fh:
-            v = load_judge.judge(fh.read())
-        os.unlink(self.path)
         return {"sm_mhz": v.median_clock, "sm_max_mhz": v.max_clock, "reasons": v.reason_names(),
-                "samples": v.busy, "flagged": v.flagged, "judge": load_judge.format_line("timed", v)}
+                "samples": v.busy, "flagged": v.flagged, "how": how, "judge": load_judge.format_line("timed", v)}
 
 
 # ---- the reference's CPU path ----------------------------------------------------------------------------------------

@@ -60,3 +60,17 @@ def test_cli():
     assert r.returncode == 0 and "could not read samples" in r.stdout and "FLAGGED" in r.stdout
     r = subprocess.run([sys.executable, "-m", "vkb.load_judge", "7"], capture_output=True, text=True, env=env)
     assert r.returncode == 2
+
+
+def test_nvml_rows_inside_the_timed_region():
+    """bench.py's NVML sampler polls only while the timed work runs: a zero utilization reading (NVML's counter
+    averages over a longer window) still counts as busy with assume_busy, and a slowdown reason still rejects."""
+    ok = "0,1965,1965,612.0,0x0000000000000000,-,-,-,-,0,41,0\n" * 5
+    v = J.judge(ok, assume_busy=True)
+    assert v.busy == 5 and not v.flagged and v.median_clock == 1965
+    assert J.judge(ok).busy == 0 and J.judge(ok).flagged          # without it: idle samples only
+    bad = "0,1965,1965,612.0,0x0000000000000008,-,-,-,-,0,41,0\n"
+    v = J.judge(bad, assume_busy=True)
+    assert v.flagged and v.reason_names() == ["hw_slowdown"]
+    low = "0,1100,1965,300.0,0x0000000000000000,-,-,-,-,0,41,0\n"
+    assert J.judge(low, assume_busy=True).low == 1                   # a low clock with no reason: a leftover lock

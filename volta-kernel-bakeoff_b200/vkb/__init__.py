@@ -39,6 +39,12 @@ def lib() -> ctypes.CDLL:
         return _lib
     if not os.path.exists(LIB_PATH):
         raise ImportError(f"{LIB_PATH} is missing: build it with python volta-kernel-bakeoff_b200/build.py")
+    # libvkb.so needs libnccl.so.2. When torch is installed, load it first: its bundled (newer) NCCL then serves both;
+    # loaded the other way round, the system NCCL would be bound first and torch's import would miss symbols.
+    try:
+        import torch  # noqa: F401
+    except ImportError:
+        pass
     L = ctypes.CDLL(LIB_PATH)
     vp, i, sz = ctypes.c_void_p, ctypes.c_int, ctypes.c_size_t
     for name in ("vkb_gemv_q4", "vkb_gemv_q8", "vkb_gemv_q2", "vkb_gemv_q4_f32", "vkb_gemv_q8_f32", "vkb_gemv_q2_f32"):

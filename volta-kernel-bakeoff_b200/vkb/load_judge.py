@@ -107,7 +107,10 @@ def _plural(n: int, what: str) -> str:
     return f"{n} {what}" if n == 1 else f"{n} {what}s"
 
 
-def judge(text: str) -> Verdict:
+def judge(text: str, assume_busy: bool = False) -> Verdict:
+    """assume_busy: every sample was taken while the timed work ran (bench.py's NVML sampler polls only inside the
+    timed region), so a zero utilization reading -- NVML averages it over a longer window than a short burst -- does
+    not make a sample idle."""
     v = Verdict()
     rows, malformed = _rows(text)
     clocks, ecc_vals = [], []
@@ -119,8 +122,10 @@ def judge(text: str) -> Verdict:
             bad_ecc += 1
         else:
             ecc_vals.append(ecc)
-        if util == 0:
+        if util == 0 and not assume_busy:
             continue   # idle: the GPU may clock down
+        if util == 0:
+            util = 100.0
         if util is None:
             bad_util += 1
         else:
