@@ -70,9 +70,9 @@ def step_bytes() -> float:
 class ClockSampler:
     """Clock samples during the timed region -- SM clock, max clock, power, clock-event reasons, utilization,
     temperature, uncorrected ECC, in nvidia-smi's CSV columns -- judged by vkb.load_judge (the B200 counterpart of the
-    reference's bench/load_flag.py). NVML is polled from a thread every 0.2 ms while the timed work runs (the timed
-    region of a default run is a few milliseconds, shorter than nvidia-smi's sampling period); without NVML it falls
-    back to nvidia-smi every 20 ms."""
+    reference's bench/load_flag.py). NVML is polled from a thread as fast as it answers while the timed work runs (the
+    timed region of a default run is a few milliseconds, shorter than nvidia-smi's sampling period); without NVML it
+    falls back to nvidia-smi every 20 ms."""
 
     def __init__(self, gpu_index: int):
         self.gpu = gpu_index
@@ -82,35 +82,45 @@ class ClockSampler:
         self.path = None
 
     def _poll(self, handle, nv):
+        # the fast queries (SM clock, clock-event reasons) in the loop; power, utilization, temperature and uncorrected
+        # ECC -- slower queries -- once at the start and once at the end of the timed window
         def field(fn, fmt):
             try:
                 return fmt(fn())
             except Exception:
                 return "[N/A]"
+
+        def slow():
+            return (field(lambda: nv.nvmlDeviceGetPowerUsage(handle) / 1000.0, lambda w: f"{w:.1f}"),
+                    field(lambda: nv.nvmlDeviceGetUtilizationRates(handle).gpu, str),
+                    field(lambda: nv.nvmlDeviceGetTemperature(handle, nv.NVML_TEMPERATURE_GPU), str),
+                    field(lambda: nv.nvmlDeviceGetTotalEccErrors(handle, nv.NVML_MEMORY_ERROR_TYPE_UNCORRECTED,
+                                                                 nv.NVML_VOLATILE_ECC), str))
+        mx = field(lambda: nv.nvmlDeviceGetMaxClockInfo(handle, nv.NVML_CLOCK_SM), str)
+        sl = slow()
+        fast = []
         while not self.stop_flag:
-            self.rows.append(",".join([
-                str(self.gpu),
-                field(lambda: nv.nvmlDeviceGetClockInfo(handle, nv.NVML_CLOCK_SM), str),
-                field(lambda: nv.nvmlDeviceGetMaxClockInfo(handle, nv.NVML_CLOCK_SM), str),
-                field(lambda: nv.nvmlDeviceGetPowerUsage(handle) / 1000.0, lambda w: f"{w:.1f}"),
-                field(lambda: nv.nvmlDeviceGetCurrentClocksEventReasons(handle), lambda b: f"0x{b:016x}"),
-                "-", "-", "-", "-",
-                field(lambda: nv.nvmlDeviceGetUtilizationRates(handle).gpu, str),
-                field(lambda: nv.nvmlDeviceGetTemperature(handle, nv.NVML_TEMPERATURE_GPU), str),
-                field(lambda: nv.nvmlDeviceGetTotalEccErrors(handle, nv.NVML_MEMORY_ERROR_TYPE_UNCORRECTED,
-                                                             nv.NVML_VOLATILE_ECC), str),
-            ]))
-            time.sleep(0.0002)
+            fast.append((field(lambda: nv.nvmlDeviceGetClockInfo(handle, nv.NVML_CLOCK_SM), str),
+                         field(lambda: nv.nvmlDeviceGetCurrentClocksEventReasons(handle), lambda b: f"0x{b:016x}")))
+            self.polling.set()
+        sl_end = slow()
+        for i, (clk, why) in enumerate(fast):
+            pw, util, temp, ecc = sl if i < len(fast) // 2 else sl_end
+            self.rows.append(",".join([str(self.gpu), clk, mx, pw, why, "-", "-", "-", "-", util, temp, ecc]))
 
     def start(self):
         import threading
         self.stop_flag = False
+        self.polling = threading.Event()
         try:
             import pynvml as nv
             nv.nvmlInit()
             handle = nv.nvmlDeviceGetHandleByIndex(self.gpu)
+            self.switch = sys.getswitchinterval()
+            sys.setswitchinterval(1e-4)   # let the sampling thread run while the main thread waits on the GPU
             self.thread = threading.Thread(target=self._poll, args=(handle, nv), daemon=True)
             self.thread.start()
+            self.polling.wait(timeout=2.0)   # the timed region starts once the sampling loop runs
             return
         except Exception:
             self.thread = None
@@ -130,7 +140,8 @@ class ClockSampler:
         if self.thread is not None:
             self.stop_flag = True
             self.thread.join(timeout=5)
-            text, how = "\n".join(self.rows) + "\n", f"NVML every 0.2 ms inside the timed region, {len(self.rows)} samples"
+            sys.setswitchinterval(self.switch)
+            text, how = "\n".join(self.rows) + "\n", f"NVML polled inside the timed region, {len(self.rows)} samples"
             v = load_judge.judge(text, assume_busy=True)
         elif self.proc is not None:
             time.sleep(0.06)
