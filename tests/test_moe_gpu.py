@@ -73,11 +73,31 @@ def test_moe_formats_and_crowded_expert(cuda, fmt):
     assert err <= 1e-3, (err, m, n)
 
 
-def test_moe_expert_parallel_subsets(cuda):
+@pytest.mark.parametrize("fmt", [O.FMT_Q4, O.FMT_Q8, O.FMT_Q2])
+@pytest.mark.parametrize("T", [1, 3, 8])
+def test_moe_few_tokens_with_repeated_experts(cuda, fmt, T):
+    """At most 8 tokens (their rows stay staged, and a column finds its token as slot / k): more slots per token than
+    experts, so experts repeat inside a token; token 0 sends all its slots to one expert (one 8-column group of a
+    single token); ragged row tiles (N = 96 + 8)."""
+    rng = np.random.default_rng(60 + 10 * fmt + T)
+    E, N, K, k = 6, 104, 768, 8
+    codes, scales = _pool(rng, fmt, E, N, K)
+    q, s = _upload(fmt, codes, scales)
+    idx = rng.integers(0, E, size=(T, k)).astype(np.int32)
+    idx[0, :] = 4
+    x = rng.uniform(-1, 1, size=(T, K)).astype(np.float16).view(np.uint16)
+    y = _run(fmt, q, s, idx, x)
+    ref, mag, _ = O.moe_ref(codes, scales, idx, x)
+    err, m, n = O.check_error(y, ref, mag)
+    assert err <= 1e-3, (err, m, n)
+
+
+@pytest.mark.parametrize("T", [2, 8])   # 16 slots (the one-slot-per-lane routing) and 64
+def test_moe_expert_parallel_subsets(cuda, T):
     """Four ranks' worth of pools (32 experts each) fill disjoint slots; their union is the full result, and a pool
     never touches slots routed elsewhere (sentinels)."""
-    rng = np.random.default_rng(11)
-    E, N, K, T, k, G = 128, 512, 2048, 8, 8, 4
+    rng = np.random.default_rng(11 + T)
+    E, N, K, k, G = 128, 512, 2048, 8, 4
     codes, scales = _pool(rng, O.FMT_Q4, E, N, K)
     idx = vkb.synth_topk(99, T, E, k)
     x = rng.uniform(-1, 1, size=(T, K)).astype(np.float16).view(np.uint16)
@@ -93,6 +113,22 @@ def test_moe_expert_parallel_subsets(cuda):
         union[mine] = y[mine]
     assert not np.isnan(union).any()
     err, m, n = O.check_error(union, ref, mag)
+    assert err <= 1e-3, (err, m, n)
+
+
+@pytest.mark.parametrize("T,k", [(4, 8), (11, 3), (2, 16)])
+def test_moe_routing_boundaries(cuda, T, k):
+    """32 slots (the largest list routed one slot per lane), 33 slots over 11 tokens (the general routing with the
+    per-segment activation rows), and 16 slots over 2 tokens with experts repeated across and inside tokens."""
+    rng = np.random.default_rng(70 + T * k)
+    E, N, K = 9, 48, 512
+    codes, scales = _pool(rng, O.FMT_Q4, E, N, K)
+    q, s = _upload(O.FMT_Q4, codes, scales)
+    idx = rng.integers(0, E, size=(T, k)).astype(np.int32)
+    x = rng.uniform(-1, 1, size=(T, K)).astype(np.float16).view(np.uint16)
+    y = _run(O.FMT_Q4, q, s, idx, x)
+    ref, mag, _ = O.moe_ref(codes, scales, idx, x)
+    err, m, n = O.check_error(y, ref, mag)
     assert err <= 1e-3, (err, m, n)
 
 

@@ -287,6 +287,10 @@ __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.lau
 __device__ __forceinline__ void named_sync(uint32_t id, uint32_t nthreads) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
+// Arrive on named barrier `id` without waiting (the threads that wait on it see this thread's earlier writes).
+__device__ __forceinline__ void named_arrive(uint32_t id, uint32_t nthreads) {
+    asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
 
 // ---- m16n8k16 f16 x f16 -> f32 ----------------------------------------------------------------------------------
 

@@ -52,6 +52,21 @@ constexpr int QMV_MAXTOK = 8;      // tokens per MMA column group (the MMA's N)
 // writes out = silu(gate) * up (and the stacked products, when asked). Stages and reductions are the dense GEMV's.
 enum : int { QMV_DENSE = 0, QMV_MOE = 1, QMV_MOE_P2P = 2, QMV_GLU = 3 };
 
+// Division by a divisor fixed at launch, without the ~150-cycle integer division sequence on the kernels' prologue
+// path (a MoE call's whole prologue comes after its dependency): q = (umulhi(x, mul) + x) >> shift with the host's
+// round-up multiplier mul = floor(2^32 (2^shift - d) / d) + 1, shift = ceil(log2 d); exact for 0 <= x < 2^31.
+struct FastDiv {
+    uint32_t mul, shift;
+};
+__host__ __device__ inline FastDiv make_fastdiv(uint32_t d) {
+    uint32_t l = 0;
+    while ((1ull << l) < d) ++l;
+    return FastDiv{(uint32_t)(((1ull << 32) * ((1ull << l) - d)) / d + 1), l};
+}
+__device__ __forceinline__ int fdiv(int x, FastDiv f) {
+    return (int)((__umulhi((uint32_t)x, f.mul) + (uint32_t)x) >> f.shift);
+}
+
 struct QmvArgs {
     const __half* x;         // [T][K] (fp32 [T][K] for the XF32 kernels)
     float* ys;               // QMV_GLU: the stacked products [T][2N] (gate, then up) or null
@@ -69,9 +84,11 @@ struct QmvArgs {
     int stage_bytes;         // shared bytes per stage (1024-aligned)
     int xpitch;              // shared bytes per staged activation row
     int xrows;               // staged activation rows per buffer (<= 8)
+    int xres;                // MoE over T <= 8 tokens: all T rows staged once (one buffer); else per segment (two)
     int tilesN;              // ceil(N / 16)
     int wg;                  // consumer warp groups (1, 2 or 4), with nstage >= wg * nchunks
     int ring_off, x_off, red_off, bar_off, moe_off;   // shared-memory carve-up (bytes from the aligned base)
+    FastDiv dv_tiles, dv_topk, dv_grid;               // by tilesN, topk (MoE; else 1), the launch's grid size
 };
 
 // ---- per-format unpack: one 32-bit word of codes -> the four f16x2 A registers this thread feeds the MMA ----------
@@ -214,90 +231,151 @@ template <typename OutT> __device__ __forceinline__ OutT to_out(float v);
 template <> __device__ __forceinline__ __half to_out<__half>(float v) { return __float2half_rn(v); }
 template <> __device__ __forceinline__ float to_out<float>(float v) { return v; }
 
-// ---- MoE routing tables (built redundantly and deterministically by every CTA) ---------------------------------
+// ---- MoE routing tables (built by each CTA's producer warp, deterministically: every CTA builds the same) -------
 //
-// A "segment" is one expert with up to 8 of its (token, slot) pairs: the tokens of one MMA column group. Slots of an
-// expert are taken in increasing slot order, so every CTA builds the identical table.
+// A "segment" is one expert with up to 8 of its (token, slot) pairs: the tokens of one MMA column group. The experts
+// a call routes to are numbered in order of first appearance in the index list ("order ids"); each expert's slots are
+// taken in increasing slot order. Segment order does not change any result (each output row is one tile's sum).
 struct MoeTables {
-    int* cnt;       // [E_local]
-    int* off;       // [E_local + 1]  first position of each expert in `slots`
-    int* segoff;    // [E_local + 1]  first segment of each expert
-    int* slots;     // [T*topk]      slot ids grouped by expert
-    int* seg;       // [T*topk]      (expert << 16) | first position in `slots`
+    int* eid;      // [E_local]     order id of each local expert, -1 before it appears (lists of more than 32 slots)
+    int* ord;      // [nslots]      local expert of each order id
+    int* cnt;      // [nslots]      slots of each order id (lists of more than 32 slots)
+    int* off;      // [nslots + 1]  first position in `slots` of each order id; off[experts seen] = routed slots
+    int* segoff;   // [nslots + 1]  first segment of each order id
+    int* slots;    // [nslots]      slot ids grouped by expert
+    int* seg;      // [nslots]      (order id << 16) | first position in `slots`
+    int* nseg;     // [1]           segments
 };
+// the arrays above, in this order: E_local + 4 * nslots + 2 * (nslots + 1) + 1 words
+__host__ __device__ constexpr int moe_table_words(int E_local, int nslots) { return E_local + 6 * nslots + 3; }
 
 __device__ __forceinline__ MoeTables moe_tables(uint8_t* base, int E_local, int nslots) {
     MoeTables t;
     int* p = reinterpret_cast<int*>(base);
-    t.cnt = p; p += E_local;
-    t.off = p; p += E_local + 1;
-    t.segoff = p; p += E_local + 1;
+    t.eid = p; p += E_local;
+    t.ord = p; p += nslots;
+    t.cnt = p; p += nslots;
+    t.off = p; p += nslots + 1;
+    t.segoff = p; p += nslots + 1;
     t.slots = p; p += nslots;
-    t.seg = p;
+    t.seg = p; p += nslots;
+    t.nseg = p;
     return t;
 }
 
-// Returns the number of segments. Call with all threads of the CTA.
-__device__ __forceinline__ int moe_route(const QmvArgs& a, MoeTables tb) {
-    const int nslots = a.T * a.topk;
-    const int tid = threadIdx.x, nth = blockDim.x;
-    for (int e = tid; e < a.E_local; e += nth) tb.cnt[e] = 0;
-    __syncthreads();
-    for (int i = tid; i < nslots; i += nth) {
-        const int e = __ldg(a.idx + i) - a.e0;
-        if (e >= 0 && e < a.E_local) atomicAdd(&tb.cnt[e], 1);
-    }
-    __syncthreads();
-    if (tid < 32) {   // one warp: exclusive scans, then a stable placement of the slots
-        const int lane = tid;
-        int run_off = 0, run_seg = 0;
-        for (int b = 0; b < a.E_local; b += 32) {
-            const int e = b + lane;
-            const int c = e < a.E_local ? tb.cnt[e] : 0;
-            const int s = (c + QMV_MAXTOK - 1) / QMV_MAXTOK;
-            int ic = c, is = s;
+// At most 32 slots (one per lane): grouping by __match_any_sync, order ids from a ballot of the group leaders, and one
+// packed warp scan of (slots, segments) over the leaders -- registers only, then the table stores.
+__device__ __forceinline__ void moe_route_small(const QmvArgs& a, MoeTables tb, int lane, int nslots) {
+    const unsigned all = 0xffffffffu, below = (1u << lane) - 1u;
+    int e = lane < nslots ? __ldg(a.idx + lane) - a.e0 : -1;
+    if (e < 0 || e >= a.E_local) e = -1;
+    const unsigned same = __match_any_sync(all, e);
+    const int leader = __ffs(same) - 1;
+    const bool lead = e >= 0 && lane == leader;
+    const unsigned leaders = __ballot_sync(all, lead);
+    const int c = __popc(same), segs = (c + QMV_MAXTOK - 1) / QMV_MAXTOK;
+    const int mine = lead ? (c | (segs << 16)) : 0;   // slots in the low half (<= 32), segments in the high half
+    int v = mine;
 #pragma unroll
-            for (int d = 1; d < 32; d <<= 1) {
-                const int vc = __shfl_up_sync(0xffffffffu, ic, d);
-                const int vs = __shfl_up_sync(0xffffffffu, is, d);
-                if (lane >= d) { ic += vc; is += vs; }
-            }
-            if (e < a.E_local) {
-                tb.off[e] = run_off + ic - c;
-                tb.segoff[e] = run_seg + is - s;
-                tb.cnt[e] = 0;   // from here on: placement cursor
-            }
-            run_off += __shfl_sync(0xffffffffu, ic, 31);
-            run_seg += __shfl_sync(0xffffffffu, is, 31);
+    for (int d = 1; d < 32; d <<= 1) {
+        const int u = __shfl_up_sync(all, v, d);
+        if (lane >= d) v += u;
+    }
+    const int excl = v - mine, tot = __shfl_sync(all, v, 31);
+    const int gexcl = __shfl_sync(all, excl, leader);
+    if (e >= 0) tb.slots[(gexcl & 0xFFFF) + __popc(same & below)] = lane;
+    if (lead) {
+        const int id = __popc(leaders & below), first = excl & 0xFFFF, s0 = excl >> 16;
+        tb.ord[id] = e;
+        tb.off[id] = first;
+        tb.segoff[id] = s0;
+        for (int k = 0; k < segs; ++k) tb.seg[s0 + k] = (id << 16) | (first + k * QMV_MAXTOK);
+    }
+    if (lane == 0) {
+        const int seen = __popc(leaders);
+        tb.off[seen] = tot & 0xFFFF;
+        tb.segoff[seen] = tot >> 16;
+        *tb.nseg = tot >> 16;
+    }
+    __syncwarp();
+}
+
+// Any number of slots: the local expert of every slot staged in `slots`; 32 slots at a time (in slot order) each
+// slot's rank among the earlier slots of its expert, and order ids for the experts met for the first time; exclusive
+// scans of the counts over the order ids; placement; segments.
+__device__ __forceinline__ void moe_route_general(const QmvArgs& a, MoeTables tb, int lane, int nslots) {
+    const unsigned all = 0xffffffffu, below = (1u << lane) - 1u;
+    for (int i = lane; i < nslots; i += 32) {
+        const int e = __ldg(a.idx + i) - a.e0;
+        tb.slots[i] = (e < 0 || e >= a.E_local) ? -1 : e;
+    }
+    for (int e = lane; e < a.E_local; e += 32) tb.eid[e] = -1;
+    __syncwarp();
+    int seen = 0;
+    for (int i0 = 0; i0 < nslots; i0 += 32) {
+        const int i = i0 + lane;
+        const int e = i < nslots ? tb.slots[i] : -1;
+        const unsigned same = __match_any_sync(all, e);
+        const int leader = __ffs(same) - 1;
+        const bool lead = e >= 0 && lane == leader;
+        int id = lead ? tb.eid[e] : 0, base = 0;
+        const bool fresh = lead && id < 0;
+        const unsigned fm = __ballot_sync(all, fresh);
+        if (fresh) {
+            id = seen + __popc(fm & below);
+            tb.eid[e] = id;
+            tb.ord[id] = e;
+        } else if (lead) {
+            base = tb.cnt[id];
         }
-        if (lane == 0) {
-            tb.off[a.E_local] = run_off;
-            tb.segoff[a.E_local] = run_seg;
-        }
+        if (lead) tb.cnt[id] = base + __popc(same);
+        seen += __popc(fm);
+        id = __shfl_sync(all, id, leader);
+        base = __shfl_sync(all, base, leader);
+        if (i < nslots) tb.seg[i] = e >= 0 ? (id << 16) | (base + __popc(same & below)) : -1;   // (staged rank)
         __syncwarp();
-        // 32 slots at a time, in slot order; a slot's rank = lanes below it with the same expert
-        for (int i0 = 0; i0 < nslots; i0 += 32) {
-            const int i = i0 + lane;
-            int e = i < nslots ? __ldg(a.idx + i) - a.e0 : -1;
-            if (e < 0 || e >= a.E_local) e = -1;
-            const unsigned same = __match_any_sync(0xffffffffu, e);
-            const int rank = __popc(same & ((1u << lane) - 1u));
-            const int leader = __ffs(same) - 1;
-            int base = (e >= 0 && lane == leader) ? tb.cnt[e] : 0;
-            base = __shfl_sync(0xffffffffu, base, leader);
-            if (e >= 0) tb.slots[tb.off[e] + base + rank] = i;
-            __syncwarp();
-            if (e >= 0 && lane == leader) tb.cnt[e] = base + __popc(same);
-            __syncwarp();
+    }
+    int run_off = 0, run_seg = 0;
+    for (int b = 0; b < seen; b += 32) {
+        const int id = b + lane;
+        const int c = id < seen ? tb.cnt[id] : 0;
+        const int s = (c + QMV_MAXTOK - 1) / QMV_MAXTOK;
+        int ic = c, is = s;
+#pragma unroll
+        for (int d = 1; d < 32; d <<= 1) {
+            const int vc = __shfl_up_sync(all, ic, d);
+            const int vs = __shfl_up_sync(all, is, d);
+            if (lane >= d) { ic += vc; is += vs; }
         }
+        if (id < seen) {
+            tb.off[id] = run_off + ic - c;
+            tb.segoff[id] = run_seg + is - s;
+        }
+        run_off += __shfl_sync(all, ic, 31);
+        run_seg += __shfl_sync(all, is, 31);
     }
-    __syncthreads();
-    for (int e = tid; e < a.E_local; e += nth) {
-        const int first = tb.off[e], n = tb.off[e + 1] - first, s0 = tb.segoff[e];
-        for (int c = 0; c * QMV_MAXTOK < n; ++c) tb.seg[s0 + c] = (e << 16) | (first + c * QMV_MAXTOK);
+    if (lane == 0) {
+        tb.off[seen] = run_off;
+        tb.segoff[seen] = run_seg;
+        *tb.nseg = run_seg;
     }
-    __syncthreads();
-    return tb.segoff[a.E_local];
+    __syncwarp();
+    for (int i = lane; i < nslots; i += 32) {
+        const int v = tb.seg[i];
+        if (v >= 0) tb.slots[tb.off[v >> 16] + (v & 0xFFFF)] = i;
+    }
+    __syncwarp();
+    for (int id = lane; id < seen; id += 32) {
+        const int first = tb.off[id], n = tb.off[id + 1] - first, s0 = tb.segoff[id];
+        for (int k = 0; k * QMV_MAXTOK < n; ++k) tb.seg[s0 + k] = (id << 16) | (first + k * QMV_MAXTOK);
+    }
+    __syncwarp();
+}
+
+__device__ __forceinline__ void moe_route_warp(const QmvArgs& a, MoeTables tb, int lane) {
+    const int nslots = a.T * a.topk;
+    if (nslots <= 32) moe_route_small(a, tb, lane, nslots);
+    else moe_route_general(a, tb, lane, nslots);
 }
 
 // ---- expert-parallel MoE with peer stores: the push of a CTA's outputs ---------------------------------------------
@@ -317,13 +395,13 @@ __device__ __noinline__ void qmv_moe_push(const QmvArgs& a, MoeTables tb, int w0
     rd = __shfl_sync(0xffffffffu, rd ? 1 : 0, 0) != 0;
     if (rd && w1 > w0) {
         const size_t rowp = (size_t)a.N * sizeof(OutT);
-        for (int sg = w0 / a.tilesN; sg <= (w1 - 1) / a.tilesN; ++sg) {
+        for (int sg = fdiv(w0, a.dv_tiles); sg <= fdiv(w1 - 1, a.dv_tiles); ++sg) {
             const int ta = max(w0, sg * a.tilesN) - sg * a.tilesN;
             const int tb_ = min(w1, (sg + 1) * a.tilesN) - sg * a.tilesN;
             const int n0 = ta * QMV_ROWS, n1 = min(a.N, tb_ * QMV_ROWS);
             if (n1 <= n0) continue;
-            const int first = tb.seg[sg] & 0xFFFF, e = tb.seg[sg] >> 16;
-            const int cnt = min(QMV_MAXTOK, tb.off[e + 1] - first);
+            const int first = tb.seg[sg] & 0xFFFF, id = tb.seg[sg] >> 16;
+            const int cnt = min(QMV_MAXTOK, tb.off[id + 1] - first);
             const size_t off0 = (size_t)n0 * sizeof(OutT);
             p2p_push(a.pp, cnt, (n1 - n0) * (int)sizeof(OutT), rowp | off0,
                      [&](int r) { return (size_t)tb.slots[first + r] * rowp + off0; }, threadIdx.x, QMV_NW * 32);
@@ -338,9 +416,9 @@ __device__ __noinline__ void qmv_moe_push(const QmvArgs& a, MoeTables tb, int w0
 //
 // The consumer warps form WG groups of QMV_NW / WG warps. Group j takes every WG-th tile of the CTA's range (tiles
 // are independent), so WG tiles are in flight at once and each tile's partial sums are reduced over QMV_NW / WG warps
-// only. Dense calls use up to 4 groups; MoE uses one (all warps on one tile at a time), because its activations
-// change per expert segment and one double-buffered activation area is what shared memory holds for eight tokens.
-// The host keeps nstage >= WG * nchunks: a group then never waits on a ring slot more than one phase ahead of that
+// only. The plan sets WG (up to 4); for MoE the host caps it at the most tiles a CTA can get from the call's slot
+// count (at one token a CTA holds one or two 16-row tiles, and a tile's latency is each warp's chain of dependent
+// MMAs over its share of K, so one tile is best split over all 16 warps). The host keeps nstage >= WG * nchunks: a group then never waits on a ring slot more than one phase ahead of that
 // slot's last completed phase, which is all an mbarrier parity wait can tell apart.
 //
 // Barrier block layout (uint64 slots from bar_off): full[nstage], empty[nstage], xfull[2], xempty[2],
@@ -360,8 +438,6 @@ qmv_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUten
     static_assert(!XF32 || MODE == QMV_DENSE || MODE == QMV_GLU, "fp32 activations: dense and gate/up calls");
     constexpr bool GLU = MODE == QMV_GLU;
     constexpr bool MOE = MODE == QMV_MOE || MODE == QMV_MOE_P2P;
-    const int WG = a.wg;
-    const int WPG = QMV_NW / WG;
     extern __shared__ uint8_t smem_raw[];
     const uint32_t pad = (1024u - (smem_u32(smem_raw) & 1023u)) & 1023u;
     uint8_t* sm = smem_raw + pad;   // pointer arithmetic on the shared array keeps the shared address space
@@ -384,17 +460,19 @@ qmv_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUten
 
     pdl_trigger();   // the next call may start its weight prefetch now (it still waits for us before touching x, y)
 
-    if (threadIdx.x == 0) {
+    // barrier initialisation for wg warp groups (one thread; the CTA's barrier follows)
+    auto init_bars = [&](int wg) {
+        const int wpg = QMV_NW / wg;
         for (int i = 0; i < a.nstage; ++i) {
             mbar_init(&full[i], 1);
-            mbar_init(&empty[i], WPG);
+            mbar_init(&empty[i], wpg);
         }
         for (int i = 0; i < 2; ++i) {
             mbar_init(&xfull[i], 1);
             mbar_init(&xempty[i], QMV_NW);
         }
-        for (int i = 0; i < 2 * WG; ++i) {
-            mbar_init(&redfull[i], WPG);
+        for (int i = 0; i < 2 * wg; ++i) {
+            mbar_init(&redfull[i], wpg);
             mbar_init(&redfree[i], 1);
         }
         for (int i = 0; i < 2; ++i) {
@@ -402,27 +480,60 @@ qmv_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUten
             mbar_init(&gfree[i], 1);
         }
         fence_mbar_init();
-    }
-
-    int nseg = 1;
+    };
+    // the CTA's tiles [w0, w1) of nseg segments x tilesN tiles; gate/up tiles are split in whole pairs
+    auto cta_range = [&](int nseg, int& w0, int& w1) {
+        const int total = nseg * a.tilesN;
+        const unsigned units = GLU ? total / 2 : total, ustep = GLU ? 2 : 1, b = blockIdx.x, n = gridDim.x;
+        if ((unsigned long long)units * n < 0x80000000ull) {
+            w0 = (int)ustep * fdiv((int)(b * units), a.dv_grid);
+            w1 = (int)ustep * fdiv((int)((b + 1) * units), a.dv_grid);
+        } else {
+            w0 = (int)(ustep * (unsigned)(((unsigned long long)b * units) / n));
+            w1 = (int)(ustep * (unsigned)(((unsigned long long)(b + 1) * units) / n));
+        }
+    };
     MoeTables tb{};
     if constexpr (MOE) {
+        // the producer warp: barriers, then -- after the dependency, since the previous grid may have written the
+        // index list and the activations -- the resident token rows and the routing tables. The consumers wait for
+        // the tables; the producer goes on to the weight stream without waiting for them.
         tb = moe_tables(sm + a.moe_off, a.E_local, a.T * a.topk);
-        nseg = moe_route(a, tb);   // contains __syncthreads
+        if (warp == QMV_NW) {
+            if (lane == 0) {
+                prefetch_tmap(&tq);   // (the descriptors' fetch overlaps the dependency wait and the routing)
+                prefetch_tmap(&ts);
+                init_bars(a.wg);
+            }
+            pdl_wait();
+            if (lane == 0 && a.xres) {
+                mbar_arrive_expect_tx(&xfull[0], (uint32_t)(a.T * a.K * 2));
+                for (int j = 0; j < a.T; ++j)
+                    bulk_load(xbuf + j * a.xpitch, a.x + (size_t)j * a.K, (uint32_t)(a.K * 2), &xfull[0]);
+            }
+            moe_route_warp(a, tb, lane);
+            named_arrive(2, 32 * (QMV_NW + 1));
+        } else {
+            named_sync(2, 32 * (QMV_NW + 1));
+        }
     } else {
+        if (threadIdx.x == 0) init_bars(a.wg);
         __syncthreads();
     }
 
-    const int total = nseg * a.tilesN;
-    // the CTA's tiles [w0, w1); gate/up tiles are split in whole pairs
-    const int units = GLU ? total / 2 : total, ustep = GLU ? 2 : 1;
-    const int w0 = ustep * (int)(((long long)blockIdx.x * units) / gridDim.x);
-    const int w1 = ustep * (int)(((long long)(blockIdx.x + 1) * units) / gridDim.x);
+    int nseg = 1;
+    if constexpr (MOE) nseg = *tb.nseg;
+    int w0, w1;
+    cta_range(nseg, w0, w1);
     const int ntl = w1 - w0;   // tiles of this CTA
+    const int WG = a.wg;                    // 1, 2 or 4
+    const int wpg_log = 5 - __ffs(WG);      // WPG = 16 / WG = 1 << wpg_log
+    const int WPG = 1 << wpg_log;
+    const bool xres = MOE && a.xres != 0;
 
     // segment accessors: expert (weight row base), token count, and the slot (dense: token) of column j
     auto seg_expert = [&](int sg) -> int {
-        if constexpr (MOE) return tb.seg[sg] >> 16; else return 0;
+        if constexpr (MOE) return tb.ord[tb.seg[sg] >> 16]; else return 0;
     };
     auto seg_first = [&](int sg) -> int {
         if constexpr (MOE) return tb.seg[sg] & 0xFFFF; else return 0;
@@ -447,7 +558,7 @@ qmv_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUten
             const int total_it = ntl * a.nchunks;
             const int pre = min(total_it, a.nstage);
             // iteration cursor: chunk c of tile `tile` of segment `sg`; ring slot stg in round rnd
-            int c = 0, sg = w0 / a.tilesN, tile = w0 % a.tilesN, stg = 0, rnd = 0, issued = 0;
+            int c = 0, sg = fdiv(w0, a.dv_tiles), tile = w0 - sg * a.tilesN, stg = 0, rnd = 0, issued = 0;
             auto issue_w = [&]() {
                 uint8_t* st = ring + stg * a.stage_bytes;
                 uint64_t* fb = &full[stg];
@@ -463,9 +574,10 @@ qmv_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUten
                 }
                 if (++stg == a.nstage) { stg = 0; ++rnd; }
             };
-            int xsegs = 0;
+            int xsegs = xres ? 1 : 0;   // activation copies issued (resident rows: the one of the prologue)
             bool ok = true;
             auto issue_x = [&](int xs) {   // activations of the next segment this CTA meets, double-buffered
+                if (xres) return;          // (resident rows: already on their way)
                 const int xb = xsegs & 1;
                 if (xsegs >= 2) ok = wait_parity(&xempty[xb], ((xsegs >> 1) - 1) & 1);
                 if (!ok) return;
@@ -484,7 +596,7 @@ qmv_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUten
             // activations of the segments the prefetched stages belong to, in order
             int last_seg = -1;
             {
-                int xsg = w0 / a.tilesN, xtile = w0 % a.tilesN;
+                int xsg = fdiv(w0, a.dv_tiles), xtile = w0 - xsg * a.tilesN;
                 for (int it = 0; it < pre && ok; it += a.nchunks) {
                     if (xsg != last_seg) {
                         if constexpr (!XF32) issue_x(xsg);   // XF32: the consumers fill the buffer
@@ -520,28 +632,44 @@ qmv_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUten
     }
 
     // ===================== consumers (warps 0..NW-1, WG groups) =====================
-    const int grp = warp / WPG, wi = warp % WPG;
+#ifndef VKB_QMV_SLEEP
+#define VKB_QMV_SLEEP 1
+#endif
+    constexpr bool SLEEP = VKB_QMV_SLEEP == 2 || (VKB_QMV_SLEEP == 1 && MOE);
+    auto cwait = [&](uint64_t* bar, uint32_t parity) -> bool {
+        if constexpr (SLEEP) return wait_parity_sleep(bar, parity); else return wait_parity(bar, parity);
+    };
+    const int grp = warp >> wpg_log, wi = warp & (WPG - 1);
     const int g = lane >> 2, t = lane & 3;
     const int GS = a.KS / 32;
-    const int G0 = wi * GS / WPG, G1w = (wi + 1) * GS / WPG;
+    const int G0 = (wi * GS) >> wpg_log, G1w = ((wi + 1) * GS) >> wpg_log;
     const uint32_t cp = (uint32_t)a.cpitch, sp = (uint32_t)a.spitch;
     const uint32_t ring_s = smem_u32(ring);
     const uint32_t xbuf_s = smem_u32(xbuf);
     const uint32_t c_row = g * cp;                                       // row g's codes inside a stage
     const uint32_t s_row = (uint32_t)(QMV_ROWS * a.cpitch) + g * sp;     // row g's scales inside a stage
     OutT* y = reinterpret_cast<OutT*>(a.y);
-    pdl_wait();   // x and y may still be written (or y read) by the previous grid
+    // x and y may still be written (or y read) by the previous grid. MoE: the producer's wait, which the consumers
+    // are ordered after by the routing barrier, has already established that for the whole grid.
+    if constexpr (!MOE) pdl_wait();
     if constexpr (XF32) {   // fp32 activations -> the fp16 buffer of segment 0, then its barrier (count 1, no bytes)
+        const int K4 = a.K / 4;
         const float4* xf = reinterpret_cast<const float4*>(a.x);
-        const int total4 = a.T * a.K / 4;
-        for (int i = threadIdx.x; i < total4; i += QMV_NW * 32) {
-            const float4 v = xf[i];
-            const int e = 4 * i, m = e / a.K, k = e - m * a.K;
-            const uint32_t lo = cvt_h2(__float_as_uint(v.x), __float_as_uint(v.y));
-            const uint32_t hi = cvt_h2(__float_as_uint(v.z), __float_as_uint(v.w));
-            asm volatile("st.shared.v2.b32 [%0], {%1, %2};" ::"r"(xbuf_s + (uint32_t)(m * a.xpitch + 2 * k)), "r"(lo),
-                         "r"(hi)
-                         : "memory");
+        for (int i = threadIdx.x; i < K4; i += QMV_NW * 32) {   // every token's 4 values at i: loads first
+            float4 v[QMV_MAXTOK];
+#pragma unroll
+            for (int m = 0; m < QMV_MAXTOK; ++m)
+                if (m < a.T) v[m] = xf[(size_t)m * K4 + i];
+#pragma unroll
+            for (int m = 0; m < QMV_MAXTOK; ++m) {
+                if (m < a.T) {
+                    const uint32_t lo = cvt_h2(__float_as_uint(v[m].x), __float_as_uint(v[m].y));
+                    const uint32_t hi = cvt_h2(__float_as_uint(v[m].z), __float_as_uint(v[m].w));
+                    asm volatile("st.shared.v2.b32 [%0], {%1, %2};" ::"r"(xbuf_s + (uint32_t)(m * a.xpitch + 8 * i)),
+                                 "r"(lo), "r"(hi)
+                                 : "memory");
+                }
+            }
         }
         named_sync(1, QMV_NW * 32);
         if (threadIdx.x == 0) mbar_arrive(&xfull[0]);
@@ -563,8 +691,8 @@ qmv_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUten
     // Activation segments of this CTA, in order: j = sg - first_seg. Every warp enters (waits xfull) and leaves (arrives
     // xempty) every segment exactly once and in order -- also the ones it has no tile in -- so that an arrival is
     // never counted towards an earlier use of the same double buffer.
-    const int first_seg = w0 / a.tilesN;
-    const int last_seg = ntl > 0 ? (w1 - 1) / a.tilesN : first_seg - 1;
+    const int first_seg = fdiv(w0, a.dv_tiles);
+    const int last_seg = ntl > 0 ? fdiv(w1 - 1, a.dv_tiles) : first_seg - 1;
     int jn = 0;            // next segment to enter
     bool held = false;     // holding segment jn - 1
     int cnt = 0;
@@ -580,33 +708,42 @@ qmv_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUten
     auto enter_upto = [&](int j_target) -> bool {   // hold segment j_target, passing through the ones before it
         while (jn <= j_target) {
             leave();
-            if (!wait_parity(&xfull[jn & 1], (jn >> 1) & 1)) return false;
+            if (!cwait(&xfull[jn & 1], (jn >> 1) & 1)) return false;
             held = true;
             ++jn;
         }
         return true;
     };
     // this group's tiles: tl = grp, grp + WG, ...; their first stage iteration is tl * nchunks
-    int sg = (w0 + grp) / a.tilesN, tile = (w0 + grp) % a.tilesN;
+    int sg = fdiv(w0 + grp, a.dv_tiles), tile = w0 + grp - sg * a.tilesN;
     int stg = 0, rnd = 0;
     {
         const int it0 = grp * a.nchunks;   // the first iteration of this group (no division in the loop)
-        rnd = it0 / a.nstage;
-        stg = it0 - rnd * a.nstage;
+        stg = it0;
+        while (stg >= a.nstage) { stg -= a.nstage; ++rnd; }
     }
     int ntile = 0;   // tiles this group has done (reduction buffer parity / reducer rotation)
     for (int tl = grp; tl < ntl && ok; tl += WG, ++ntile) {
         if (sg - first_seg != jn - 1 || !held) {
-            if (!enter_upto(sg - first_seg)) { ok = false; break; }
-            const int xb = (jn - 1) & 1;
+            if (xres) {   // resident token rows: wait for them once
+                if (!held && !cwait(&xfull[0], 0)) { ok = false; break; }
+                held = true;
+                jn = sg - first_seg + 1;
+            } else if (!enter_upto(sg - first_seg)) {
+                ok = false;
+                break;
+            }
+            const int xb = xres ? 0 : (jn - 1) & 1;
             cnt = seg_count(sg);
-            xrow = xbuf_s + (uint32_t)(xb * a.xrows * a.xpitch + (g < cnt ? g : 0) * a.xpitch) +
-                   x_lane_off<F>(t);
+            const int col = g < cnt ? g : 0;
+            int xr = col;   // staged row of this thread's column
+            if constexpr (MOE) if (xres) xr = fdiv(seg_slot(sg, col), a.dv_topk);
+            xrow = xbuf_s + (uint32_t)((xb * a.xrows + xr) * a.xpitch) + x_lane_off<F>(t);
         }
         float acc[4] = {0.f, 0.f, 0.f, 0.f};
         int kc = 0;
         for (int c = 0; c < a.nchunks; ++c, kc += GS) {
-            if (!wait_parity(&full[stg], rnd & 1)) { ok = false; break; }
+            if (!cwait(&full[stg], rnd & 1)) { ok = false; break; }
             const uint32_t st = ring_s + (uint32_t)(stg * a.stage_bytes);
             const int G1 = min(G1w, KG - kc);
             consume_stage<F>(st + c_row, cp, st + s_row, sp, G0, G1, xrow + (uint32_t)(kc * 64), t, acc);
@@ -616,16 +753,16 @@ qmv_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUten
         }
         if (!ok) break;
         // reduction over the group's warps (double-buffered, bounded mbarrier handshakes); the reducer rotates
-        const int tp = ntile & 1, use = ntile >> 1, reducer = ntile % WPG;
+        const int tp = ntile & 1, use = ntile >> 1, reducer = ntile & (WPG - 1);
         uint64_t* rfull = &redfull[grp * 2 + tp];
         uint64_t* rfree = &redfree[grp * 2 + tp];
         float4* rb = red + ((grp * 2 + tp) * WPG) * 32;
-        if (use > 0 && !wait_parity(rfree, (use - 1) & 1)) { ok = false; break; }
+        if (use > 0 && !cwait(rfree, (use - 1) & 1)) { ok = false; break; }
         rb[wi * 32 + lane] = make_float4(acc[0], acc[1], acc[2], acc[3]);
         __syncwarp();
         if (lane == 0) mbar_arrive(rfull);
         if (wi == reducer) {
-            if (!wait_parity(rfull, use & 1)) { ok = false; break; }
+            if (!cwait(rfull, use & 1)) { ok = false; break; }
             float4 r = rb[lane];
             for (int v = 1; v < WPG; ++v) {
                 const float4 q = rb[v * 32 + lane];
@@ -685,8 +822,10 @@ qmv_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUten
         while (stg >= a.nstage) { stg -= a.nstage; ++rnd; }
     }
     // release the rest of the CTA's segments (also those this group had no tile in)
-    if (ok) ok = enter_upto(last_seg - first_seg);
-    leave();
+    if (!xres) {
+        if (ok) ok = enter_upto(last_seg - first_seg);
+        leave();
+    }
     if constexpr (MODE == QMV_MOE_P2P) qmv_moe_push<OutT>(a, tb, w0, w1, ok, cta_state);
 }
 

@@ -178,7 +178,7 @@ static int round_up(int v, int m) { return (v + m - 1) / m * m; }
 // glu: gate/up tile pairs over a [2N][K] table (N output rows, 2 ceil(N / 16) tiles, the gate hand-over slots after
 // the reduction region).
 static bool plan_qmv(int fmt, int N, int K, int xrows, int moe_slots, int E_local, const DeviceInfo& d, QmvPlan* p,
-                     bool glu = false) {
+                     bool glu = false, bool xres = false) {
     const int bits = fmt_bits(fmt), unit = QMV_KS_UNIT;
     static const int ks_force = getenv("VKB_QMV_KSMAX") ? atoi(getenv("VKB_QMV_KSMAX")) : 0;   // tuning override
     const int ks_max = ks_force >= unit ? ks_force : 12288 / bits;   // 1.5 KB of codes per row per stage (the
@@ -189,10 +189,10 @@ static bool plan_qmv(int fmt, int N, int K, int xrows, int moe_slots, int E_loca
     const int spitch = KS / 16 + ((KS / 256) % 2 == 0 ? 16 : 32);   // pitch / 4 = 4 x odd: conflict-free rows
     const int stage_bytes = round_up(QMV_ROWS * (cpitch + spitch), 128);
     const int xpitch = round_up(K * 2, 128) + 64;
-    const int xbufs = moe_slots > 0 ? 2 : 1;
+    const int xbufs = moe_slots > 0 && !xres ? 2 : 1;   // MoE over more than 8 tokens: per-segment rows, double-buffered
     const int xbytes = round_up(xbufs * xrows * xpitch, 16);
     const int redbytes = 2 * QMV_NW * 32 * 16 + (glu ? 2 * 32 * 16 : 0);
-    const int moebytes = moe_slots > 0 ? round_up(4 * (3 * E_local + 2 + 2 * moe_slots), 16) : 0;
+    const int moebytes = moe_slots > 0 ? round_up(4 * moe_table_words(E_local, moe_slots), 16) : 0;
     const int slack = 1024;
     auto fixed_for = [&](int nstage) { return 8 * qmv_nbars(nstage) + xbytes + redbytes + moebytes + slack; };
     const int pair_budget = d.smem_per_sm / 2 - 1024;   // two CTAs per SM
@@ -209,7 +209,10 @@ static bool plan_qmv(int fmt, int N, int K, int xrows, int moe_slots, int E_loca
     QmvArgs& a = p->a;
     a.N = N; a.K = K; a.KS = KS; a.nchunks = nchunks; a.nstage = nstage; a.stage_bytes = stage_bytes;
     a.cpitch = cpitch; a.spitch = spitch;
-    a.xpitch = xpitch; a.xrows = xrows; a.tilesN = (glu ? 2 : 1) * ((N + QMV_ROWS - 1) / QMV_ROWS);
+    a.xpitch = xpitch; a.xrows = xrows; a.xres = xres ? 1 : 0;
+    a.tilesN = (glu ? 2 : 1) * ((N + QMV_ROWS - 1) / QMV_ROWS);
+    a.dv_tiles = make_fastdiv((uint32_t)a.tilesN);
+    a.dv_topk = make_fastdiv(1);
     a.ring_off = 0;
     a.x_off = nstage * stage_bytes;
     a.red_off = a.x_off + xbytes;
@@ -256,7 +259,9 @@ static int launch_qmv(const QmvPlan& p, const CUtensorMap& tq, const CUtensorMap
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl_enabled() && pdl_stream_ok(st) ? 1 : 0;
-    const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, tq, ts, p.a);
+    QmvArgs a = p.a;
+    a.dv_grid = make_fastdiv((uint32_t)grid);
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, tq, ts, a);
     return e == cudaSuccess ? 0 : -(int)e;
 }
 
@@ -319,8 +324,11 @@ static int qmv_entry(const void* q, const void* s, const void* x, void* y, bool 
 
     const bool fast = K % 256 == 0 && aligned16(q) && aligned16(s) && aligned16(x);
     QmvPlan p{};
-    const int xrows = moe ? (slots < QMV_MAXTOK ? slots : QMV_MAXTOK) : M;
-    if (fast && plan_qmv(F, N, K, xrows, slots, E_local, d, &p)) {
+    // MoE over at most 8 tokens: every token row stays resident (columns index it by slot / topk); more tokens: the
+    // rows of each expert segment (at most 8 slots) are staged in turn
+    const bool xres = moe && M <= QMV_MAXTOK;
+    const int xrows = moe && !xres ? (slots < QMV_MAXTOK ? slots : QMV_MAXTOK) : M;
+    if (fast && plan_qmv(F, N, K, xrows, slots, E_local, d, &p, false, xres)) {
         constexpr int BITS = FmtTraits<F>::BITS;
         CUtensorMap tq, ts;
         int r = get_tmap_2d(&tq, q, (uint64_t)rows, (uint64_t)K * BITS / 8, CU_TENSOR_MAP_DATA_TYPE_UINT64, 8,
@@ -334,13 +342,28 @@ static int qmv_entry(const void* q, const void* s, const void* x, void* y, bool 
         p.a.idx = idx;
         p.a.T = M;
         p.a.topk = topk;
+        if (moe) p.a.dv_topk = make_fastdiv((uint32_t)topk);
         p.a.E_local = E_local;
         p.a.e0 = e0;
         p.a.zero_foreign = zero_foreign;
         if (p2p) p.a.pp = *p2p;
         int grid;
         if (moe) {
-            grid = d.sm_count;
+            // The tile count is known only in the kernel; the host bounds it: segments <= n + (slots - n) / 8 with
+            // n = min(E_local, slots) (each routed expert has ceil(c / 8) <= 1 + (c - 1) / 8 of them). One CTA per
+            // SM, or two when two fit (the two-CTA footprint) and a CTA can get 8 or more tiles: twice the stages
+            // in flight per SM (measured on B200: the 2048x512 down set at 8 tokens 20.1 us against 23.4, at 64 tokens
+            // 51 against 65), while calls of a few tiles per CTA pay for the second CTA's prologue (8 experts of
+            // 512x2048 at one token: 6.6 us against 5.4). Peer-store calls keep one per SM (one flag pair per CTA).
+            const long long n = E_local < slots ? E_local : slots;
+            const long long tiles = (n + (slots - n) / QMV_MAXTOK) * p.a.tilesN;
+            static const int per_sm_force = getenv("VKB_MOE_CTAS_PER_SM") ? atoi(getenv("VKB_MOE_CTAS_PER_SM")) : 0;
+            const bool fits2 = 2 * (p.smem + 1024) <= d.smem_per_sm && !p2p;   // (1 KB reserved per CTA)
+            const bool two = per_sm_force ? (per_sm_force == 2 && fits2) : (fits2 && tiles >= 8ll * d.sm_count);
+            grid = d.sm_count * (two ? 2 : 1);   // (VKB_MOE_CTAS_PER_SM: tuning override)
+            // warp groups: no more than the most tiles a CTA can get
+            const long long most = (tiles + grid - 1) / grid;
+            while (p.a.wg > 1 && p.a.wg > most) p.a.wg /= 2;
         } else {
             grid = p.a.tilesN < d.sm_count ? p.a.tilesN : d.sm_count;
         }
