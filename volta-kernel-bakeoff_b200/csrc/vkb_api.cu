@@ -238,10 +238,10 @@ static bool plan_qmv(int fmt, int N, int K, int xrows, int moe_slots, int E_loca
     return true;
 }
 
-template <int F, int MODE, typename OutT, bool XF32 = false>
+template <int F, int MODE, typename OutT, bool XF32 = false, int MINB = 2>
 static int launch_qmv(const QmvPlan& p, const CUtensorMap& tq, const CUtensorMap& ts, int grid, cudaStream_t st,
                       int dev) {
-    auto kern = qmv_kernel<F, MODE, OutT, XF32>;
+    auto kern = qmv_kernel<F, MODE, OutT, XF32, MINB>;
     static std::once_flag once[kMaxDevices];
     static cudaError_t attr_err[kMaxDevices];
     std::call_once(once[dev], [&] {
@@ -368,11 +368,16 @@ static int qmv_entry(const void* q, const void* s, const void* x, void* y, bool 
             grid = p.a.tilesN < d.sm_count ? p.a.tilesN : d.sm_count;
         }
         if (p2p && grid > P2P_MAX_CTAS) return VKB_EUNSUPPORTED;   // one flag pair per CTA
-        if (moe)
-            return p2p ? (f32 ? launch_qmv<F, QMV_MOE_P2P, float>(p, tq, ts, grid, st, dev)
-                              : launch_qmv<F, QMV_MOE_P2P, __half>(p, tq, ts, grid, st, dev))
-                       : (f32 ? launch_qmv<F, QMV_MOE, float>(p, tq, ts, grid, st, dev)
-                              : launch_qmv<F, QMV_MOE, __half>(p, tq, ts, grid, st, dev));
+        if (moe) {
+            if (p2p)   // one CTA per SM
+                return f32 ? launch_qmv<F, QMV_MOE_P2P, float, false, 1>(p, tq, ts, grid, st, dev)
+                           : launch_qmv<F, QMV_MOE_P2P, __half, false, 1>(p, tq, ts, grid, st, dev);
+            if (grid > d.sm_count)
+                return f32 ? launch_qmv<F, QMV_MOE, float>(p, tq, ts, grid, st, dev)
+                           : launch_qmv<F, QMV_MOE, __half>(p, tq, ts, grid, st, dev);
+            return f32 ? launch_qmv<F, QMV_MOE, float, false, 1>(p, tq, ts, grid, st, dev)
+                       : launch_qmv<F, QMV_MOE, __half, false, 1>(p, tq, ts, grid, st, dev);
+        }
         return f32 ? launch_qmv<F, QMV_DENSE, float>(p, tq, ts, grid, st, dev)
                    : launch_qmv<F, QMV_DENSE, __half>(p, tq, ts, grid, st, dev);
     }
