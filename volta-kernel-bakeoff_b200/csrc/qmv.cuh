@@ -196,7 +196,8 @@ __device__ __forceinline__ void qmv_group(uint32_t ca, uint32_t cp, int G, int t
 //   ca, cp: shared address of row g's codes in the stage, code row pitch
 //   sc, sp: shared address of row g's scales in the stage, scale row pitch
 //   xa:     shared address of this thread's activations for stage-local group 0
-template <int F>
+// U: groups per loop iteration (2, or 4 where the register budget allows: four independent MMA chains in flight).
+template <int F, int U = 2>
 __device__ __forceinline__ void consume_stage(uint32_t ca, uint32_t cp, uint32_t sc, uint32_t sp, int G0, int G1,
                                               uint32_t xa, int t, float (&acc)[4]) {
     int G = G0;
@@ -206,6 +207,17 @@ __device__ __forceinline__ void consume_stage(uint32_t ca, uint32_t cp, uint32_t
             qmv_group<F>(ca, cp, G, t, xa + 64 * G, half_hi_f32(p0), half_hi_f32(p1), acc);
         }
         ++G;
+    }
+    if constexpr (U == 4) {
+#pragma unroll 1
+        for (; G + 3 < G1; G += 4) {
+            const uint32_t p0 = lds32(sc + 2 * G), p1 = lds32(sc + 8 * sp + 2 * G);
+            const uint32_t q0 = lds32(sc + 2 * G + 4), q1 = lds32(sc + 8 * sp + 2 * G + 4);
+            qmv_group<F>(ca, cp, G, t, xa + 64 * G, half_lo_f32(p0), half_lo_f32(p1), acc);
+            qmv_group<F>(ca, cp, G + 1, t, xa + 64 * (G + 1), half_hi_f32(p0), half_hi_f32(p1), acc);
+            qmv_group<F>(ca, cp, G + 2, t, xa + 64 * (G + 2), half_lo_f32(q0), half_lo_f32(q1), acc);
+            qmv_group<F>(ca, cp, G + 3, t, xa + 64 * (G + 3), half_hi_f32(q0), half_hi_f32(q1), acc);
+        }
     }
 #pragma unroll 1
     for (; G + 1 < G1; G += 2) {
@@ -752,7 +764,8 @@ qmv_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUten
             if (!cwait(&full[stg], rnd & 1)) { ok = false; break; }
             const uint32_t st = ring_s + (uint32_t)(stg * a.stage_bytes);
             const int G1 = min(G1w, KG - kc);
-            consume_stage<F>(st + c_row, cp, st + s_row, sp, G0, G1, xrow + (uint32_t)(kc * 64), t, acc);
+            consume_stage<F, MINB == 1 ? 4 : 2>(st + c_row, cp, st + s_row, sp, G0, G1, xrow + (uint32_t)(kc * 64), t,
+                                                acc);
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[stg]);
             if (++stg == a.nstage) { stg = 0; ++rnd; }

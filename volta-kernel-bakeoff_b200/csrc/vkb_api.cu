@@ -351,15 +351,16 @@ static int qmv_entry(const void* q, const void* s, const void* x, void* y, bool 
         if (moe) {
             // The tile count is known only in the kernel; the host bounds it: segments <= n + (slots - n) / 8 with
             // n = min(E_local, slots) (each routed expert has ceil(c / 8) <= 1 + (c - 1) / 8 of them). One CTA per
-            // SM, or two when two fit (the two-CTA footprint) and a CTA can get 8 or more tiles: twice the stages
-            // in flight per SM (measured on B200: the 2048x512 down set at 8 tokens 20.1 us against 23.4, at 64 tokens
-            // 51 against 65), while calls of a few tiles per CTA pay for the second CTA's prologue (8 experts of
-            // 512x2048 at one token: 6.6 us against 5.4). Peer-store calls keep one per SM (one flag pair per CTA).
+            // SM, or two when two fit (the two-CTA footprint) and a CTA can get 4 or more tiles: twice the stages
+            // in flight per SM (measured on B200, the 2048x512 down set: 1 token 5.3 us against 5.8, 8 tokens 18.1
+            // against 23.4, 64 tokens 50 against 65), while calls of one or two tiles per CTA pay for the second
+            // CTA's prologue (8 experts of 512x2048 at one token: 4.9 us against 4.4). Peer-store calls keep one per
+            // SM (one flag pair per CTA).
             const long long n = E_local < slots ? E_local : slots;
             const long long tiles = (n + (slots - n) / QMV_MAXTOK) * p.a.tilesN;
             static const int per_sm_force = getenv("VKB_MOE_CTAS_PER_SM") ? atoi(getenv("VKB_MOE_CTAS_PER_SM")) : 0;
             const bool fits2 = 2 * (p.smem + 1024) <= d.smem_per_sm && !p2p;   // (1 KB reserved per CTA)
-            const bool two = per_sm_force ? (per_sm_force == 2 && fits2) : (fits2 && tiles >= 8ll * d.sm_count);
+            const bool two = per_sm_force ? (per_sm_force == 2 && fits2) : (fits2 && tiles >= 4ll * d.sm_count);
             grid = d.sm_count * (two ? 2 : 1);   // (VKB_MOE_CTAS_PER_SM: tuning override)
             // warp groups: no more than the most tiles a CTA can get
             const long long most = (tiles + grid - 1) / grid;
