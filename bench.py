@@ -247,6 +247,7 @@ def bench_config():
 # ---- extra sections: prompt GEMM, MoE, sharded paths -------------------------------------------------------------
 
 PROMPT_SHAPES = [(12288, 2560), (8192, 2048)]          # configs[4]
+PROMPT_TABLES = PROMPT_SHAPES + [(2560, 6144), (2048, 6144)]   # + configs[1]'s tables with few row tiles
 PROMPT_TOKENS = [64, 512]
 MOE_CASES = [  # configs[2] and configs[3]: (name, experts, top-k, N, K, token counts)
     ("qwen36_gate_up_128x512x2048_top8", 128, 8, 512, 2048, [1, 8, 64]),
@@ -302,9 +303,10 @@ def _copies(nbytes: int, L2: int) -> int:
 def prompt_section(torch, vkb, dev, stream, L2, peaks):
     """configs[4] on one GPU: the tcgen05 prompt GEMM against cuBLAS bf16 (torch.matmul, bf16 in and out) at the same
     shapes, weights cycled over >= 4x L2 for both; the same shapes with Q8 weights (the Q8 prompt kernel the reference
-    planned but never built) as q8_* entries."""
+    planned but never built) as q8_* entries; also the small-N / large-K tables, which the planner runs as split-K
+    clusters."""
     out = {}
-    for N, K in PROMPT_SHAPES:
+    for N, K in PROMPT_TABLES:
         sets = {}
         for fmt in (0, 1):
             codes, scales = vkb.quantize(fmt, vkb.synth_normal(0, (N, K), 0.02))

@@ -229,7 +229,10 @@ int vkb_version(void);
  *   kind 1, prompt GEMM (fmt Q4 / Q8, any M), one CTA per tile:
  *     info = {smem, tokens per tile NT, 128-row blocks per tile, TMEM accumulators, A slots, first A column, TMEM
  *             columns, X stages, K steps per X stage, P chunks, K steps per P chunk, grid, tiles, X stage bytes,
- *             row tiles, CTAs per tile} */
+ *             row tiles, CTAs per tile}
+ *   kind 3, prompt GEMM as the entry points plan it, split-K included (Q4 tables with few row tiles: a cluster of
+ *     CTAs shares each tile's K range; the cluster-occupancy limit is taken as sm_count / CTAs per cluster):
+ *     the info of kind 1 with the last field = CTAs sharing a tile's K range (1: no split) */
 #define VKB_PLAN_INFO_LEN 16
 int vkb_plan_describe(int kind, int fmt, int N, int K, int M, int sm_count, int smem_optin, int smem_per_sm,
                       int* info);

@@ -112,13 +112,16 @@ print("WORST", worst, "STATUS", vkb.device_status())
 
 @pytest.mark.parametrize("env", [{"VKB_TC_CG": "2"}, {"VKB_TC_RB": "2"}, {"VKB_TC_RB": "2", "VKB_TC_NT": "176"},
                                  {"VKB_TC_RB": "2", "VKB_TC_NT": "48"}, {"VKB_TC_RB": "1", "VKB_TC_NT": "176"},
-                                 {"VKB_TC_RB": "1", "VKB_TC_NT": "80"}],
-                         ids=["pair", "rb2", "rb2_nt176", "rb2_nt48", "rb1_nt176", "rb1_nt80"])
+                                 {"VKB_TC_RB": "1", "VKB_TC_NT": "80"}, {"VKB_TC_SPLIT": "2"},
+                                 {"VKB_TC_SPLIT": "3", "VKB_TC_NT": "80"}, {"VKB_TC_SPLIT": "1"}],
+                         ids=["pair", "rb2", "rb2_nt176", "rb2_nt48", "rb1_nt176", "rb1_nt80", "split2",
+                              "split3_nt80", "nosplit"])
 def test_tc_kernel_variants(cuda, env):
     """Every prompt-kernel variant the planner can pick, forced by its tuning overrides (read once per process, so in
-    a child process) against torch fp32: the CTA pair (tcgen05 cta_group::2), two 128-row blocks per CTA, and token
-    tiles that are multiples of 16 but not of 32 (one accumulator, two blocks, or two accumulators). A forced value
-    that does not fit a shape leaves that shape to the planner."""
+    a child process) against torch fp32: the CTA pair (tcgen05 cta_group::2), two 128-row blocks per CTA, token
+    tiles that are multiples of 16 but not of 32 (one accumulator, two blocks, or two accumulators), and split-K over
+    2 or 3 CTAs (even and uneven shares of the K units; 640x2560 has 5 units) or none. A forced value that does not
+    fit a shape leaves that shape to the planner."""
     import os
     import subprocess
     import sys
@@ -129,6 +132,33 @@ def test_tc_kernel_variants(cuda, env):
     assert r.returncode == 0, r.stderr[-2000:]
     line = [l for l in r.stdout.splitlines() if l.startswith("WORST")][-1].split()
     assert float(line[1]) < 1e-5 and int(line[3]) == 0, line
+
+
+@pytest.mark.parametrize("N,K,M", [(2560, 6144, 64), (2560, 6144, 512), (2048, 6144, 64), (2048, 6144, 512),
+                                   (1000, 6144, 77)])
+def test_tc_split_k_small_tables(cuda, N, K, M):
+    """The survey's small-N / large-K prompt tables (and a ragged one), which the planner runs as split-K clusters
+    (each tile's K range shared by several CTAs, partials summed in rank order over distributed shared memory):
+    against torch fp32 over the same fp16 weights (tight), the oracle with the reference's tc tolerance and fp16-output
+    bound, and two calls bit-identical (the reduction order is fixed)."""
+    import torch
+    p = vkb.plan(vkb.PLAN_TC_SPLIT, O.FMT_Q4, N, K, M)
+    assert p["splits"] > 1 and p["grid"] == p["tiles"] * p["splits"] <= vkb.B200_LIMITS["sm_count"], p
+    rng = np.random.default_rng(N + M)
+    codes, scales = random_codes(rng, O.FMT_Q4, N, K)
+    q, s = device_weights(O.FMT_Q4, codes, scales)
+    x = uniform_x(rng, M, K)
+    y = _tc(q, s, x, M, out_f32=True)
+    ref = _torch_ref(codes, scales, x)
+    err = ((y - ref).abs().max() / (ref.abs().max() + 1e-12)).item()
+    assert err < 1e-5, err
+    y2 = _tc(q, s, x, M, out_f32=True)
+    assert torch.equal(y, y2)
+    yh = _tc(q, s, x, M, out_f32=False).float().cpu().numpy().astype(np.float64)
+    ref64, mag = O.ref_value(codes, scales, x), O.ref_scale(codes, scales, x)
+    e, m, n = O.check_error(yh, ref64, mag)
+    assert e <= O.TOL_FP16, (e, m, n)
+    assert vkb.device_status() == 0
 
 
 @pytest.mark.parametrize("N,K,M", [(512, 256, 16), (1031, 768, 65), (2048, 2048, 511), (12288, 2560, 512),

@@ -73,6 +73,7 @@ struct TcArgs {
     int ldy, ycol0;     // output row stride and first column (row split: the full y, this rank's columns)
     int p2p;            // 1: push every tile into every peer's copy of y (pp.peer_base), epoch protocol (P2P kernels)
     P2PArgs pp;
+    int splits, kunit;  // split-K kernels: CTAs sharing a tile's K range (a cluster), K steps per unit of that range
 };
 
 // ---- tcgen05 wrappers ----------------------------------------------------------------------------------------------
@@ -295,6 +296,33 @@ __device__ __forceinline__ void tc_epi_store(const TcArgs& a, uint32_t tq_addr, 
     }
 }
 
+// Split-K: one warp's share of a finished partial accumulator into this CTA's shared memory as fp32 [token][128 rows]
+// at `part` (shared address): the TMEM chunks of tc_epi_store; each store covers 32 consecutive rows of one token.
+__device__ __forceinline__ void tc_epi_stash(const TcArgs& a, uint32_t tq_addr, int rloc, int tok0, int sub, int parts,
+                                             uint32_t part) {
+    const int ntok = min(a.NT, a.M - tok0);
+    uint32_t v[32];
+    for (int c = 32 * sub; c < ntok; c += 32 * parts) {
+        tmem_ld32(tq_addr + (uint32_t)c, v);
+        const int lim = ntok - c;
+        const uint32_t p0 = part + (uint32_t)((c * TC_BM + rloc) * 4);
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+            if (j < lim)
+                asm volatile("st.shared.b32 [%0], %1;" ::"r"(p0 + (uint32_t)(j * TC_BM * 4)), "r"(v[j]) : "memory");
+    }
+}
+
+// Four fp32 values from the shared memory of a CTA of the cluster (address from mapa_shared).
+__device__ __forceinline__ float4 ld_cluster_f4(uint32_t addr) {
+    float4 v;
+    asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+                 : "r"(addr)
+                 : "memory");
+    return v;
+}
+
 // Push the finished tile (weight rows row0.., tokens tok0..) from this rank's y to every peer; thread t of nth.
 // Out of line, so that the epilogue's register allocation does not carry it.
 template <typename OutT>
@@ -314,6 +342,12 @@ __device__ __noinline__ void tc_push_tile(const TcArgs& a, int row0, int tok0, i
 // complete on the leader's barrier); the leader's commits arrive on both CTAs' barriers. No TMA multicast.
 // WF: weight format, 0 = Q4 (the reference's tc_q4), 1 = Q8 (the tc_q8 it planned but never built): only the packed
 // chunk layout and the dequantisation differ.
+// SPLIT: split-K for tables with few row tiles (2560x6144 has 20): a cluster of a.splits CTAs shares one tile, CTA r
+// taking its share of the K range (units of a.kunit K steps) through the unchanged pipeline. Each CTA stores its fp32
+// partial accumulator in its own shared memory (the rings are idle by then), the cluster synchronises, and CTA r sums
+// token slice r over the cluster's partials in rank order (distributed shared memory reads), so the result does not
+// depend on timing: deterministic, unlike an atomic reduction. A second cluster barrier keeps every partial readable
+// until all slices are done. One tile per cluster (the planner launches tiles x splits CTAs).
 // RB = 2 (opt-in, VKB_TC_RB=2): one CTA holds a 256-row tile as two 128-row blocks, each with its own accumulator
 // (TMEM columns 0 and NT rounded up to 32), and every activation K step feeds the MMAs of both blocks: the activations
 // are streamed from L2 once per 256 weight rows instead of once per 128 (that stream, N / 128 times the activations,
@@ -321,13 +355,14 @@ __device__ __noinline__ void tc_push_tile(const TcArgs& a, int row0, int tok0, i
 // compiled out). A slots hold one K step of both blocks (64 columns); dequantising group g (four warps) converts block
 // g. Measured slower than one block at every shape (the MMA issue loop and the 2-slot A ring bound it first), so the
 // planner never picks it.
-template <typename OutT, int PK, bool P2P, int CG, int WF = 0, int RB = 1>
+template <typename OutT, int PK, bool P2P, int CG, int WF = 0, int RB = 1, bool SPLIT = false>
 __global__ void __launch_bounds__(TC_THREADS, 1)
 tc_q4_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap ts,
              const __grid_constant__ CUtensorMap tx, const __grid_constant__ TcArgs a) {
     static_assert(CG == 1 || (CG == 2 && !P2P), "peer stores use the one-CTA kernel");
     static_assert(WF == 0 || (WF == 1 && !P2P && CG == 1), "Q8 weights: the one-CTA kernel without peer stores");
     static_assert(RB == 1 || (RB == 2 && CG == 1 && !P2P && WF == 0), "two row blocks: the one-CTA Q4 kernel");
+    static_assert(!SPLIT || (CG == 1 && !P2P && RB == 1), "split-K: one-CTA tiles, no peer stores, one row block");
     constexpr int BMR = TC_BM * RB;                         // weight rows of a CTA's tile
     constexpr int SK = RB == 1 ? TC_SLOT : 1;               // K steps per A slot
     constexpr int SLOT_COLS = RB * SK * TC_ACOLS;           // TMEM columns per A slot (128, or 64 with two blocks)
@@ -348,13 +383,22 @@ tc_q4_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUt
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accempty + a.nacc);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int nk = a.nk, nch = nk / PK, nxs = nk / a.xk, nslots = nk / SK;
+    // this CTA's K steps [kofs, kofs + nk) of every tile (split-K: its rank's share of the units)
+    int kofs = 0, nk = a.nk;
+    uint32_t srank = 0;
+    if constexpr (SPLIT) {
+        srank = cluster_ctarank();
+        const int nun = a.nk / a.kunit, lo = (int)srank * nun / a.splits, hi = ((int)srank + 1) * nun / a.splits;
+        kofs = lo * a.kunit;
+        nk = (hi - lo) * a.kunit;
+    }
+    const int nch = nk / PK, nxs = nk / a.xk, nslots = nk / SK;
     const int rbcol = (a.NT + 31) & ~31;   // TMEM columns between the row blocks' accumulators (32-aligned)
     // the CTA's place in its pair (CG = 2) and the pairs of the grid; a "unit" is a CTA (CG = 1) or a pair
     const uint32_t crank = CG == 2 ? cluster_ctarank() : 0u;
     const bool leader = crank == 0;
-    const int units = CG == 2 ? (int)cluster_count_x() : (int)gridDim.x;
-    const int unit = CG == 2 ? (int)cluster_id_x() : (int)blockIdx.x;
+    const int units = CG == 2 || SPLIT ? (int)cluster_count_x() : (int)gridDim.x;
+    const int unit = CG == 2 || SPLIT ? (int)cluster_id_x() : (int)blockIdx.x;
     // tiles of this unit: t = unit + i * units (a tile: 128 RB CG weight rows x NT tokens; this CTA's rows start at
     // row0_of(t), its tokens for the B operand at tok0_of(t) + crank NT / CG)
     const int ntl = unit < a.tiles ? (a.tiles - 1 - unit) / units + 1 : 0;
@@ -381,8 +425,8 @@ tc_q4_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUt
         const int t = tile_of(g / nch), c = g % nch;
         uint8_t* dst = sm + a.p_off + b * PCHUNK;
         mbar_arrive_expect_tx(&pfull[b], (uint32_t)PCHUNK);
-        tma_load_2d(dst, &tq, c * PK * (KSB / 8), row0_of(t), &pfull[b]);        // PK K steps of codes, 8-B units
-        tma_load_2d(dst + SCOFF, &ts, c * PK * 2, row0_of(t), &pfull[b]);         // 2 PK (+ pad) fp16 scales
+        tma_load_2d(dst, &tq, (kofs + c * PK) * (KSB / 8), row0_of(t), &pfull[b]);   // PK K steps of codes, 8-B units
+        tma_load_2d(dst + SCOFF, &ts, (kofs + c * PK) * 2, row0_of(t), &pfull[b]);    // 2 PK (+ pad) fp16 scales
     };
 
     // peer stores: some thread of this CTA gave up a wait (its part of the call is missing); the word after the TMEM
@@ -453,7 +497,10 @@ tc_q4_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUt
 #pragma unroll
             for (int rb = 0; rb < RB; ++rb) {   // row block rb: accumulator columns from rb rbcol, rows from 128 rb
                 const uint32_t tq_addr = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(acc * 128 + rb * rbcol);
-                tc_epi_store<OutT>(a, tq_addr, row0 + rb * TC_BM + 32 * q + lane, tok0, sub, parts);
+                if constexpr (SPLIT)
+                    tc_epi_stash(a, tq_addr, 32 * q + lane, tok0, sub, parts, smem_u32(sm));
+                else
+                    tc_epi_store<OutT>(a, tq_addr, row0 + rb * TC_BM + 32 * q + lane, tok0, sub, parts);
             }
             // every TMEM read of this accumulator has completed: the MMA warp may overwrite it
             if (arrive) {
@@ -497,7 +544,7 @@ tc_q4_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUt
                 const int t = tile_of(gs / nxs), xs = gs % nxs;
                 if constexpr (CG == 1) {
                     mbar_arrive_expect_tx(&xfull[b], (uint32_t)a.x_stage);
-                    tma_load_3d(sm + a.x_off + b * a.x_stage, &tx, 0, tok0_of(t), xs * a.xk, &xfull[b]);
+                    tma_load_3d(sm + a.x_off + b * a.x_stage, &tx, 0, tok0_of(t), kofs + xs * a.xk, &xfull[b]);
                 } else {   // this CTA's half of the tokens; both halves complete on the leader's barrier
                     if (leader) mbar_arrive_expect_tx(&xfull[b], (uint32_t)(2 * a.x_stage));
                     tma_load_3d_cg2(sm + a.x_off + b * a.x_stage, &tx, 0, tok0_of(t) + (int)crank * (a.NT / 2),
@@ -748,6 +795,31 @@ tc_q4_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUt
         for (int i = 0; i < ntl && (ok || P2P); ++i) epi_tile(i, 0, i == ntl - 1 ? 3 : 1, true);
     } else if (warp >= TC_WDQ0 && ntl > 0 && (ok || P2P)) {   // the last tile
         epi_tile(ntl - 1, 1 + ((warp - TC_WDQ0) >> 2), 3, false);
+    }
+    // split-K: the cluster's partials -> y, CTA r summing token slice r over the ranks in order
+    if constexpr (SPLIT) {
+        cluster_sync();   // every CTA's partial is in its shared memory
+        pdl_wait();       // y may still be read or written by the previous grid
+        if (ntl > 0) {
+            const int t = tile_of(0), row0 = row0_of(t), tok0 = tok0_of(t), ntok = min(a.NT, a.M - tok0);
+            const int lo = (int)srank * ntok / a.splits, hi = ((int)srank + 1) * ntok / a.splits;
+            OutT* y = reinterpret_cast<OutT*>(a.y);
+            const int n = row0 + 4 * lane;
+            for (int tk = lo + warp; tk < hi; tk += TC_THREADS / 32) {
+                const uint32_t off = smem_u32(sm) + (uint32_t)((tk * TC_BM + 4 * lane) * 4);
+                float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+                for (int r = 0; r < a.splits; ++r) {
+                    const float4 v = ld_cluster_f4(mapa_shared(off, (uint32_t)r));
+                    acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
+                }
+                OutT* yp = y + (size_t)(tok0 + tk) * a.ldy + a.ycol0 + n;
+                if (n < a.N) yp[0] = tc_out<OutT>(acc.x);
+                if (n + 1 < a.N) yp[1] = tc_out<OutT>(acc.y);
+                if (n + 2 < a.N) yp[2] = tc_out<OutT>(acc.z);
+                if (n + 3 < a.N) yp[3] = tc_out<OutT>(acc.w);
+            }
+        }
+        cluster_sync();   // no CTA releases its shared memory while a peer still reads its partial
     }
     // teardown: every MMA has completed (the epilogue waited on each accumulator) before TMEM is released
     if (warp == 1 && !ok && ntl > 0) wait_b(&accfull[(ntl - 1) % a.nacc], ((ntl - 1) / a.nacc) & 1,

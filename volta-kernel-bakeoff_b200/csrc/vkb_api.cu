@@ -497,17 +497,29 @@ struct TcPlan {
 // up to 32 KB (an even count: two producers), P chunks of 8 K steps when they fit (else 4; 4 with two blocks), both
 // deepened while shared memory lasts. With cg = 2 the units are CTA pairs (at most `units_max` co-resident), a tile
 // has 256 rows and each CTA's X stages hold half of the tile's tokens.
+//
+// Split-K (split_max > 1: Q4, one-CTA tiles, no peer stores): with few tiles the MMAs of one tile's K range are the
+// whole call (2560x6144 at 512 tokens: 40 tiles on 148 SMs), so S CTAs of a cluster share a tile, each taking units
+// of TC_KUNIT K steps, at one tile per cluster (tiles x S <= SMs, and <= the clusters of S that fit at once:
+// clusters_max[S], or SMs / S when null). Cost: the longest share's K steps, plus the partial exchange (shared
+// memory stores of the accumulator, two cluster barriers, distributed shared-memory reads of ntok / S tokens of
+// every rank: ~2000 + 12 NT cycles).
+constexpr int TC_KUNIT = 8;
 static bool plan_tc(int N, int K, int M, int out_bytes, const DeviceInfo& d, TcPlan* p, int cg, int units_max,
-                    int wf = 0, bool allow_rb2 = false) {
+                    int wf = 0, bool allow_rb2 = false, int split_max = 1, const int* clusters_max = nullptr) {
     TcArgs& a = p->a;
     const int nk = K / TC_BK;
-    int NT = 0, RB = 1;
+    int NT = 0, RB = 1, SPL = 1;
     double best = 1e300;
+    static const int split_env = getenv("VKB_TC_SPLIT") ? atoi(getenv("VKB_TC_SPLIT")) : 0;   // tuning override
+    if (cg != 1 || wf != 0 || nk % TC_KUNIT != 0 || split_env == 1) split_max = 1;   // (VKB_TC_SPLIT=1: none)
+    int split_force = split_max > 1 ? split_env : 0;
     const int nt_max = round_up(M, 32) < 256 ? round_up(M, 32) : 256;
     static const int nt_force = getenv("VKB_TC_NT") ? atoi(getenv("VKB_TC_NT")) : 0;   // tuning overrides
     static const int rb_force = getenv("VKB_TC_RB") ? atoi(getenv("VKB_TC_RB")) : 0;
     const int rb = rb_force == 2 && allow_rb2 && cg == 1 && wf == 0 ? 2 : 1;
-    for (int pass = 0; pass < 2 && NT == 0; ++pass) {   // pass 1: without the NT override (it does not fit)
+    for (int pass = 0; pass < 3 && NT == 0; ++pass) {   // pass 1: without the NT override (it does not fit); pass 2:
+        if (pass == 2) split_force = 0;                  // without the split override either
         // steps of 16 above 128 tokens (512 = 3 x 176 wastes 3 % of the MMAs, 3 x 192 11 %; measured 1 % faster),
         // of 32 below (48-token tiles were slower than 64 at 6144x2048 x 128 tokens: more passes over the weights)
         for (int nt = nt_max; nt >= 32; nt -= ((pass == 0 && nt_force > 0) || nt > 128) && cg == 1 ? 16 : 32) {
@@ -520,7 +532,16 @@ static bool plan_tc(int N, int K, int M, int out_bytes, const DeviceInfo& d, TcP
             const double step = umma > 180.0 * rb ? umma : 180.0 * rb;
             const double epi = nt <= 128 && rb == 1 ? 0.0 : 1500.0 + 10.0 * nt * rb;
             const double t = (double)per_cta * nk * step + (double)(per_cta - 1) * epi + 6000.0;
-            if (t < best * 0.999) { best = t; NT = nt; RB = rb; }
+            if (t < best * 0.999 && split_force <= 1) { best = t; NT = nt; RB = rb; SPL = 1; }
+            if (rb != 1) continue;
+            const int nun = nk / TC_KUNIT;
+            for (int sp = 2; sp <= split_max && sp <= 8 && sp <= nun; ++sp) {
+                if (split_force > 1 && sp != split_force) continue;
+                const long fit = clusters_max ? clusters_max[sp] : d.sm_count / sp;
+                if (tiles * sp > d.sm_count || tiles > fit) continue;
+                const double ts = (double)((nun + sp - 1) / sp) * TC_KUNIT * step + 6000.0 + 2000.0 + 12.0 * nt;
+                if (ts < best * 0.999) { best = ts; NT = nt; RB = 1; SPL = sp; }
+            }
         }
     }
     if (NT == 0) return false;
@@ -570,18 +591,25 @@ static bool plan_tc(int N, int K, int M, int out_bytes, const DeviceInfo& d, TcP
         p->smem = total();
         p->cg = cg;
         p->grid = dim3((unsigned)((a.tiles < units_max ? a.tiles : units_max) * cg));
+        a.splits = 1;
+        a.kunit = TC_KUNIT;
+        // split-K: the partial accumulator (fp32, 128 rows x NT tokens) goes where the rings were
+        if (SPL > 1 && TC_BM * NT * 4 <= a.bar_off) {
+            a.splits = SPL;
+            p->grid = dim3((unsigned)(a.tiles * SPL));
+        }
         return true;
     }
     return false;
 }
 
 // Opt one prompt-GEMM kernel variant into the device's shared memory, once per device.
-template <typename OutT, int PK, bool P2P, int CG, int WF = 0, int RB = 1>
+template <typename OutT, int PK, bool P2P, int CG, int WF = 0, int RB = 1, bool SPLIT = false>
 static int tc_attr(int dev, int smem_optin) {
     static std::once_flag once[kMaxDevices];
     static cudaError_t err[kMaxDevices];
     std::call_once(once[dev], [&] {
-        err[dev] = cudaFuncSetAttribute(tc_q4_kernel<OutT, PK, P2P, CG, WF, RB>,
+        err[dev] = cudaFuncSetAttribute(tc_q4_kernel<OutT, PK, P2P, CG, WF, RB, SPLIT>,
                                         cudaFuncAttributeMaxDynamicSharedMemorySize, smem_optin);
     });
     return err[dev] == cudaSuccess ? 0 : -(int)err[dev];
@@ -614,6 +642,35 @@ static int tc_max_pairs(int dev, int smem) {
     return pairs[dev];
 }
 
+// Co-resident clusters of S split-K CTAs at full shared memory, for S = 0..8 (0 where the query fails), once per
+// device.
+static const int* tc_split_clusters(int dev, int smem) {
+    static std::once_flag once[kMaxDevices];
+    static int n[kMaxDevices][9];
+    std::call_once(once[dev], [&] {
+        if (tc_attr<__half, 8, false, 1, 0, 1, true>(dev, smem) != 0) return;
+        for (int sp = 2; sp <= 8; ++sp) {
+            cudaLaunchConfig_t cfg{};
+            cfg.gridDim = dim3(sp * 256);
+            cfg.blockDim = dim3(TC_THREADS);
+            cfg.dynamicSmemBytes = (size_t)smem;
+            cudaLaunchAttribute attr[1];
+            attr[0].id = cudaLaunchAttributeClusterDimension;
+            attr[0].val.clusterDim.x = (unsigned)sp;
+            attr[0].val.clusterDim.y = 1;
+            attr[0].val.clusterDim.z = 1;
+            cfg.attrs = attr;
+            cfg.numAttrs = 1;
+            int c = 0;
+            if (cudaOccupancyMaxActiveClusters(&c, tc_q4_kernel<__half, 8, false, 1, 0, 1, true>, &cfg) == cudaSuccess)
+                n[dev][sp] = c;
+            else
+                cudaGetLastError();
+        }
+    });
+    return n[dev];
+}
+
 template <typename OutT>
 static int tc_entry(const void* q, const void* s, const void* x, void* y, int N, int K, int M, cudaStream_t st,
                     const TcOut* out = nullptr, int wf = 0) {
@@ -639,7 +696,10 @@ static int tc_entry(const void* q, const void* s, const void* x, void* y, int N,
     }
     TcPlan p{};
     const bool p2p = out && out->p2p;
-    if (!plan_tc(N, K, M, (int)sizeof(OutT), d, &p, cg, units_max, wf, !p2p)) return VKB_EUNSUPPORTED;
+    const bool split_ok = !p2p && cg == 1 && wf == 0;
+    const int* clusters = split_ok ? tc_split_clusters(dev, d.smem_optin) : nullptr;
+    if (!plan_tc(N, K, M, (int)sizeof(OutT), d, &p, cg, units_max, wf, !p2p, split_ok ? 8 : 1, clusters))
+        return VKB_EUNSUPPORTED;
     p.a.y = y;
     p.a.ldy = out ? out->ldy : N;
     p.a.ycol0 = out ? out->col0 : 0;
@@ -665,6 +725,10 @@ static int tc_entry(const void* q, const void* s, const void* x, void* y, int N,
         } else {
             return VKB_EUNSUPPORTED;
         }
+    } else if (p.a.splits > 1) {   // split-K clusters (Q4, one CTA per tile share)
+        kern = p.pk == 8 ? tc_q4_kernel<OutT, 8, false, 1, 0, 1, true> : tc_q4_kernel<OutT, 4, false, 1, 0, 1, true>;
+        ra = p.pk == 8 ? tc_attr<OutT, 8, false, 1, 0, 1, true>(dev, d.smem_optin)
+                       : tc_attr<OutT, 4, false, 1, 0, 1, true>(dev, d.smem_optin);
     } else if (p.rb == 2) {   // 256-row tiles in one CTA (Q4, chunks of 4 K steps)
         kern = tc_q4_kernel<OutT, 4, false, 1, 0, 2>;
         ra = tc_attr<OutT, 4, false, 1, 0, 2>(dev, d.smem_optin);
@@ -692,9 +756,9 @@ static int tc_entry(const void* q, const void* s, const void* x, void* y, int N,
         attr[na].val.programmaticStreamSerializationAllowed = 1;
         ++na;
     }
-    if (p.cg == 2) {   // clusters of two CTAs along x: blocks 2c and 2c + 1 form pair c
+    if (p.cg == 2 || p.a.splits > 1) {   // clusters along x: blocks kc .. kc + k - 1 form cluster c
         attr[na].id = cudaLaunchAttributeClusterDimension;
-        attr[na].val.clusterDim.x = 2;
+        attr[na].val.clusterDim.x = p.cg == 2 ? 2u : (unsigned)p.a.splits;
         attr[na].val.clusterDim.y = 1;
         attr[na].val.clusterDim.z = 1;
         ++na;
@@ -866,14 +930,15 @@ int vkb_plan_describe(int kind, int fmt, int N, int K, int M, int sm_count, int 
         for (int i = 0; i < (int)(sizeof(v) / sizeof(v[0])); ++i) info[i] = v[i];
         return 0;
     }
-    if (kind == 1) {   // prompt GEMM, one CTA per tile (the planner's default kernel family)
+    if (kind == 1 || kind == 3) {   // prompt GEMM: one CTA per tile / with split-K where the planner picks it
         if (fmt != VKB_FMT_Q4 && fmt != VKB_FMT_Q8) return VKB_EINVAL;
         if (K < 256 || K % 256 != 0) return VKB_EUNSUPPORTED;
         TcPlan p{};
-        if (!plan_tc(N, K, M, 2, d, &p, 1, sm_count, fmt == VKB_FMT_Q8 ? 1 : 0, true)) return VKB_EUNSUPPORTED;
+        const int wf = fmt == VKB_FMT_Q8 ? 1 : 0;
+        if (!plan_tc(N, K, M, 2, d, &p, 1, sm_count, wf, true, kind == 3 ? 8 : 1)) return VKB_EUNSUPPORTED;
         const TcArgs& a = p.a;
         const int v[] = {p.smem, a.NT, p.rb, a.nacc, a.na, a.a_col0, a.tmem_cols, a.nx, a.xk, a.np, p.pk,
-                         (int)p.grid.x, a.tiles, a.x_stage, a.tiles_n, p.cg};
+                         (int)p.grid.x, a.tiles, a.x_stage, a.tiles_n, kind == 3 ? a.splits : p.cg};
         for (int i = 0; i < (int)(sizeof(v) / sizeof(v[0])); ++i) info[i] = v[i];
         return 0;
     }

@@ -129,12 +129,14 @@ def _register_optional(L) -> None:
 
 # B200: 148 SMs, 227 KB of shared memory per block (opt-in), 228 KB per SM
 B200_LIMITS = {"sm_count": 148, "smem_optin": 232448, "smem_per_sm": 233472}
-PLAN_GEMV, PLAN_TC, PLAN_GLU = 0, 1, 2
+PLAN_GEMV, PLAN_TC, PLAN_GLU, PLAN_TC_SPLIT = 0, 1, 2, 3
 _PLAN_FIELDS = {
     PLAN_GEMV: ("smem", "nstage", "nchunks", "KS", "wg", "stage_bytes", "grid", "cpitch", "spitch", "tiles"),
     PLAN_GLU: ("smem", "nstage", "nchunks", "KS", "wg", "stage_bytes", "grid", "cpitch", "spitch", "tiles"),
     PLAN_TC: ("smem", "NT", "rb", "nacc", "na", "a_col0", "tmem_cols", "nx", "xk", "np", "pk", "grid", "tiles",
               "x_stage", "tiles_n", "cg"),
+    PLAN_TC_SPLIT: ("smem", "NT", "rb", "nacc", "na", "a_col0", "tmem_cols", "nx", "xk", "np", "pk", "grid", "tiles",
+                    "x_stage", "tiles_n", "splits"),
 }
 
 
