@@ -77,7 +77,11 @@ def _rank_main(rank, world, port, q):
                 err = O.check_error(y_rs.float().cpu().numpy().astype(np.float64), ref, mag)[0]
                 out.append((f"rowsplit N{N} K{K} M{M} f32={f32}", same, err, O.TOL_FP16))
         # ---- row split with the all-gather fused into the epilogue (peer stores into a symmetric buffer) ----
-        for (N, K, M) in [(1024, 2048, 64), (2048, 2560, 512), (512, 768, 65)]:
+        # (40960, 256, 64), (38912, 512, 512): more tiles per rank than CTAs (two accumulators / one), so CTAs push
+        # earlier tiles while the dequantising warps join the last tile's epilogue; (1024, 2048, 64), (2048, 6144, 512):
+        # the one-GPU plan is split-K, which every rank's part repeats (clusters pushing their token slices)
+        for (N, K, M) in [(1024, 2048, 64), (2048, 2560, 512), (512, 768, 65), (40960, 256, 64), (38912, 512, 512),
+                          (2048, 6144, 512)]:
             codes = rng.integers(-8, 8, size=(N, K)).astype(np.int8)
             scales = rng.uniform(0.004, 0.02, size=(N, K // 32)).astype(np.float16).view(np.uint16)
             qfull = vkb.to_device_packed(O.pack(O.FMT_Q4, codes), dev)

@@ -112,8 +112,10 @@ static int rowsplit(vkb_comm_t* c, const void* q, const void* s, const void* x, 
     const size_t esz = f32 ? 4 : 2;
     const size_t chunk = (size_t)M * nl;                    // elements per rank
     uint8_t* mine = static_cast<uint8_t*>(work) + (size_t)c->rank * chunk * esz;
-    // a local refusal past this point (e.g. an unaligned pointer on one rank) still joins the collective
-    int rc = tc_dispatch(q, s, x, mine, f32, nl, K, M, st);
+    // a local refusal past this point (e.g. an unaligned pointer on one rank) still joins the collective. The local
+    // product takes the split-K count of the whole problem's one-GPU plan, so y is the one-GPU result bit for bit.
+    const TcOut out{nl, 0, nullptr, tc_split_for(N, K, M, f32)};
+    int rc = tc_dispatch(q, s, x, mine, f32, nl, K, M, st, &out);
     const int rc_nccl = nccl_rc(ncclAllGather(mine, work, chunk, f32 ? ncclFloat : ncclHalf, c->nc, st));
     if (rc == 0) rc = rc_nccl;
     const int rc_p = f32 ? launch_permute<float>(work, y, M, nl, c->size, st)
@@ -422,7 +424,7 @@ int vkb_gemm_q4_tc_rowsplit_p2p(vkb_comm_t* comm, const void* q_local, const voi
     if (b) {
         const P2PArgs pp = p2p_args(comm, b);
         const int nl = N / comm->size;
-        TcOut out{N, comm->rank * nl, &pp};
+        const TcOut out{N, comm->rank * nl, &pp, tc_split_for(N, K, M, false)};   // (the one-GPU split: same bits)
         rc = tc_dispatch(q_local, s_local, x, y_sym, false, nl, K, M, st, &out);
     }
     if (rc != 0) abstain(comm, st);

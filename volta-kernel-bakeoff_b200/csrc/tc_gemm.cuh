@@ -347,7 +347,9 @@ __device__ __noinline__ void tc_push_tile(const TcArgs& a, int row0, int tok0, i
 // partial accumulator in its own shared memory (the rings are idle by then), the cluster synchronises, and CTA r sums
 // token slice r over the cluster's partials in rank order (distributed shared memory reads), so the result does not
 // depend on timing: deterministic, unlike an atomic reduction. A second cluster barrier keeps every partial readable
-// until all slices are done. One tile per cluster (the planner launches tiles x splits CTAs).
+// until all slices are done. One tile per cluster (the planner launches tiles x splits CTAs). With peer stores (the
+// row split), each CTA then pushes its finished token slice to every peer; the row split uses the split count of the
+// whole problem's one-GPU plan, so its result is the one-GPU result bit for bit.
 // RB = 2 (opt-in, VKB_TC_RB=2): one CTA holds a 256-row tile as two 128-row blocks, each with its own accumulator
 // (TMEM columns 0 and NT rounded up to 32), and every activation K step feeds the MMAs of both blocks: the activations
 // are streamed from L2 once per 256 weight rows instead of once per 128 (that stream, N / 128 times the activations,
@@ -362,7 +364,7 @@ tc_q4_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUt
     static_assert(CG == 1 || (CG == 2 && !P2P), "peer stores use the one-CTA kernel");
     static_assert(WF == 0 || (WF == 1 && !P2P && CG == 1), "Q8 weights: the one-CTA kernel without peer stores");
     static_assert(RB == 1 || (RB == 2 && CG == 1 && !P2P && WF == 0), "two row blocks: the one-CTA Q4 kernel");
-    static_assert(!SPLIT || (CG == 1 && !P2P && RB == 1), "split-K: one-CTA tiles, no peer stores, one row block");
+    static_assert(!SPLIT || (CG == 1 && RB == 1), "split-K: one-CTA tiles, one row block");
     constexpr int BMR = TC_BM * RB;                         // weight rows of a CTA's tile
     constexpr int SK = RB == 1 ? TC_SLOT : 1;               // K steps per A slot
     constexpr int SLOT_COLS = RB * SK * TC_ACOLS;           // TMEM columns per A slot (128, or 64 with two blocks)
@@ -471,8 +473,9 @@ tc_q4_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUt
     // 32 consecutive outputs of one token: 64 or 128 contiguous bytes). With `arrive` the warp then
     // releases the accumulator to the MMA warp. With peer stores, the participants of a tile then push the finished
     // tile from this rank's y to every peer (p2p_push: 16-byte words) while the MMA warp works on the next tile; every
-    // participant passes the tile's named barrier, also after a failed wait (it then skips the work), so that no
-    // barrier waits for a warp that left.
+    // participant passes the tile's named barrier (id 2 for the epilogue warps alone, 3 for the last tile's three
+    // participants per lane quarter), also after a failed wait (it then skips the work), so that no barrier waits for
+    // a warp that left.
     // The epilogue warps empty every tile (with two accumulators, behind the next tile's MMAs); the dequantising
     // warps, idle by then, join for the CTA's last tile, whose epilogue nothing else overlaps. (Joining every tile
     // when there is one accumulator was measured slower: the epilogue code inside the dequantising loop, inline or
@@ -482,7 +485,7 @@ tc_q4_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUt
         if (!epi_began) {
             epi_began = true;
             pdl_wait();   // y may still be read or written by the previous grid
-            if constexpr (P2P) {   // this rank's copy may now be written; wait until every peer's may be
+            if constexpr (P2P && !SPLIT) {   // this rank's copy may now be written; wait until every peer's may be
                 const uint32_t e = p2p_epoch(a.pp);
                 if (warp == TC_WEPI0 && lane == 0) p2p_post_ready(a.pp, e);
                 if (lane == 0 && !p2p_wait_ready(a.pp, e)) ok = false;
@@ -509,8 +512,11 @@ tc_q4_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUt
                 if (lane == 0) arrive_leader(&accempty[acc]);
             }
         }
-        if constexpr (P2P) {   // the tile is complete in this rank's copy: its participants push it to every peer
-            named_sync(2, 128u * (uint32_t)parts);
+        if constexpr (P2P && !SPLIT) {   // the tile is complete in this rank's copy: its participants push it to every peer
+            // one barrier id per participant count: the epilogue warps' earlier tiles (128 threads) may still be
+            // at their barrier when the dequantising warps reach the last tile's (384); two counts on one named
+            // barrier at once is undefined (on B200 it raised an illegal-instruction fault)
+            named_sync(parts == 1 ? 2u : 3u, 128u * (uint32_t)parts);
             if (ok) tc_push_tile<OutT>(a, row0, tok0, (warp >= TC_WEPI0 ? warp - TC_WEPI0 : warp - TC_WDQ0 + 4) * 32
                                        + lane, 128 * parts);
         }
@@ -800,9 +806,14 @@ tc_q4_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUt
     if constexpr (SPLIT) {
         cluster_sync();   // every CTA's partial is in its shared memory
         pdl_wait();       // y may still be read or written by the previous grid
+        uint32_t e = 0;
+        if constexpr (P2P) {   // this rank's copy may now be written
+            e = p2p_epoch(a.pp);
+            if (threadIdx.x == 0) p2p_post_ready(a.pp, e);
+        }
+        const int t = tile_of(0), row0 = row0_of(t), tok0 = tok0_of(t), ntok = min(a.NT, a.M - tok0);
+        const int lo = (int)srank * ntok / a.splits, hi = ((int)srank + 1) * ntok / a.splits;
         if (ntl > 0) {
-            const int t = tile_of(0), row0 = row0_of(t), tok0 = tok0_of(t), ntok = min(a.NT, a.M - tok0);
-            const int lo = (int)srank * ntok / a.splits, hi = ((int)srank + 1) * ntok / a.splits;
             OutT* y = reinterpret_cast<OutT*>(a.y);
             const int n = row0 + 4 * lane;
             for (int tk = lo + warp; tk < hi; tk += TC_THREADS / 32) {
@@ -820,6 +831,21 @@ tc_q4_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUt
             }
         }
         cluster_sync();   // no CTA releases its shared memory while a peer still reads its partial
+        if constexpr (P2P) {
+            // the CTA's token slice of the tile is complete in this rank's copy (the barrier above orders every
+            // thread's stores): push it to every peer once every peer's CTA of this index accepts writes
+            bool rd = ok;
+            if (lane == 0 && rd) rd = p2p_wait_ready(a.pp, e);
+            rd = __shfl_sync(0xffffffffu, rd ? 1 : 0, 0) != 0;
+            ok = ok && rd;
+            if (rd && ntl > 0 && hi > lo) {
+                const int cols = min(TC_BM, a.N - row0);
+                const size_t pitch = (size_t)a.ldy * sizeof(OutT);
+                const size_t off = ((size_t)(tok0 + lo) * a.ldy + a.ycol0 + row0) * sizeof(OutT);
+                p2p_push(a.pp, hi - lo, cols * (int)sizeof(OutT), off | pitch,
+                         [&](int r) { return off + (size_t)r * pitch; }, threadIdx.x, TC_THREADS);
+            }
+        }
     }
     // teardown: every MMA has completed (the epilogue waited on each accumulator) before TMEM is released
     if (warp == 1 && !ok && ntl > 0) wait_b(&accfull[(ntl - 1) % a.nacc], ((ntl - 1) / a.nacc) & 1,

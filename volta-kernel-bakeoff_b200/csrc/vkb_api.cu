@@ -362,8 +362,10 @@ static int qmv_entry(const void* q, const void* s, const void* x, void* y, bool 
             const bool fits2 = 2 * (p.smem + 1024) <= d.smem_per_sm && !p2p;   // (1 KB reserved per CTA)
             const bool two = per_sm_force ? (per_sm_force == 2 && fits2) : (fits2 && tiles >= 4ll * d.sm_count);
             grid = d.sm_count * (two ? 2 : 1);   // (VKB_MOE_CTAS_PER_SM: tuning override)
-            // warp groups: no more than the most tiles a CTA can get
-            const long long most = (tiles + grid - 1) / grid;
+            // warp groups: no more than the tiles a CTA can get, bounded without E_local or the grid (a segment per
+            // slot, one CTA per SM): the groups set how a tile's K range is split over warps, so an expert-parallel
+            // rank and one GPU holding every expert must pick the same number to produce the same bits
+            const long long most = ((long long)slots * p.a.tilesN + d.sm_count - 1) / d.sm_count;
             while (p.a.wg > 1 && p.a.wg > most) p.a.wg /= 2;
         } else {
             grid = p.a.tilesN < d.sm_count ? p.a.tilesN : d.sm_count;
@@ -506,7 +508,8 @@ struct TcPlan {
 // every rank: ~2000 + 12 NT cycles).
 constexpr int TC_KUNIT = 8;
 static bool plan_tc(int N, int K, int M, int out_bytes, const DeviceInfo& d, TcPlan* p, int cg, int units_max,
-                    int wf = 0, bool allow_rb2 = false, int split_max = 1, const int* clusters_max = nullptr) {
+                    int wf = 0, bool allow_rb2 = false, int split_max = 1, const int* clusters_max = nullptr,
+                    int split_exact = 0) {
     TcArgs& a = p->a;
     const int nk = K / TC_BK;
     int NT = 0, RB = 1, SPL = 1;
@@ -514,12 +517,16 @@ static bool plan_tc(int N, int K, int M, int out_bytes, const DeviceInfo& d, TcP
     static const int split_env = getenv("VKB_TC_SPLIT") ? atoi(getenv("VKB_TC_SPLIT")) : 0;   // tuning override
     if (cg != 1 || wf != 0 || nk % TC_KUNIT != 0 || split_env == 1) split_max = 1;   // (VKB_TC_SPLIT=1: none)
     int split_force = split_max > 1 ? split_env : 0;
+    if (split_exact > 0) {   // exactly this split (a row split matching the whole problem's plan): no overrides
+        split_max = split_exact;
+        split_force = split_exact;
+    }
     const int nt_max = round_up(M, 32) < 256 ? round_up(M, 32) : 256;
     static const int nt_force = getenv("VKB_TC_NT") ? atoi(getenv("VKB_TC_NT")) : 0;   // tuning overrides
     static const int rb_force = getenv("VKB_TC_RB") ? atoi(getenv("VKB_TC_RB")) : 0;
     const int rb = rb_force == 2 && allow_rb2 && cg == 1 && wf == 0 ? 2 : 1;
     for (int pass = 0; pass < 3 && NT == 0; ++pass) {   // pass 1: without the NT override (it does not fit); pass 2:
-        if (pass == 2) split_force = 0;                  // without the split override either
+        if (pass == 2 && split_exact == 0) split_force = 0;   // without the split override either
         // steps of 16 above 128 tokens (512 = 3 x 176 wastes 3 % of the MMAs, 3 x 192 11 %; measured 1 % faster),
         // of 32 below (48-token tiles were slower than 64 at 6144x2048 x 128 tokens: more passes over the weights)
         for (int nt = nt_max; nt >= 32; nt -= ((pass == 0 && nt_force > 0) || nt > 128) && cg == 1 ? 16 : 32) {
@@ -598,6 +605,7 @@ static bool plan_tc(int N, int K, int M, int out_bytes, const DeviceInfo& d, TcP
             a.splits = SPL;
             p->grid = dim3((unsigned)(a.tiles * SPL));
         }
+        if (split_exact > 0 && a.splits != split_exact) return false;
         return true;
     }
     return false;
@@ -696,9 +704,12 @@ static int tc_entry(const void* q, const void* s, const void* x, void* y, int N,
     }
     TcPlan p{};
     const bool p2p = out && out->p2p;
-    const bool split_ok = !p2p && cg == 1 && wf == 0;
+    // split-K: the planner's choice, or exactly the caller's count (the row split's); none for other peer-store calls
+    const int split_exact = out ? out->split : 0;
+    const bool split_ok = cg == 1 && wf == 0 && (split_exact > 0 || !p2p);
     const int* clusters = split_ok ? tc_split_clusters(dev, d.smem_optin) : nullptr;
-    if (!plan_tc(N, K, M, (int)sizeof(OutT), d, &p, cg, units_max, wf, !p2p, split_ok ? 8 : 1, clusters))
+    if (!plan_tc(N, K, M, (int)sizeof(OutT), d, &p, cg, units_max, wf, !p2p, split_ok ? 8 : 1, clusters,
+                 split_ok ? split_exact : 0))
         return VKB_EUNSUPPORTED;
     p.a.y = y;
     p.a.ldy = out ? out->ldy : N;
@@ -718,10 +729,16 @@ static int tc_entry(const void* q, const void* s, const void* x, void* y, int N,
     void (*kern)(CUtensorMap, CUtensorMap, CUtensorMap, TcArgs) = nullptr;
     int ra = 0;
     if (p.a.p2p) {
-        if constexpr (std::is_same<OutT, __half>::value) {   // peer stores: fp16 outputs, one CTA per tile
-            kern = p.pk == 8 ? tc_q4_kernel<OutT, 8, true, 1> : tc_q4_kernel<OutT, 4, true, 1>;
-            ra = p.pk == 8 ? tc_attr<OutT, 8, true, 1>(dev, d.smem_optin)
-                           : tc_attr<OutT, 4, true, 1>(dev, d.smem_optin);
+        if constexpr (std::is_same<OutT, __half>::value) {   // peer stores: fp16 outputs, one CTA per tile (share)
+            if (p.a.splits > 1) {
+                kern = p.pk == 8 ? tc_q4_kernel<OutT, 8, true, 1, 0, 1, true> : tc_q4_kernel<OutT, 4, true, 1, 0, 1, true>;
+                ra = p.pk == 8 ? tc_attr<OutT, 8, true, 1, 0, 1, true>(dev, d.smem_optin)
+                               : tc_attr<OutT, 4, true, 1, 0, 1, true>(dev, d.smem_optin);
+            } else {
+                kern = p.pk == 8 ? tc_q4_kernel<OutT, 8, true, 1> : tc_q4_kernel<OutT, 4, true, 1>;
+                ra = p.pk == 8 ? tc_attr<OutT, 8, true, 1>(dev, d.smem_optin)
+                               : tc_attr<OutT, 4, true, 1>(dev, d.smem_optin);
+            }
         } else {
             return VKB_EUNSUPPORTED;
         }
@@ -767,6 +784,19 @@ static int tc_entry(const void* q, const void* s, const void* x, void* y, int N,
     cfg.numAttrs = na;
     const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, tq, ts, tx, p.a);
     return e == cudaSuccess ? 0 : -(int)e;
+}
+
+int tc_split_for(int N, int K, int M, bool f32, int wf) {
+    int dev = 0;
+    if (current_device(&dev) != 0) return 1;
+    const DeviceInfo& d = device_info(dev);
+    if (d.cc_major < 10 || N < 1 || M < 1 || K < 256 || K % 256 != 0 || wf != 0) return 1;
+    static const int cg_force = getenv("VKB_TC_CG") ? atoi(getenv("VKB_TC_CG")) : 0;   // (tc_entry's override)
+    if (cg_force == 2 && N >= 2 * TC_BM) return 1;
+    TcPlan p{};
+    const int* clusters = tc_split_clusters(dev, d.smem_optin);
+    if (!plan_tc(N, K, M, f32 ? 4 : 2, d, &p, 1, d.sm_count, wf, true, 8, clusters)) return 1;
+    return p.a.splits;
 }
 
 int tc_dispatch(const void* q, const void* s, const void* x, void* y, bool f32, int N, int K, int M, cudaStream_t st,

@@ -37,7 +37,11 @@ int qmv_dispatch(int fmt, const void* q, const void* s, const void* x, void* y, 
 struct TcOut {
     int ldy, col0;
     const P2PArgs* p2p;
+    int split = 0;   // split-K CTAs per tile: 0 the planner's choice (none with peer stores), n >= 1 exactly n
 };
+// The split-K count the one-GPU prompt GEMM of the whole problem takes on the current device (1: none): a row split
+// whose ranks use it sums every output in the one-GPU order.
+int tc_split_for(int N, int K, int M, bool f32, int wf = 0);
 // wf: weight format of the prompt GEMM (0 = Q4, 1 = Q8).
 int tc_dispatch(const void* q, const void* s, const void* x, void* y, bool f32, int N, int K, int M, cudaStream_t st,
                 const TcOut* out = nullptr, int wf = 0);
