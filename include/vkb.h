@@ -110,7 +110,10 @@ int vkb_moe(int fmt, const void* qpool, const void* spool, const int32_t* idx, i
  * Replaces tc_q4 / tc_q4_v2 (reference src/stage2.cuh:94-154, :226-229; src/stage4_tc.cuh:38-200): the weights are
  * dequantised to fp16 exactly as the reference rounds them ((code - 8) * scale, one rounding) and multiplied on the
  * 5th-generation tensor cores with fp32 accumulation. Needs K % 256 == 0 and 16-byte aligned q, s, x; any M
- * and N (no tile-multiple requirement). fp16 output; _f32 writes fp32 (the reference's float* y). */
+ * and N (no tile-multiple requirement). fp16 output; _f32 writes fp32 (the reference's float* y).
+ * Tables with few 128-row tiles (Q4, K % 512 == 0) run split-K (the reference's split-K, src/stage4_tc.cuh:130-141):
+ * clusters of 2-8 CTAs share a tile's K range and sum their fp32 partials in a fixed order over distributed shared
+ * memory, so repeated calls give identical bits (the reference's atomicAdd reduction does not). */
 int vkb_gemm_q4_tc(const void* q, const void* s, const void* x, void* y, int N, int K, int M, vkb_stream_t stream);
 int vkb_gemm_q4_tc_f32(const void* q, const void* s, const void* x, float* y, int N, int K, int M,
                        vkb_stream_t stream);
@@ -148,7 +151,8 @@ int vkb_moe_ep(vkb_comm_t* comm, int fmt, const void* qpool, const void* spool, 
                const void* x, void* y, int out_f32, int E_local, int e0, int N, int K, vkb_stream_t stream);
 /* Prompt GEMM, row split: this rank holds weight rows [r N/G, (r+1) N/G) (q_local, s_local in the vkb_gemm_q4_tc
  * layout, N/G rows); x [M][K] on every rank. After the call every rank's y [M][N] is the full product. work: device
- * memory of vkb_gemm_rowsplit_work_bytes(M, N, out_f32) bytes (caller-owned). N must be divisible by the rank count. */
+ * memory of vkb_gemm_rowsplit_work_bytes(M, N, out_f32) bytes (caller-owned). N must be divisible by the rank count.
+ * y is the one-GPU vkb_gemm_q4_tc result bit for bit (each rank's part uses the whole problem's split-K count). */
 size_t vkb_gemm_rowsplit_work_bytes(int M, int N, int out_f32);
 int vkb_gemm_q4_tc_rowsplit(vkb_comm_t* comm, const void* q_local, const void* s_local, const void* x, void* y,
                             void* work, int N, int K, int M, vkb_stream_t stream);
@@ -183,7 +187,8 @@ int vkb_comm_alloc(vkb_comm_t* comm, size_t bytes, void** ptr);
 int vkb_comm_free(vkb_comm_t* comm, void* ptr);
 int vkb_comm_epoch(const vkb_comm_t* comm, unsigned int* epoch);
 /* Row split with the all-gather fused into the GEMM: the tcgen05 epilogue stores this rank's columns of y straight
- * into every rank's copy of y_sym (>= M x N fp16). Same operands and result as vkb_gemm_q4_tc_rowsplit. */
+ * into every rank's copy of y_sym (>= M x N fp16). Same operands and result as vkb_gemm_q4_tc_rowsplit (the one-GPU
+ * result bit for bit; with split-K each CTA pushes its finished token slice). */
 int vkb_gemm_q4_tc_rowsplit_p2p(vkb_comm_t* comm, const void* q_local, const void* s_local, const void* x, void* y_sym,
                                 int N, int K, int M, vkb_stream_t stream);
 /* Expert-parallel MoE with the combine fused into the GEMV: each rank's kernel stores the slots of its own experts
