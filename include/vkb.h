@@ -24,7 +24,8 @@
  *     the tail of call i; activations and outputs are still ordered after the previous kernel on the stream. The
  *     weights and scales are read BEFORE the preceding kernel in the stream has finished, so that kernel must not
  *     write them (weights are normally static; after a kernel that repacks them, call vkb_set_pdl(0) for the next
- *     call or put any other kernel in between).
+ *     call or put any other kernel in between). MoE calls read nothing before the preceding kernel has finished: their
+ *     index list (which a router kernel may have just written) decides which weights they read.
  */
 #ifndef VKB_H
 #define VKB_H
