@@ -441,10 +441,10 @@ constexpr int QMV_MAXWG = 4;
 __host__ __device__ constexpr int qmv_nbars(int nstage) { return 2 * nstage + 4 + 4 * QMV_MAXWG + 4 + 1; }
 
 // MINB: CTAs per SM the register budget is sized for. 2 (56 registers a thread) lets the next call's CTA share the SM
-// under PDL and is what dense calls and two-CTA MoE calls use; a MoE call with one CTA per SM (it cannot start before
-// its dependency anyway: the index list decides its weights) uses MINB = 1, without spills and with more
-// registers for overlap (measured on B200: 8 experts of 512x2048, 8 tokens 13.7 us against 14.7, 64 tokens 35.0
-// against 37.2).
+// under PDL (its weight prefetch); calls planned with one CTA per SM -- most dense fp16-in calls, and MoE calls, which
+// cannot start before their dependency anyway (the index list decides the weights) -- use MINB = 1: no spills, and
+// registers for four MMA chains per loop iteration (measured on B200: 8 experts of 512x2048, 8 tokens 13.7 us against
+// 14.7; dense 12288x2560 Q4 1 token 8.0 us against 9.1).
 // XF32: the activations arrive as fp32 (the reference's fp32-in decode entry). After the dependency wait the consumer
 // warps read them from global memory (16-byte loads), round them to fp16 (round to nearest even, the reference's
 // conversion) straight into the fp16 activation buffer and complete its barrier themselves: no conversion launch,
@@ -453,7 +453,7 @@ template <int F, int MODE, typename OutT, bool XF32 = false, int MINB = 2>
 __global__ void __launch_bounds__(32 * (QMV_NW + 1), MINB)
 qmv_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap ts, const __grid_constant__ QmvArgs a) {
     static_assert(!XF32 || MODE == QMV_DENSE || MODE == QMV_GLU, "fp32 activations: dense and gate/up calls");
-    static_assert(MINB == 2 || MODE == QMV_MOE || MODE == QMV_MOE_P2P, "one-CTA register budget: MoE calls");
+    static_assert(MINB == 2 || (MODE != QMV_GLU && !XF32), "one-CTA register budget: dense fp16-in and MoE calls");
     constexpr bool GLU = MODE == QMV_GLU;
     constexpr bool MOE = MODE == QMV_MOE || MODE == QMV_MOE_P2P;
     extern __shared__ uint8_t smem_raw[];

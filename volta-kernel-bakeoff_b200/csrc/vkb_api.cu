@@ -178,7 +178,7 @@ static int round_up(int v, int m) { return (v + m - 1) / m * m; }
 // glu: gate/up tile pairs over a [2N][K] table (N output rows, 2 ceil(N / 16) tiles, the gate hand-over slots after
 // the reduction region).
 static bool plan_qmv(int fmt, int N, int K, int xrows, int moe_slots, int E_local, const DeviceInfo& d, QmvPlan* p,
-                     bool glu = false, bool xres = false) {
+                     bool glu = false, bool xres = false, bool dense = false) {
     const int bits = fmt_bits(fmt), unit = QMV_KS_UNIT;
     static const int ks_force = getenv("VKB_QMV_KSMAX") ? atoi(getenv("VKB_QMV_KSMAX")) : 0;   // tuning override
     const int ks_max = ks_force >= unit ? ks_force : 12288 / bits;   // 1.5 KB of codes per row per stage (the
@@ -198,8 +198,14 @@ static bool plan_qmv(int fmt, int N, int K, int xrows, int moe_slots, int E_loca
     const int pair_budget = d.smem_per_sm / 2 - 1024;   // two CTAs per SM
     const int solo_budget = d.smem_optin;
     static const int pair_min = getenv("VKB_QMV_PAIRMIN") ? atoi(getenv("VKB_QMV_PAIRMIN")) : 4;   // tuning override
+    // dense fp16-in calls (`dense`): the two-CTA footprint only for one-stage tiles of K <= 2048 with more tiles than
+    // SMs, the short calls whose next call's weight prefetch (under PDL, in the second CTA) is worth a shallow ring;
+    // every other dense call takes one CTA per SM with the deepest ring and the kernel's 96-register variant
+    // (measured on B200, configs[1] tables, 50 same-shape calls per graph: 12288x2560 Q4 1 token 8.0 us against 9.1,
+    // 2048x6144 4.6 against 4.8, 6144x2048 Q4 4.4 against 4.0 -- the exception).
+    const bool pair_first = !dense || (K <= 2048 && nchunks == 1 && (N + QMV_ROWS - 1) / QMV_ROWS > d.sm_count);
     int nstage = 0, budget = pair_budget;
-    for (int pass = 0; pass < 2; ++pass) {
+    for (int pass = pair_first ? 0 : 1; pass < 2; ++pass) {
         budget = pass == 0 ? pair_budget : solo_budget;
         nstage = 16;
         while (nstage >= 2 && nstage * stage_bytes + fixed_for(nstage) > budget) --nstage;
@@ -328,7 +334,7 @@ static int qmv_entry(const void* q, const void* s, const void* x, void* y, bool 
     // rows of each expert segment (at most 8 slots) are staged in turn
     const bool xres = moe && M <= QMV_MAXTOK;
     const int xrows = moe && !xres ? (slots < QMV_MAXTOK ? slots : QMV_MAXTOK) : M;
-    if (fast && plan_qmv(F, N, K, xrows, slots, E_local, d, &p, false, xres)) {
+    if (fast && plan_qmv(F, N, K, xrows, slots, E_local, d, &p, false, xres, !moe)) {
         constexpr int BITS = FmtTraits<F>::BITS;
         CUtensorMap tq, ts;
         int r = get_tmap_2d(&tq, q, (uint64_t)rows, (uint64_t)K * BITS / 8, CU_TENSOR_MAP_DATA_TYPE_UINT64, 8,
@@ -381,6 +387,9 @@ static int qmv_entry(const void* q, const void* s, const void* x, void* y, bool 
             return f32 ? launch_qmv<F, QMV_MOE, float, false, 1>(p, tq, ts, grid, st, dev)
                        : launch_qmv<F, QMV_MOE, __half, false, 1>(p, tq, ts, grid, st, dev);
         }
+        if (2 * (p.smem + 1024) > d.smem_per_sm)   // one CTA per SM: the 96-register variant
+            return f32 ? launch_qmv<F, QMV_DENSE, float, false, 1>(p, tq, ts, grid, st, dev)
+                       : launch_qmv<F, QMV_DENSE, __half, false, 1>(p, tq, ts, grid, st, dev);
         return f32 ? launch_qmv<F, QMV_DENSE, float>(p, tq, ts, grid, st, dev)
                    : launch_qmv<F, QMV_DENSE, __half>(p, tq, ts, grid, st, dev);
     }
@@ -953,7 +962,7 @@ int vkb_plan_describe(int kind, int fmt, int N, int K, int M, int sm_count, int 
         if (M > QMV_MAXTOK) return VKB_EUNSUPPORTED;
         if (K % 256 != 0) return VKB_EUNSUPPORTED;
         QmvPlan p{};
-        if (!plan_qmv(fmt, N, K, M, 0, 0, d, &p, kind == 2)) return VKB_EUNSUPPORTED;
+        if (!plan_qmv(fmt, N, K, M, 0, 0, d, &p, kind == 2, false, kind == 0)) return VKB_EUNSUPPORTED;
         const QmvArgs& a = p.a;
         const int v[] = {p.smem, a.nstage, a.nchunks, a.KS, a.wg, a.stage_bytes,
                          a.tilesN < sm_count ? a.tilesN : sm_count, a.cpitch, a.spitch, a.tilesN};
