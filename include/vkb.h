@@ -93,6 +93,11 @@ int vkb_gate_up_glu_q4(const void* q, const void* s, const void* x, float* ystac
  * the block layouts: vkb_host.h). One memory-bound kernel on stream. No counterpart in the reference, which states
  * value parity with GGUF (src/bakeoff.cu:5-7) but loads no GGUF data. */
 int vkb_gguf_to_vkb_device(int fmt, const void* blocks, int N, int K, void* q, void* scales, vkb_stream_t stream);
+/* Dense copy of packed weights: w [N][K] fp16 (out_bf16 = 0) or bf16 = code * scale with one round-to-nearest (the
+ * reference's dequant_q4, src/bakeoff.cu:52-68, that feeds its "dq4+cublas" control, :687-690; here for every
+ * format). q in the layout of the format's GEMV (4-byte aligned for Q4, 8 for Q8, 2 for Q2), s fp16 [N][K/32], w
+ * 16-byte aligned. K % 32 == 0 (Q2: K % 64 == 0). */
+int vkb_dequant(int fmt, const void* q, const void* s, void* w, int N, int K, int out_bf16, vkb_stream_t stream);
 
 /* ---- MoE decode, one launch ----------------------------------------------------------------------------------------
  * Replaces moe_fused_q4 + MoePtrs (reference src/bakeoff.cu:157-186, :826-830), where the host picked one pointer set

@@ -20,7 +20,7 @@ pytestmark = pytest.mark.gpu
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 BAKEOFF = os.path.join(ROOT, "volta-kernel-bakeoff_b200", "bin", "bakeoff")
 PACKED = {"vkb_q4", "vkb_q8", "vkb_q2", "vkb_q4_f16out", "vkb_q8_f16out", "vkb_q2_f16out", "vkb_tc_q4",
-          "vkb_tc_q4_f16out", "vkb_tc_q8", "vkb_q4_f32in", "vkb_glu_q4_f32in", "vkb_moe_q4"}
+          "vkb_tc_q4_f16out", "vkb_tc_q8", "vkb_q4_f32in", "vkb_glu_q4_f32in", "vkb_moe_q4", "dq4+cublas"}
 
 
 def _run(sabotage: bool):

@@ -29,7 +29,7 @@ BAKEOFF = os.path.join(BINDIR, "bakeoff")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ARCH + ["-lineinfo", "-O3", "-std=c++17", "-Xcompiler", "-fPIC", "-I" + os.path.join(ROOT, "include")]
 
-LIB_SOURCES = ["vkb_api.cu", "comm.cu", "gguf.cu", "formats.cpp"]
+LIB_SOURCES = ["vkb_api.cu", "comm.cu", "gguf.cu", "dequant.cu", "formats.cpp"]
 
 
 def nvcc() -> str:

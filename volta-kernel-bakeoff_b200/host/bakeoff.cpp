@@ -16,7 +16,8 @@
 // vkb_glu_q4_f32in (gate + up + SwiGLU, fp32 activations), vkb_tc_q4 / vkb_tc_q8 (prompt GEMM on tcgen05, Q4 or Q8
 // weights, any token count),
 // vkb_moe_q4 (MoE, one launch over a device index list), and the controls cublas_fp16 (the reference's
-// cublasGemmEx fp16 x fp16 -> fp32, src/bakeoff.cu:249-253) and cublas_bf16 (bf16 x bf16 -> bf16). Timing follows the
+// cublasGemmEx fp16 x fp16 -> fp32, src/bakeoff.cu:249-253), cublas_bf16 (bf16 x bf16 -> bf16) and dq4+cublas (the
+// packed Q4 weights dequantised on the GPU by vkb_dequant, then cublas_fp16: the reference's row, src/bakeoff.cu:687-690). Timing follows the
 // reference's time_us (src/bakeoff.cu:283-298: 20 warm-up calls, the median of 5 repetitions of 50 calls), with the 50
 // calls captured in a CUDA graph on a created stream so that host launch cost is not measured, and the weights
 // cycled over copies that span at least 4x the L2 (every call reads HBM).
@@ -237,7 +238,7 @@ static void run_sweep() {
             const auto p = packed(w, false);
             Set st{fmt, p.size() + w.scale.size() * 2, 0, {}, {}};
             if ((any_gemv && want(gname[fmt])) ||
-                (fmt == VKB_FMT_Q4 && (want("vkb_tc_q4") || (any_gemv && want("vkb_q4_f32in")))) ||
+                (fmt == VKB_FMT_Q4 && (want("vkb_tc_q4") || want("dq4+cublas") || (any_gemv && want("vkb_q4_f32in")))) ||
                 (fmt == VKB_FMT_Q8 && want("vkb_tc_q8")))
                 st.c = copies_for(st.bytes);
             for (int i = 0; i < st.c; ++i) {
@@ -276,6 +277,18 @@ static void run_sweep() {
             if (want("cublas_bf16"))
                 report("cublas_bf16", time_us([&](int i) { cublas_bf16(db[i % cf], dxb, dyh, sh.N, sh.K, M); return true; }),
                        NK * 2, cf);
+            if (want("dq4+cublas") && sets[0].c > 0) {   // the reference's control: dequantise, then a cuBLAS fp16 GEMM
+                const Set& s4d = sets[0];
+                void* wtmp = dalloc<uint16_t>(NK);
+                report("dq4+cublas", time_us([&](int i) {
+                           if (!VK(vkb_dequant(VKB_FMT_Q4, s4d.q[i % s4d.c], s4d.s[i % s4d.c], wtmp, sh.N, sh.K, 0,
+                                               (vkb_stream_t)g_st), "vkb_dequant"))
+                               return false;
+                           cublas_f16(wtmp, dx, dy, sh.N, sh.K, M);
+                           return true;
+                       }), s4d.bytes, s4d.c);
+                CK(cudaFree(wtmp));
+            }
             const Set& s4 = sets[0];
             if (want("vkb_tc_q4"))
                 report("vkb_tc_q4", time_us([&](int i) {
@@ -481,6 +494,7 @@ static void check_tables(bool sabotage, std::mt19937& rng) {
             void* dq = dupload(packed(w, sabotage));
             void* ds = dupload(w.scale);
             void* dwf = fmt == VKB_FMT_Q4 ? dupload(dequant(w, false)) : nullptr;
+            void* dwq = fmt == VKB_FMT_Q4 ? dalloc<uint16_t>((size_t)sh.N * sh.K) : nullptr;   // vkb_dequant's output
             struct XCase { int M, kind; };
             std::vector<XCase> xcases;
             for (int M : {1, 2, 4, 8}) xcases.push_back({M, 0});
@@ -520,6 +534,12 @@ static void check_tables(bool sabotage, std::mt19937& rng) {
                         cublas_f16(dwf, dx, (float*)y, sh.N, sh.K, M);
                         return true;
                     }, rng);
+                    check_one("dq4+cublas", label, w, x, M, true, 2e-3, [&](void* y) {   // packed -> GPU dequant
+                        if (!VK(vkb_dequant(VKB_FMT_Q4, dq, ds, dwq, sh.N, sh.K, 0, (vkb_stream_t)g_st), "vkb_dequant"))
+                            return false;
+                        cublas_f16(dwq, dx, (float*)y, sh.N, sh.K, M);
+                        return true;
+                    }, rng);
                 }
                 if (fmt == VKB_FMT_Q8 && xc.kind != 1) {   // the Q8 prompt GEMM (tc_q8, planned by the reference)
                     check_one("vkb_tc_q8", label, w, x, M, true, 2e-3, [&](void* y) {
@@ -532,6 +552,7 @@ static void check_tables(bool sabotage, std::mt19937& rng) {
             CK(cudaFree(dq));
             CK(cudaFree(ds));
             if (dwf) CK(cudaFree(dwf));
+            if (dwq) CK(cudaFree(dwq));
         }
     }
 }

@@ -109,6 +109,7 @@ def _register_optional(L) -> None:
         "vkb_gemm_q8_tc": ([vp, vp, vp, vp, i, i, i, vp], i),
         "vkb_gemm_q8_tc_f32": ([vp, vp, vp, vp, i, i, i, vp], i),
         "vkb_gguf_to_vkb_device": ([i, vp, i, i, vp, vp, vp], i),
+        "vkb_dequant": ([i, vp, vp, vp, i, i, i, vp], i),
         "vkb_gguf_bytes": ([i, i, i], ctypes.c_size_t),
         "vkb_gguf_to_vkb": ([i, vp, i, i, vp, vp], i),
         "vkb_vkb_to_gguf": ([i, vp, vp, i, i, vp], i),
@@ -322,6 +323,15 @@ def gguf_to_vkb_device(fmt: int, blocks, N: int, K: int, stream=None):
     check(lib().vkb_gguf_to_vkb_device(fmt, _ptr(blocks), N, K, _ptr(q), _ptr(s), _stream(stream)),
           "vkb_gguf_to_vkb_device")
     return q, s
+
+
+def dequant(fmt: int, q, s, N: int, K: int, bf16: bool = False, w=None, stream=None):
+    """Device: packed weights -> a dense fp16 (or bf16) [N][K] tensor, code * scale rounded once (vkb_dequant)."""
+    torch = _torch()
+    if w is None:
+        w = torch.empty((N, K), dtype=torch.bfloat16 if bf16 else torch.float16, device=q.device)
+    check(lib().vkb_dequant(fmt, _ptr(q), _ptr(s), _ptr(w), N, K, int(bf16), _stream(stream)), "vkb_dequant")
+    return w
 
 
 def moe(fmt: int, qpool, spool, idx, x, y=None, E_local: int | None = None, e0: int = 0, out_f32: bool = False,
