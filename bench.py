@@ -304,7 +304,7 @@ def prompt_section(torch, vkb, dev, stream, L2, peaks):
     """configs[4] on one GPU: the tcgen05 prompt GEMM against cuBLAS bf16 (torch.matmul, bf16 in and out) at the same
     shapes, weights cycled over >= 4x L2 for both; the same shapes with Q8 weights (the Q8 prompt kernel the reference
     planned but never built) as q8_* entries; also the small-N / large-K tables, which the planner runs as split-K
-    clusters."""
+    clusters. dq4_cublas_fp16_us: the reference's dq4+cublas control (GPU dequantisation, then an fp16 cuBLAS GEMM)."""
     out = {}
     for N, K in PROMPT_TABLES:
         sets = {}
@@ -324,6 +324,13 @@ def prompt_section(torch, vkb, dev, stream, L2, peaks):
             yb = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
             us_b = _median_us(torch, stream, lambda i: torch.matmul(xb, wl[i % nb].t(), out=yb), vkb_graph=False)
             fl = 2.0 * M * N * K
+            # the reference's dq4+cublas control: the packed Q4 weights dequantised on the GPU (vkb_dequant), then
+            # an fp16 GEMM (torch.matmul, cuBLAS)
+            ql4, sl4, nq4 = sets[0]
+            wtmp = torch.empty((N, K), dtype=torch.float16, device=dev)
+            us_dq = _median_us(torch, stream, lambda i: (vkb.dequant(0, ql4[i % nq4], sl4[i % nq4], N, K, w=wtmp),
+                                                         torch.matmul(x, wtmp.t(), out=y)), vkb_graph=False)
+            del wtmp
             for fmt, tag in ((0, "q4"), (1, "q8")):
                 ql, sl, nq = sets[fmt]
                 us = _median_us(torch, stream, lambda i: vkb.gemm_tc(ql[i % nq], sl[i % nq], x, y=y, fmt=fmt))
@@ -331,6 +338,8 @@ def prompt_section(torch, vkb, dev, stream, L2, peaks):
                     "us": round(us, 2), "tflops": round(fl / us / 1e6, 1), "cublas_bf16_us": round(us_b, 2),
                     "cublas_bf16_tflops": round(fl / us_b / 1e6, 1), "time_vs_cublas_bf16": round(us_b / us, 3),
                     "frac_of_bf16_peak": round(fl / us / 1e6 / float(peaks.get("bf16_tflops", 1590.0)), 3)}
+                if fmt == 0:
+                    out[f"{tag}_{N}x{K}_m{M}"]["dq4_cublas_fp16_us"] = round(us_dq, 2)
         del sets, wl
     return out
 
