@@ -764,8 +764,11 @@ qmv_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUten
             if (!cwait(&full[stg], rnd & 1)) { ok = false; break; }
             const uint32_t st = ring_s + (uint32_t)(stg * a.stage_bytes);
             const int G1 = min(G1w, KG - kc);
-            consume_stage<F, MINB == 1 ? 4 : 2>(st + c_row, cp, st + s_row, sp, G0, G1, xrow + (uint32_t)(kc * 64), t,
-                                                acc);
+            // four groups per iteration with the one-CTA register budget and in dense calls (measured on B200 under
+            // the 56-register cap: 8192x2048 Q4 1 token 4.59 -> 4.44 us; two groups stay for gate/up, whose two-
+            // and four-token calls got 8% slower, and for two-CTA MoE)
+            consume_stage<F, (MINB == 1 || MODE == QMV_DENSE) ? 4 : 2>(st + c_row, cp, st + s_row, sp, G0, G1,
+                                                                      xrow + (uint32_t)(kc * 64), t, acc);
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[stg]);
             if (++stg == a.nstage) { stg = 0; ++rnd; }
