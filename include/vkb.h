@@ -117,7 +117,7 @@ int vkb_moe(int fmt, const void* qpool, const void* spool, const int32_t* idx, i
  * dequantised to fp16 exactly as the reference rounds them ((code - 8) * scale, one rounding) and multiplied on the
  * 5th-generation tensor cores with fp32 accumulation. Needs K % 256 == 0 and 16-byte aligned q, s, x; any M
  * and N (no tile-multiple requirement). fp16 output; _f32 writes fp32 (the reference's float* y).
- * Tables with few 128-row tiles (Q4, K % 512 == 0) run split-K (the reference's split-K, src/stage4_tc.cuh:130-141):
+ * Tables with few 128-row tiles (K % 512 == 0) run split-K (the reference's split-K, src/stage4_tc.cuh:130-141):
  * clusters of 2-8 CTAs share a tile's K range and sum their fp32 partials in a fixed order over distributed shared
  * memory, so repeated calls give identical bits (the reference's atomicAdd reduction does not). */
 int vkb_gemm_q4_tc(const void* q, const void* s, const void* x, void* y, int N, int K, int M, vkb_stream_t stream);

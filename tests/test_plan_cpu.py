@@ -85,11 +85,12 @@ def test_prompt_plans_fit(fmt):
 
 
 def test_split_k_plans():
-    """Kind 3, the prompt planner with split-K: the small-N / large-K tables (20 and 16 row tiles) take clusters of 2-8
-    CTAs per tile, one tile per cluster, all within the SM count, K units (8 K steps) to spare for every CTA, and the
-    fp32 partial (128 rows x NT) inside the shared memory the rings used; large tables keep the one-CTA plan."""
-    for (N, K), M in itertools.product([(2560, 6144), (2048, 6144)], [16, 64, 128, 512]):
-        p = vkb.plan(vkb.PLAN_TC_SPLIT, O.FMT_Q4, N, K, M)
+    """Kind 3, the prompt planner with split-K: the small-N / large-K tables (20 and 16 row tiles; Q4 and Q8) take
+    clusters of 2-8 CTAs per tile, one tile per cluster, all within the SM count, K units (8 K steps) to spare for
+    every CTA, and the fp32 partial (128 rows x NT) inside the shared memory the rings used; large tables keep the
+    one-CTA plan."""
+    for (N, K), M, fmt in itertools.product([(2560, 6144), (2048, 6144)], [16, 64, 128, 512], [O.FMT_Q4, O.FMT_Q8]):
+        p = vkb.plan(vkb.PLAN_TC_SPLIT, fmt, N, K, M)
         assert 2 <= p["splits"] <= 8 and p["splits"] <= K // 64 // 8, (N, K, M, p)
         assert p["grid"] == p["tiles"] * p["splits"] <= LIM["sm_count"], (N, K, M, p)
         assert 128 * p["NT"] * 4 <= p["nx"] * p["x_stage"] + p["np"] * 128 * (32 * p["pk"] + 16 + 48), p
@@ -97,8 +98,8 @@ def test_split_k_plans():
         p, q = vkb.plan(vkb.PLAN_TC_SPLIT, O.FMT_Q4, N, K, M), vkb.plan(vkb.PLAN_TC, O.FMT_Q4, N, K, M)
         assert p["splits"] == 1 and {k: v for k, v in p.items() if k != "splits"} == \
             {k: v for k, v in q.items() if k != "cg"}, (N, K, M, p, q)
-    # Q8 weights and K without whole 8-step units stay unsplit
-    assert vkb.plan(vkb.PLAN_TC_SPLIT, O.FMT_Q8, 2560, 6144, 512)["splits"] == 1
+    # Q8 weights split too; K without whole 8-step units stays unsplit
+    assert vkb.plan(vkb.PLAN_TC_SPLIT, O.FMT_Q8, 2560, 6144, 512)["splits"] > 1
     assert vkb.plan(vkb.PLAN_TC_SPLIT, O.FMT_Q4, 2560, 768, 64)["splits"] == 1
 
 

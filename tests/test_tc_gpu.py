@@ -162,7 +162,7 @@ def test_tc_split_k_small_tables(cuda, N, K, M):
 
 
 @pytest.mark.parametrize("N,K,M", [(512, 256, 16), (1031, 768, 65), (2048, 2048, 511), (12288, 2560, 512),
-                                   (8192, 2048, 64)])
+                                   (8192, 2048, 64), (2560, 6144, 512), (2048, 6144, 64)])   # (the last two: split-K)
 def test_tc_q8_vs_torch_fp32_and_oracle(cuda, N, K, M):
     """The Q8 prompt GEMM (vkb_gemm_tc with Q8 weights): against torch fp32 over the fp16-rounded weights (tight) and
     the CPU oracle of the exact codes with the fp16-class tolerance."""

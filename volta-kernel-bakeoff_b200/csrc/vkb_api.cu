@@ -509,7 +509,7 @@ struct TcPlan {
 // deepened while shared memory lasts. With cg = 2 the units are CTA pairs (at most `units_max` co-resident), a tile
 // has 256 rows and each CTA's X stages hold half of the tile's tokens.
 //
-// Split-K (split_max > 1: Q4, one-CTA tiles, no peer stores): with few tiles the MMAs of one tile's K range are the
+// Split-K (split_max > 1: one-CTA tiles, no peer stores unless the row split asks for its exact count): with few tiles the MMAs of one tile's K range are the
 // whole call (2560x6144 at 512 tokens: 40 tiles on 148 SMs), so S CTAs of a cluster share a tile, each taking units
 // of TC_KUNIT K steps, at one tile per cluster (tiles x S <= SMs, and <= the clusters of S that fit at once:
 // clusters_max[S], or SMs / S when null). Cost: the longest share's K steps, plus the partial exchange (shared
@@ -524,7 +524,7 @@ static bool plan_tc(int N, int K, int M, int out_bytes, const DeviceInfo& d, TcP
     int NT = 0, RB = 1, SPL = 1;
     double best = 1e300;
     static const int split_env = getenv("VKB_TC_SPLIT") ? atoi(getenv("VKB_TC_SPLIT")) : 0;   // tuning override
-    if (cg != 1 || wf != 0 || nk % TC_KUNIT != 0 || split_env == 1) split_max = 1;   // (VKB_TC_SPLIT=1: none)
+    if (cg != 1 || nk % TC_KUNIT != 0 || split_env == 1) split_max = 1;   // (VKB_TC_SPLIT=1: none)
     int split_force = split_max > 1 ? split_env : 0;
     if (split_exact > 0) {   // exactly this split (a row split matching the whole problem's plan): no overrides
         split_max = split_exact;
@@ -715,7 +715,7 @@ static int tc_entry(const void* q, const void* s, const void* x, void* y, int N,
     const bool p2p = out && out->p2p;
     // split-K: the planner's choice, or exactly the caller's count (the row split's); none for other peer-store calls
     const int split_exact = out ? out->split : 0;
-    const bool split_ok = cg == 1 && wf == 0 && (split_exact > 0 || !p2p);
+    const bool split_ok = cg == 1 && (split_exact > 0 || !p2p);
     const int* clusters = split_ok ? tc_split_clusters(dev, d.smem_optin) : nullptr;
     if (!plan_tc(N, K, M, (int)sizeof(OutT), d, &p, cg, units_max, wf, !p2p, split_ok ? 8 : 1, clusters,
                  split_ok ? split_exact : 0))
@@ -751,6 +751,10 @@ static int tc_entry(const void* q, const void* s, const void* x, void* y, int N,
         } else {
             return VKB_EUNSUPPORTED;
         }
+    } else if (p.a.splits > 1 && wf == 1) {   // split-K clusters, Q8 weights
+        kern = p.pk == 8 ? tc_q4_kernel<OutT, 8, false, 1, 1, 1, true> : tc_q4_kernel<OutT, 4, false, 1, 1, 1, true>;
+        ra = p.pk == 8 ? tc_attr<OutT, 8, false, 1, 1, 1, true>(dev, d.smem_optin)
+                       : tc_attr<OutT, 4, false, 1, 1, 1, true>(dev, d.smem_optin);
     } else if (p.a.splits > 1) {   // split-K clusters (Q4, one CTA per tile share)
         kern = p.pk == 8 ? tc_q4_kernel<OutT, 8, false, 1, 0, 1, true> : tc_q4_kernel<OutT, 4, false, 1, 0, 1, true>;
         ra = p.pk == 8 ? tc_attr<OutT, 8, false, 1, 0, 1, true>(dev, d.smem_optin)
