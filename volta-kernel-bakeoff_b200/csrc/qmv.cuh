@@ -571,8 +571,10 @@ qmv_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUten
     if (warp == QMV_NW) {
         // ===================== producer (one thread) =====================
         if (lane == 0) {
-            prefetch_tmap(&tq);
-            prefetch_tmap(&ts);
+            if constexpr (!MOE) {   // (MoE: prefetched in the prologue, before the dependency wait)
+                prefetch_tmap(&tq);
+                prefetch_tmap(&ts);
+            }
             const int total_it = ntl * a.nchunks;
             const int pre = min(total_it, a.nstage);
             // iteration cursor: chunk c of tile `tile` of segment `sg`; ring slot stg in round rnd
