@@ -118,7 +118,7 @@ def test_moe_expert_parallel_subsets(cuda, T):
 
 @pytest.mark.parametrize("T,k", [(4, 8), (11, 3), (2, 16)])
 def test_moe_routing_boundaries(cuda, T, k):
-    """32 slots (the largest list routed one slot per lane), 33 slots over 11 tokens (the general routing with the
+    """32 slots (the largest list routed one slot per lane), 33 slots over 11 tokens (the CTA-wide routing with the
     per-segment activation rows), and 16 slots over 2 tokens with experts repeated across and inside tokens."""
     rng = np.random.default_rng(70 + T * k)
     E, N, K = 9, 48, 512
@@ -130,6 +130,28 @@ def test_moe_routing_boundaries(cuda, T, k):
     ref, mag, _ = O.moe_ref(codes, scales, idx, x)
     err, m, n = O.check_error(y, ref, mag)
     assert err <= 1e-3, (err, m, n)
+
+
+@pytest.mark.parametrize("E,N,K,T,k,crowd", [(16, 1040, 512, 96, 2, True), (1000, 64, 256, 64, 8, False),
+                                               (40, 520, 512, 600, 1, False)])
+def test_moe_cta_routing(cuda, E, N, K, T, k, crowd):
+    """Lists of more than 32 slots are routed by the whole CTA, and every CTA must build the same segments: one expert
+    taking 96+ slots (past the per-slot count, the one-warp countdown), 1000 local experts (several passes of the
+    expert scan), and 600 slots (more than one per thread). Every slot written (sentinels), repeat runs bit-equal."""
+    rng = np.random.default_rng(E + T + k)
+    codes, scales = _pool(rng, O.FMT_Q4, E, N, K)
+    q, s = _upload(O.FMT_Q4, codes, scales)
+    idx = vkb.synth_topk(5 + T, T, E, k)
+    if crowd:
+        idx[:, 0] = 3
+        idx[:, 1] = np.where(idx[:, 1] == 3, 4, idx[:, 1])
+    x = rng.uniform(-1, 1, size=(T, K)).astype(np.float16).view(np.uint16)
+    y = _run(O.FMT_Q4, q, s, idx, x, sentinel=-7.0)
+    assert not np.any(y == -7.0)
+    ref, mag, _ = O.moe_ref(codes, scales, idx, x)
+    err, m, n = O.check_error(y, ref, mag)
+    assert err <= 1e-3, (err, m, n)
+    assert np.array_equal(_run(O.FMT_Q4, q, s, idx, x), y)
 
 
 def test_moe_sabotage_fails(cuda):

@@ -243,40 +243,44 @@ template <typename OutT> __device__ __forceinline__ OutT to_out(float v);
 template <> __device__ __forceinline__ __half to_out<__half>(float v) { return __float2half_rn(v); }
 template <> __device__ __forceinline__ float to_out<float>(float v) { return v; }
 
-// ---- MoE routing tables (built by each CTA's producer warp, deterministically: every CTA builds the same) -------
+// ---- MoE routing tables (built by each CTA, deterministically: every CTA builds the same) ------------------------
 //
-// A "segment" is one expert with up to 8 of its (token, slot) pairs: the tokens of one MMA column group. The experts
-// a call routes to are numbered in order of first appearance in the index list ("order ids"); each expert's slots are
-// taken in increasing slot order. Segment order does not change any result (each output row is one tile's sum).
+// A "segment" is one expert with up to 8 of its (token, slot) pairs: the tokens of one MMA column group. Segment order
+// and the order of slots inside an expert change no result -- each output row is one tile's sum, and the MMA's columns
+// are independent, so a slot's value does not depend on the column it lands in -- but every CTA of the grid must build
+// the same segments, since each takes its own range of (segment, row tile) pairs.
 struct MoeTables {
-    int* eid;      // [E_local]     order id of each local expert, -1 before it appears (lists of more than 32 slots)
-    int* ord;      // [nslots]      local expert of each order id
-    int* cnt;      // [nslots]      slots of each order id (lists of more than 32 slots)
-    int* off;      // [nslots + 1]  first position in `slots` of each order id; off[experts seen] = routed slots
-    int* segoff;   // [nslots + 1]  first segment of each order id
-    int* slots;    // [nslots]      slot ids grouped by expert
-    int* seg;      // [nslots]      (order id << 16) | first position in `slots`
-    int* nseg;     // [1]           segments
+    int* slots;    // [nslots]     slot ids grouped by segment
+    int* seg;      // [nslots]     (local expert << 16) | first position in `slots`, per segment
+    int* segc;     // [nslots]     slots of the segment (1-8)
+    int* nseg;     // [2]          segments; (more than 32 slots) the largest load of one expert
+    int* cnt;      // [E_local]    (more than 32 slots) slots per local expert
+    int* off;      // [E_local]    (more than 32 slots) first position of each expert in `slots`
+    int* segoff;   // [E_local]    (more than 32 slots) first segment of each expert
+    int* tmp;      // [nslots]     (more than 32 slots) (local expert << 16) | atomic ticket, or -1
+    int* list;     // [nslots]     (more than 32 slots) slot ids by ticket inside each expert's range
 };
-// the arrays above, in this order: E_local + 4 * nslots + 2 * (nslots + 1) + 1 words
-__host__ __device__ constexpr int moe_table_words(int E_local, int nslots) { return E_local + 6 * nslots + 3; }
+// the arrays above, in this order
+__host__ __device__ constexpr int moe_table_words(int E_local, int nslots) { return 5 * nslots + 3 * E_local + 2; }
 
 __device__ __forceinline__ MoeTables moe_tables(uint8_t* base, int E_local, int nslots) {
     MoeTables t;
     int* p = reinterpret_cast<int*>(base);
-    t.eid = p; p += E_local;
-    t.ord = p; p += nslots;
-    t.cnt = p; p += nslots;
-    t.off = p; p += nslots + 1;
-    t.segoff = p; p += nslots + 1;
     t.slots = p; p += nslots;
     t.seg = p; p += nslots;
-    t.nseg = p;
+    t.segc = p; p += nslots;
+    t.nseg = p; p += 2;
+    t.cnt = p; p += E_local;
+    t.off = p; p += E_local;
+    t.segoff = p; p += E_local;
+    t.tmp = p; p += nslots;
+    t.list = p;
     return t;
 }
 
-// At most 32 slots (one per lane): grouping by __match_any_sync, order ids from a ballot of the group leaders, and one
-// packed warp scan of (slots, segments) over the leaders -- registers only, then the table stores.
+// At most 32 slots, one warp (one slot per lane): grouping by __match_any_sync, experts in order of first appearance
+// from a ballot of the group leaders, one packed warp scan of (slots, segments) over the leaders -- registers only,
+// then the table stores.
 __device__ __forceinline__ void moe_route_small(const QmvArgs& a, MoeTables tb, int lane, int nslots) {
     const unsigned all = 0xffffffffu, below = (1u << lane) - 1u;
     int e = lane < nslots ? __ldg(a.idx + lane) - a.e0 : -1;
@@ -284,7 +288,6 @@ __device__ __forceinline__ void moe_route_small(const QmvArgs& a, MoeTables tb, 
     const unsigned same = __match_any_sync(all, e);
     const int leader = __ffs(same) - 1;
     const bool lead = e >= 0 && lane == leader;
-    const unsigned leaders = __ballot_sync(all, lead);
     const int c = __popc(same), segs = (c + QMV_MAXTOK - 1) / QMV_MAXTOK;
     const int mine = lead ? (c | (segs << 16)) : 0;   // slots in the low half (<= 32), segments in the high half
     int v = mine;
@@ -297,97 +300,105 @@ __device__ __forceinline__ void moe_route_small(const QmvArgs& a, MoeTables tb, 
     const int gexcl = __shfl_sync(all, excl, leader);
     if (e >= 0) tb.slots[(gexcl & 0xFFFF) + __popc(same & below)] = lane;
     if (lead) {
-        const int id = __popc(leaders & below), first = excl & 0xFFFF, s0 = excl >> 16;
-        tb.ord[id] = e;
-        tb.off[id] = first;
-        tb.segoff[id] = s0;
-        for (int k = 0; k < segs; ++k) tb.seg[s0 + k] = (id << 16) | (first + k * QMV_MAXTOK);
+        const int first = excl & 0xFFFF, s0 = excl >> 16;
+        for (int k = 0; k < segs; ++k) {
+            tb.seg[s0 + k] = (e << 16) | (first + k * QMV_MAXTOK);
+            tb.segc[s0 + k] = min(QMV_MAXTOK, c - k * QMV_MAXTOK);
+        }
     }
-    if (lane == 0) {
-        const int seen = __popc(leaders);
-        tb.off[seen] = tot & 0xFFFF;
-        tb.segoff[seen] = tot >> 16;
-        *tb.nseg = tot >> 16;
-    }
+    if (lane == 0) *tb.nseg = tot >> 16;
     __syncwarp();
 }
 
-// Any number of slots: the local expert of every slot staged in `slots`; 32 slots at a time (in slot order) each
-// slot's rank among the earlier slots of its expert, and order ids for the experts met for the first time; exclusive
-// scans of the counts over the order ids; placement; segments.
-__device__ __forceinline__ void moe_route_general(const QmvArgs& a, MoeTables tb, int lane, int nslots) {
+// Any number of slots, by every thread of the CTA (`barrier` synchronises them): counts per local expert by shared
+// atomics, exclusive scans of the counts and of the segments over the experts (one warp), then the slots in index
+// order inside each expert. The atomics' order differs between CTAs while all CTAs must see the same segments, so a
+// slot's place is its count of smaller slot ids of its expert, not its atomic ticket. Up to MOE_SCAN_MAX slots per
+// expert each slot lists itself in its expert's range by the ticket and counts the smaller ids listed there (a few
+// steps for spread routing); past that -- one expert taking most slots -- one warp walks the list from the end in
+// 32-slot chunks, counting each expert down from its load. Both give the same tables. Five barriers; the index list
+// is read once, one load per thread.
+constexpr int MOE_SCAN_MAX = 64;
+
+template <typename Barrier>
+__device__ __forceinline__ void moe_route_cta(const QmvArgs& a, MoeTables tb, int nslots, Barrier barrier) {
+    const int tid = threadIdx.x, nth = blockDim.x, warp = tid >> 5, lane = tid & 31;
     const unsigned all = 0xffffffffu, below = (1u << lane) - 1u;
-    for (int i = lane; i < nslots; i += 32) {
+    for (int e = tid; e < a.E_local; e += nth) tb.cnt[e] = 0;
+    barrier();
+    for (int i = tid; i < nslots; i += nth) {
         const int e = __ldg(a.idx + i) - a.e0;
-        tb.slots[i] = (e < 0 || e >= a.E_local) ? -1 : e;
+        tb.tmp[i] = (e < 0 || e >= a.E_local) ? -1 : (e << 16) | atomicAdd(&tb.cnt[e], 1);
     }
-    for (int e = lane; e < a.E_local; e += 32) tb.eid[e] = -1;
-    __syncwarp();
-    int seen = 0;
-    for (int i0 = 0; i0 < nslots; i0 += 32) {
-        const int i = i0 + lane;
-        const int e = i < nslots ? tb.slots[i] : -1;
-        const unsigned same = __match_any_sync(all, e);
-        const int leader = __ffs(same) - 1;
-        const bool lead = e >= 0 && lane == leader;
-        int id = lead ? tb.eid[e] : 0, base = 0;
-        const bool fresh = lead && id < 0;
-        const unsigned fm = __ballot_sync(all, fresh);
-        if (fresh) {
-            id = seen + __popc(fm & below);
-            tb.eid[e] = id;
-            tb.ord[id] = e;
-        } else if (lead) {
-            base = tb.cnt[id];
-        }
-        if (lead) tb.cnt[id] = base + __popc(same);
-        seen += __popc(fm);
-        id = __shfl_sync(all, id, leader);
-        base = __shfl_sync(all, base, leader);
-        if (i < nslots) tb.seg[i] = e >= 0 ? (id << 16) | (base + __popc(same & below)) : -1;   // (staged rank)
-        __syncwarp();
-    }
-    int run_off = 0, run_seg = 0;
-    for (int b = 0; b < seen; b += 32) {
-        const int id = b + lane;
-        const int c = id < seen ? tb.cnt[id] : 0;
-        const int s = (c + QMV_MAXTOK - 1) / QMV_MAXTOK;
-        int ic = c, is = s;
+    barrier();
+    if (warp == 0) {
+        int run_off = 0, run_seg = 0, cmax = 0;
+        for (int b = 0; b < a.E_local; b += 32) {
+            const int e = b + lane;
+            const int c = e < a.E_local ? tb.cnt[e] : 0;
+            const int s = (c + QMV_MAXTOK - 1) / QMV_MAXTOK;
+            int ic = c, is = s;
 #pragma unroll
-        for (int d = 1; d < 32; d <<= 1) {
-            const int vc = __shfl_up_sync(all, ic, d);
-            const int vs = __shfl_up_sync(all, is, d);
-            if (lane >= d) { ic += vc; is += vs; }
+            for (int d = 1; d < 32; d <<= 1) {
+                const int vc = __shfl_up_sync(all, ic, d);
+                const int vs = __shfl_up_sync(all, is, d);
+                if (lane >= d) { ic += vc; is += vs; }
+            }
+            if (e < a.E_local) {
+                tb.off[e] = run_off + ic - c;
+                tb.segoff[e] = run_seg + is - s;
+            }
+            run_off += __shfl_sync(all, ic, 31);
+            run_seg += __shfl_sync(all, is, 31);
+            cmax = max(cmax, c);
         }
-        if (id < seen) {
-            tb.off[id] = run_off + ic - c;
-            tb.segoff[id] = run_seg + is - s;
+        cmax = __reduce_max_sync(all, cmax);
+        if (lane == 0) {
+            tb.nseg[0] = run_seg;
+            tb.nseg[1] = cmax;
         }
-        run_off += __shfl_sync(all, ic, 31);
-        run_seg += __shfl_sync(all, is, 31);
     }
-    if (lane == 0) {
-        tb.off[seen] = run_off;
-        tb.segoff[seen] = run_seg;
-        *tb.nseg = run_seg;
+    barrier();
+    const bool scan = tb.nseg[1] <= MOE_SCAN_MAX;
+    if (scan) {
+        for (int i = tid; i < nslots; i += nth) {
+            const int v = tb.tmp[i];
+            if (v >= 0) tb.list[tb.off[v >> 16] + (v & 0xFFFF)] = i;
+        }
     }
-    __syncwarp();
-    for (int i = lane; i < nslots; i += 32) {
-        const int v = tb.seg[i];
-        if (v >= 0) tb.slots[tb.off[v >> 16] + (v & 0xFFFF)] = i;
+    for (int e = tid; e < a.E_local; e += nth) {
+        const int c = tb.cnt[e], first = tb.off[e], s0 = tb.segoff[e];
+        for (int k = 0; k * QMV_MAXTOK < c; ++k) {
+            tb.seg[s0 + k] = (e << 16) | (first + k * QMV_MAXTOK);
+            tb.segc[s0 + k] = min(QMV_MAXTOK, c - k * QMV_MAXTOK);
+        }
     }
-    __syncwarp();
-    for (int id = lane; id < seen; id += 32) {
-        const int first = tb.off[id], n = tb.off[id + 1] - first, s0 = tb.segoff[id];
-        for (int k = 0; k * QMV_MAXTOK < n; ++k) tb.seg[s0 + k] = (id << 16) | (first + k * QMV_MAXTOK);
+    barrier();
+    if (scan) {
+        for (int i = tid; i < nslots; i += nth) {
+            const int v = tb.tmp[i];
+            if (v < 0) continue;
+            const int first = tb.off[v >> 16], c = tb.cnt[v >> 16];
+            int r = 0;
+            for (int j = 0; j < c; ++j) r += tb.list[first + j] < i;
+            tb.slots[first + r] = i;
+        }
+    } else if (warp == 0) {
+        for (int i0 = (nslots - 1) & ~31; i0 >= 0; i0 -= 32) {   // (cnt becomes a countdown cursor)
+            const int i = i0 + lane;
+            const int e = i < nslots ? tb.tmp[i] >> 16 : -1;   // (-1 >> 16 == -1)
+            const unsigned same = __match_any_sync(all, e);
+            const int leader = __ffs(same) - 1;
+            int base = 0;
+            if (e >= 0 && lane == leader) {
+                base = tb.cnt[e] - __popc(same);
+                tb.cnt[e] = base;
+            }
+            base = __shfl_sync(all, base, leader);
+            if (e >= 0) tb.slots[tb.off[e] + base + __popc(same & below)] = i;
+        }
     }
-    __syncwarp();
-}
-
-__device__ __forceinline__ void moe_route_warp(const QmvArgs& a, MoeTables tb, int lane) {
-    const int nslots = a.T * a.topk;
-    if (nslots <= 32) moe_route_small(a, tb, lane, nslots);
-    else moe_route_general(a, tb, lane, nslots);
+    barrier();
 }
 
 // ---- expert-parallel MoE with peer stores: the push of a CTA's outputs ---------------------------------------------
@@ -412,8 +423,7 @@ __device__ __noinline__ void qmv_moe_push(const QmvArgs& a, MoeTables tb, int w0
             const int tb_ = min(w1, (sg + 1) * a.tilesN) - sg * a.tilesN;
             const int n0 = ta * QMV_ROWS, n1 = min(a.N, tb_ * QMV_ROWS);
             if (n1 <= n0) continue;
-            const int first = tb.seg[sg] & 0xFFFF, id = tb.seg[sg] >> 16;
-            const int cnt = min(QMV_MAXTOK, tb.off[id + 1] - first);
+            const int first = tb.seg[sg] & 0xFFFF, cnt = tb.segc[sg];
             const size_t off0 = (size_t)n0 * sizeof(OutT);
             p2p_push(a.pp, cnt, (n1 - n0) * (int)sizeof(OutT), rowp | off0,
                      [&](int r) { return (size_t)tb.slots[first + r] * rowp + off0; }, threadIdx.x, QMV_NW * 32);
@@ -514,9 +524,11 @@ qmv_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUten
     MoeTables tb{};
     if constexpr (MOE) {
         // the producer warp: barriers, then -- after the dependency, since the previous grid may have written the
-        // index list and the activations -- the resident token rows and the routing tables. The consumers wait for
-        // the tables; the producer goes on to the weight stream without waiting for them.
-        tb = moe_tables(sm + a.moe_off, a.E_local, a.T * a.topk);
+        // index list and the activations -- the resident token rows. Up to 32 slots it also builds the routing
+        // tables alone and goes on to the weight stream while the consumers wait for them; more slots are routed by
+        // the whole CTA.
+        const int nslots = a.T * a.topk;
+        tb = moe_tables(sm + a.moe_off, a.E_local, nslots);
         if (warp == QMV_NW) {
             if (lane == 0) {
                 prefetch_tmap(&tq);   // (the descriptors' fetch overlaps the dependency wait and the routing)
@@ -529,10 +541,16 @@ qmv_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUten
                 for (int j = 0; j < a.T; ++j)
                     bulk_load(xbuf + j * a.xpitch, a.x + (size_t)j * a.K, (uint32_t)(a.K * 2), &xfull[0]);
             }
-            moe_route_warp(a, tb, lane);
-            named_arrive(2, 32 * (QMV_NW + 1));
+            if (nslots <= 32) moe_route_small(a, tb, lane, nslots);
+        } else if (nslots > 32) {
+            pdl_wait();
+        }
+        if (nslots <= 32) {
+            // one warp routed: the producer goes on to the weight stream at once
+            if (warp == QMV_NW) named_arrive(2, 32 * (QMV_NW + 1));
+            else named_sync(2, 32 * (QMV_NW + 1));
         } else {
-            named_sync(2, 32 * (QMV_NW + 1));
+            moe_route_cta(a, tb, nslots, [] { __syncthreads(); });
         }
     } else {
         if (threadIdx.x == 0) init_bars(a.wg);
@@ -551,13 +569,13 @@ qmv_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUten
 
     // segment accessors: expert (weight row base), token count, and the slot (dense: token) of column j
     auto seg_expert = [&](int sg) -> int {
-        if constexpr (MOE) return tb.ord[tb.seg[sg] >> 16]; else return 0;
+        if constexpr (MOE) return tb.seg[sg] >> 16; else return 0;
     };
     auto seg_first = [&](int sg) -> int {
         if constexpr (MOE) return tb.seg[sg] & 0xFFFF; else return 0;
     };
     auto seg_count = [&](int sg) -> int {
-        if constexpr (MOE) return min(QMV_MAXTOK, tb.off[(tb.seg[sg] >> 16) + 1] - seg_first(sg));
+        if constexpr (MOE) return tb.segc[sg];
         else return a.T;
     };
     auto seg_slot = [&](int sg, int j) -> int {
