@@ -144,10 +144,14 @@ __device__ __forceinline__ void load_a(uint32_t a, int t, uint32_t (&r)[4]) {
 
 // The B registers (two k16 steps) of this thread's token for the group whose activations start at shared address xa
 // (xa already includes the thread's t offset). Padding token columns read a real row: their MMA columns are never
-// stored, and the MMA keeps columns independent.
-template <int F>
+// stored, and the MMA keeps columns independent. PX: the rows are staged in fragment order (stage_x_chunk), so the
+// four registers are one 16-byte load; otherwise they are in k order and permuted here.
+template <int F, bool PX>
 __device__ __forceinline__ void load_b(uint32_t xa, uint32_t (&b)[4]) {
-    if constexpr (F == FMT_Q2) {
+    if constexpr (PX) {
+        const uint4 v = lds128(xa);
+        b[0] = v.x; b[1] = v.y; b[2] = v.z; b[3] = v.w;
+    } else if constexpr (F == FMT_Q2) {
         const uint2 xa0 = lds64(xa), xb0 = lds64(xa + 16);
         b[0] = prmt(xa0.x, xb0.x, 0x5410u);   // (x0, x8)
         b[1] = prmt(xa0.x, xb0.x, 0x7632u);   // (x1, x9)
@@ -167,19 +171,46 @@ __device__ __forceinline__ void load_b(uint32_t xa, uint32_t (&b)[4]) {
 }
 
 // Per-thread byte offset of its activations inside a 32-value group (see load_b).
-template <int F>
+template <int F, bool PX>
 __device__ __forceinline__ uint32_t x_lane_off(int t) {
-    if constexpr (F == FMT_Q2) return 32 * (t >> 1) + 8 * (t & 1);
+    if constexpr (F == FMT_Q2 && !PX) return 32 * (t >> 1) + 8 * (t & 1);
     else return 16 * t;
 }
 
+// Fragment-order staging: 16-byte chunk c of a staged row is lane-in-quad (c & 3)'s four B registers of group c / 4,
+// built from 8 activations in k order (lo, hi: f16x2 words 0-1 and 2-3 of the format's source pairs). Q4 takes
+// activations 8c..8c+7 and pairs (x0,x4) (x1,x5) (x2,x6) (x3,x7); Q2 takes 4 of each half of its 16-value block
+// (block c / 2, offset 4 (c & 1)) and pairs (x0,x8) (x1,x9) (x2,x10) (x3,x11); Q8 keeps k order.
+template <int F>
+__device__ __forceinline__ uint4 frag_order(uint2 lo, uint2 hi) {
+    if constexpr (F == FMT_Q8) return make_uint4(lo.x, lo.y, hi.x, hi.y);
+    else return make_uint4(prmt(lo.x, hi.x, 0x5410u), prmt(lo.x, hi.x, 0x7632u), prmt(lo.y, hi.y, 0x5410u),
+                           prmt(lo.y, hi.y, 0x7632u));
+}
+// element offset, in a [K] row, of chunk c's first 4 source activations; the other 4 are chunk_hi further
+template <int F>
+__device__ __forceinline__ int chunk_src(int c) {
+    if constexpr (F == FMT_Q2) return 16 * (c >> 1) + 4 * (c & 1);
+    else return 8 * c;
+}
+template <int F>
+__device__ __forceinline__ constexpr int chunk_hi() { return F == FMT_Q2 ? 8 : 4; }
+
+// Dense calls with more activations than this (tokens x K) use the XB kernels: their rows come in by the producer's
+// bulk copy in k order and the consumers permute each group's registers as they load them; smaller ones are loaded
+// by the consumer threads themselves, in fragment order. Measured on B200 (µs, 50-call graphs): 8 x 6144 activations
+// staged by the consumers took 2048x6144 2-bit from 4.7 to 5.7 and Q8 from 6.05 to 6.6, while 2 x 6144 took Q4
+// 2560x6144 from 6.2 to 5.6; permuting the bulk copy in place once was slower than both (shared-memory traffic), and
+// one kernel holding both loops ran both slower than the single-loop kernels.
+constexpr int QMV_XSTAGE_MAX = 16384;
+
 // One group: two k16 MMAs into a fresh fragment, then the per-row fp32 scales. ca: row g's codes in the stage;
 // row g+8 is 8 * cp further.
-template <int F>
+template <int F, bool PX>
 __device__ __forceinline__ void qmv_group(uint32_t ca, uint32_t cp, int G, int t, uint32_t xa, float s0, float s1,
                                           float (&acc)[4]) {
     uint32_t b[4], ar[4], ar8[4];
-    load_b<F>(xa, b);
+    load_b<F, PX>(xa, b);
     const uint32_t a = ca + code_off<F>(G, t);
     load_a<F>(a, t, ar);
     load_a<F>(a + 8 * cp, t, ar8);
@@ -197,14 +228,14 @@ __device__ __forceinline__ void qmv_group(uint32_t ca, uint32_t cp, int G, int t
 //   sc, sp: shared address of row g's scales in the stage, scale row pitch
 //   xa:     shared address of this thread's activations for stage-local group 0
 // U: groups per loop iteration (2, or 4 where the register budget allows: four independent MMA chains in flight).
-template <int F, int U = 2>
+template <int F, int U, bool PX>
 __device__ __forceinline__ void consume_stage(uint32_t ca, uint32_t cp, uint32_t sc, uint32_t sp, int G0, int G1,
                                               uint32_t xa, int t, float (&acc)[4]) {
     int G = G0;
     if (G & 1) {   // odd start: single group, its scale from the aligned pair
         if (G < G1) {
             const uint32_t p0 = lds32(sc + 2 * (G - 1)), p1 = lds32(sc + 8 * sp + 2 * (G - 1));
-            qmv_group<F>(ca, cp, G, t, xa + 64 * G, half_hi_f32(p0), half_hi_f32(p1), acc);
+            qmv_group<F, PX>(ca, cp, G, t, xa + 64 * G, half_hi_f32(p0), half_hi_f32(p1), acc);
         }
         ++G;
     }
@@ -213,21 +244,21 @@ __device__ __forceinline__ void consume_stage(uint32_t ca, uint32_t cp, uint32_t
         for (; G + 3 < G1; G += 4) {
             const uint32_t p0 = lds32(sc + 2 * G), p1 = lds32(sc + 8 * sp + 2 * G);
             const uint32_t q0 = lds32(sc + 2 * G + 4), q1 = lds32(sc + 8 * sp + 2 * G + 4);
-            qmv_group<F>(ca, cp, G, t, xa + 64 * G, half_lo_f32(p0), half_lo_f32(p1), acc);
-            qmv_group<F>(ca, cp, G + 1, t, xa + 64 * (G + 1), half_hi_f32(p0), half_hi_f32(p1), acc);
-            qmv_group<F>(ca, cp, G + 2, t, xa + 64 * (G + 2), half_lo_f32(q0), half_lo_f32(q1), acc);
-            qmv_group<F>(ca, cp, G + 3, t, xa + 64 * (G + 3), half_hi_f32(q0), half_hi_f32(q1), acc);
+            qmv_group<F, PX>(ca, cp, G, t, xa + 64 * G, half_lo_f32(p0), half_lo_f32(p1), acc);
+            qmv_group<F, PX>(ca, cp, G + 1, t, xa + 64 * (G + 1), half_hi_f32(p0), half_hi_f32(p1), acc);
+            qmv_group<F, PX>(ca, cp, G + 2, t, xa + 64 * (G + 2), half_lo_f32(q0), half_lo_f32(q1), acc);
+            qmv_group<F, PX>(ca, cp, G + 3, t, xa + 64 * (G + 3), half_hi_f32(q0), half_hi_f32(q1), acc);
         }
     }
 #pragma unroll 1
     for (; G + 1 < G1; G += 2) {
         const uint32_t p0 = lds32(sc + 2 * G), p1 = lds32(sc + 8 * sp + 2 * G);
-        qmv_group<F>(ca, cp, G, t, xa + 64 * G, half_lo_f32(p0), half_lo_f32(p1), acc);
-        qmv_group<F>(ca, cp, G + 1, t, xa + 64 * (G + 1), half_hi_f32(p0), half_hi_f32(p1), acc);
+        qmv_group<F, PX>(ca, cp, G, t, xa + 64 * G, half_lo_f32(p0), half_lo_f32(p1), acc);
+        qmv_group<F, PX>(ca, cp, G + 1, t, xa + 64 * (G + 1), half_hi_f32(p0), half_hi_f32(p1), acc);
     }
     if (G < G1) {
         const uint32_t p0 = lds32(sc + 2 * G), p1 = lds32(sc + 8 * sp + 2 * G);
-        qmv_group<F>(ca, cp, G, t, xa + 64 * G, half_lo_f32(p0), half_lo_f32(p1), acc);
+        qmv_group<F, PX>(ca, cp, G, t, xa + 64 * G, half_lo_f32(p0), half_lo_f32(p1), acc);
     }
 }
 
@@ -455,14 +486,16 @@ __host__ __device__ constexpr int qmv_nbars(int nstage) { return 2 * nstage + 4 
 // cannot start before their dependency anyway (the index list decides the weights) -- use MINB = 1: no spills, and
 // registers for four MMA chains per loop iteration (measured on B200: 8 experts of 512x2048, 8 tokens 13.7 us against
 // 14.7; dense 12288x2560 Q4 1 token 8.0 us against 9.1).
-// XF32: the activations arrive as fp32 (the reference's fp32-in decode entry). After the dependency wait the consumer
-// warps read them from global memory (16-byte loads), round them to fp16 (round to nearest even, the reference's
-// conversion) straight into the fp16 activation buffer and complete its barrier themselves: no conversion launch,
-// no extra shared memory, and the MMA path is the fp16 one.
-template <int F, int MODE, typename OutT, bool XF32 = false, int MINB = 2>
+// XF32: the activations arrive as fp32 (the reference's fp32-in decode entry). The consumer warps stage every dense
+// and gate/up call's activations themselves after the dependency wait; these they round to fp16 on the way (round to
+// nearest even, the reference's conversion): no conversion launch, no extra shared memory, and the MMA path is the
+// fp16 one.
+// XB: a dense fp16-in call whose activations come in by the producer's bulk copy (QMV_XSTAGE_MAX).
+template <int F, int MODE, typename OutT, bool XF32 = false, int MINB = 2, bool XB = false>
 __global__ void __launch_bounds__(32 * (QMV_NW + 1), MINB)
 qmv_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap ts, const __grid_constant__ QmvArgs a) {
     static_assert(!XF32 || MODE == QMV_DENSE || MODE == QMV_GLU, "fp32 activations: dense and gate/up calls");
+    static_assert(!XB || (MODE == QMV_DENSE && !XF32), "bulk-copied activations: dense fp16-in calls");
     static_assert(MINB == 2 || (MODE != QMV_GLU && !XF32), "one-CTA register budget: dense fp16-in and MoE calls");
     constexpr bool GLU = MODE == QMV_GLU;
     constexpr bool MOE = MODE == QMV_MOE || MODE == QMV_MOE_P2P;
@@ -582,6 +615,9 @@ qmv_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUten
         if constexpr (MOE) return tb.slots[seg_first(sg) + j]; else return j;
     };
 
+    // dense and gate/up calls: the consumers load the activations themselves (see their staging), unless XB
+    constexpr bool xdirect = !MOE && !XB;
+
     constexpr int BITS = FmtTraits<F>::BITS;
     const int ksb = a.KS * BITS / 8;                                          // code bytes per row per stage
     const uint32_t stage_tx = (uint32_t)(QMV_ROWS * (a.cpitch + a.spitch));   // both boxes, pads included
@@ -637,15 +673,15 @@ qmv_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUten
                 int xsg = fdiv(w0, a.dv_tiles), xtile = w0 - xsg * a.tilesN;
                 for (int it = 0; it < pre && ok; it += a.nchunks) {
                     if (xsg != last_seg) {
-                        if constexpr (!XF32) issue_x(xsg);   // XF32: the consumers fill the buffer
+                        if (!xdirect) issue_x(xsg);   // (else the consumers load the activations)
                         last_seg = xsg;
                     }
                     if (++xtile == a.tilesN) { xtile = 0; ++xsg; }
                 }
             }
             for (int it = pre; it < total_it && ok; ++it) {
-                if (c == 0 && sg != last_seg) {   // dense and gate/up calls have one segment: never for XF32
-                    if constexpr (!XF32) issue_x(sg);
+                if (c == 0 && sg != last_seg) {   // (dense and gate/up calls have one segment)
+                    if (MOE) issue_x(sg);
                     last_seg = sg;
                     if (!ok) break;
                 }
@@ -690,27 +726,57 @@ qmv_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUten
     // x and y may still be written (or y read) by the previous grid. MoE: the producer's wait, which the consumers
     // are ordered after by the routing barrier, has already established that for the whole grid.
     if constexpr (!MOE) pdl_wait();
-    if constexpr (XF32) {   // fp32 activations -> the fp16 buffer of segment 0, then its barrier (count 1, no bytes)
-        const int K4 = a.K / 4;
-        const float4* xf = reinterpret_cast<const float4*>(a.x);
-        for (int i = threadIdx.x; i < K4; i += QMV_NW * 32) {   // every token's 4 values at i: loads first
-            float4 v[QMV_MAXTOK];
+    if constexpr (xdirect) {
+        // dense and gate/up calls: the consumers stage the token rows themselves, in fragment order (frag_order), so
+        // that every group's B registers are one 16-byte load; fp32 activations are rounded to fp16 on the way (round
+        // to nearest even, the reference's conversion). Items = (token, 16-byte chunk) pairs over the consumer
+        // threads, coalesced; each thread keeps R items' loads in flight (one round for QMV_XSTAGE_MAX values). Then
+        // one barrier. (Measured on B200 against the producer's bulk copy with the permutation in every group's load:
+        // 8192x2048 Q4 1 token 4.6 -> 4.1-4.4 us.)
+        constexpr int R = XF32 ? 4 : (MINB == 1 ? 8 : 4);
+        const int nch = a.K / 8, items = a.T * nch;
+        int m = 0, c = threadIdx.x;   // item threadIdx.x: token m, chunk c
+        while (c >= nch) { c -= nch; ++m; }
+        for (int i = threadIdx.x; i < items; i += R * QMV_NW * 32) {
+            uint32_t dst[R];
+            uint2 lo[R], hi[R];
+            float4 f0[XF32 ? R : 1], f1[XF32 ? R : 1];
 #pragma unroll
-            for (int m = 0; m < QMV_MAXTOK; ++m)
-                if (m < a.T) v[m] = xf[(size_t)m * K4 + i];
-#pragma unroll
-            for (int m = 0; m < QMV_MAXTOK; ++m) {
-                if (m < a.T) {
-                    const uint32_t lo = cvt_h2(__float_as_uint(v[m].x), __float_as_uint(v[m].y));
-                    const uint32_t hi = cvt_h2(__float_as_uint(v[m].z), __float_as_uint(v[m].w));
-                    asm volatile("st.shared.v2.b32 [%0], {%1, %2};" ::"r"(xbuf_s + (uint32_t)(m * a.xpitch + 8 * i)),
-                                 "r"(lo), "r"(hi)
-                                 : "memory");
+            for (int r = 0; r < R; ++r) {   // the loads
+                dst[r] = 0xFFFFFFFFu;
+                if (i + r * QMV_NW * 32 < items) {
+                    const int e0 = chunk_src<F>(c), e1 = e0 + chunk_hi<F>();
+                    dst[r] = xbuf_s + (uint32_t)(m * a.xpitch + 16 * c);
+                    if constexpr (XF32) {
+                        const float* row = reinterpret_cast<const float*>(a.x) + (size_t)m * a.K;
+                        f0[r] = __ldcg(reinterpret_cast<const float4*>(row + e0));
+                        f1[r] = __ldcg(reinterpret_cast<const float4*>(row + e1));
+                    } else if constexpr (F == FMT_Q2) {
+                        const __half* row = a.x + (size_t)m * a.K;
+                        lo[r] = __ldcg(reinterpret_cast<const uint2*>(row + e0));
+                        hi[r] = __ldcg(reinterpret_cast<const uint2*>(row + e1));
+                    } else {   // (e1 = e0 + 4: one 16-byte load)
+                        const uint4 v = __ldcg(reinterpret_cast<const uint4*>(a.x + (size_t)m * a.K + e0));
+                        lo[r] = make_uint2(v.x, v.y);
+                        hi[r] = make_uint2(v.z, v.w);
+                    }
+                    c += QMV_NW * 32;
+                    while (c >= nch) { c -= nch; ++m; }
                 }
+            }
+#pragma unroll
+            for (int r = 0; r < R; ++r) {   // fragment order and the stores
+                if (dst[r] == 0xFFFFFFFFu) continue;
+                if constexpr (XF32) {
+                    lo[r] = make_uint2(cvt_h2(__float_as_uint(f0[r].x), __float_as_uint(f0[r].y)),
+                                       cvt_h2(__float_as_uint(f0[r].z), __float_as_uint(f0[r].w)));
+                    hi[r] = make_uint2(cvt_h2(__float_as_uint(f1[r].x), __float_as_uint(f1[r].y)),
+                                       cvt_h2(__float_as_uint(f1[r].z), __float_as_uint(f1[r].w)));
+                }
+                sts128(dst[r], frag_order<F>(lo[r], hi[r]));
             }
         }
         named_sync(1, QMV_NW * 32);
-        if (threadIdx.x == 0) mbar_arrive(&xfull[0]);
     }
     if constexpr (MODE == QMV_MOE_P2P) {   // peer stores: this rank's copy may be written from now on
         if (warp == 0 && lane == 0) p2p_post_ready(a.pp, p2p_epoch(a.pp));
@@ -763,7 +829,10 @@ qmv_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUten
     int ntile = 0;   // tiles this group has done (reduction buffer parity / reducer rotation)
     for (int tl = grp; tl < ntl && ok; tl += WG, ++ntile) {
         if (sg - first_seg != jn - 1 || !held) {
-            if (xres) {   // resident token rows: wait for them once
+            if (xdirect) {   // staged by the consumers above, before their barrier
+                held = true;
+                jn = 1;
+            } else if (xres) {   // resident token rows: wait for them once
                 if (!held && !cwait(&xfull[0], 0)) { ok = false; break; }
                 held = true;
                 jn = sg - first_seg + 1;
@@ -776,7 +845,7 @@ qmv_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUten
             const int col = g < cnt ? g : 0;
             int xr = col;   // staged row of this thread's column
             if constexpr (MOE) if (xres) xr = fdiv(seg_slot(sg, col), a.dv_topk);
-            xrow = xbuf_s + (uint32_t)((xb * a.xrows + xr) * a.xpitch) + x_lane_off<F>(t);
+            xrow = xbuf_s + (uint32_t)((xb * a.xrows + xr) * a.xpitch) + x_lane_off<F, xdirect>(t);
         }
         float acc[4] = {0.f, 0.f, 0.f, 0.f};
         int kc = 0;
@@ -787,8 +856,9 @@ qmv_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUten
             // four groups per iteration with the one-CTA register budget and in dense calls (measured on B200 under
             // the 56-register cap: 8192x2048 Q4 1 token 4.59 -> 4.44 us; two groups stay for gate/up, whose two-
             // and four-token calls got 8% slower, and for two-CTA MoE)
-            consume_stage<F, (MINB == 1 || MODE == QMV_DENSE) ? 4 : 2>(st + c_row, cp, st + s_row, sp, G0, G1,
-                                                                      xrow + (uint32_t)(kc * 64), t, acc);
+            constexpr int U = (MINB == 1 || MODE == QMV_DENSE) ? 4 : 2;
+            const uint32_t xa = xrow + (uint32_t)(kc * 64);
+            consume_stage<F, U, xdirect>(st + c_row, cp, st + s_row, sp, G0, G1, xa, t, acc);
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[stg]);
             if (++stg == a.nstage) { stg = 0; ++rnd; }
@@ -864,7 +934,7 @@ qmv_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUten
         while (stg >= a.nstage) { stg -= a.nstage; ++rnd; }
     }
     // release the rest of the CTA's segments (also those this group had no tile in)
-    if (!xres) {
+    if (!xdirect && !xres) {
         if (ok) ok = enter_upto(last_seg - first_seg);
         leave();
     }

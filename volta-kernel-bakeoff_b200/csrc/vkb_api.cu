@@ -244,10 +244,10 @@ static bool plan_qmv(int fmt, int N, int K, int xrows, int moe_slots, int E_loca
     return true;
 }
 
-template <int F, int MODE, typename OutT, bool XF32 = false, int MINB = 2>
+template <int F, int MODE, typename OutT, bool XF32 = false, int MINB = 2, bool XB = false>
 static int launch_qmv(const QmvPlan& p, const CUtensorMap& tq, const CUtensorMap& ts, int grid, cudaStream_t st,
                       int dev) {
-    auto kern = qmv_kernel<F, MODE, OutT, XF32, MINB>;
+    auto kern = qmv_kernel<F, MODE, OutT, XF32, MINB, XB>;
     static std::once_flag once[kMaxDevices];
     static cudaError_t attr_err[kMaxDevices];
     std::call_once(once[dev], [&] {
@@ -387,9 +387,13 @@ static int qmv_entry(const void* q, const void* s, const void* x, void* y, bool 
             return f32 ? launch_qmv<F, QMV_MOE, float, false, 1>(p, tq, ts, grid, st, dev)
                        : launch_qmv<F, QMV_MOE, __half, false, 1>(p, tq, ts, grid, st, dev);
         }
-        if (2 * (p.smem + 1024) > d.smem_per_sm)   // one CTA per SM: the 96-register variant
+        if (2 * (p.smem + 1024) > d.smem_per_sm) {   // one CTA per SM: the 96-register variant
+            if ((long long)M * K > QMV_XSTAGE_MAX)       // activations by bulk copy
+                return f32 ? launch_qmv<F, QMV_DENSE, float, false, 1, true>(p, tq, ts, grid, st, dev)
+                           : launch_qmv<F, QMV_DENSE, __half, false, 1, true>(p, tq, ts, grid, st, dev);
             return f32 ? launch_qmv<F, QMV_DENSE, float, false, 1>(p, tq, ts, grid, st, dev)
                        : launch_qmv<F, QMV_DENSE, __half, false, 1>(p, tq, ts, grid, st, dev);
+        }
         return f32 ? launch_qmv<F, QMV_DENSE, float>(p, tq, ts, grid, st, dev)
                    : launch_qmv<F, QMV_DENSE, __half>(p, tq, ts, grid, st, dev);
     }
