@@ -17,14 +17,15 @@
 //     bytes inside it). Few, large TMA requests are what keep HBM busy: 16-row x 128-byte boxes ran at under half
 //     the bandwidth of these on B200. The weight stages are issued
 //     before griddepcontrol.wait, so under programmatic dependent launch the next call's weight stream overlaps the
-//     previous call's tail. The activations (after the wait) come in as 1-D bulk copies.
+//     previous call's tail. The activations (after the wait): dense calls' small blocks are loaded by the consumers
+//     themselves in fragment order (see QMV_XSTAGE_MAX); larger blocks and MoE segments come in as 1-D bulk copies.
 //   * warps 0..NW-1 split each stage's K range and run the m16n8k16 tensor-core MMA with the weights as A (16 rows)
 //     and the tokens as B (8 columns). The codes enter the MMA exactly: the fp16 magic-number trick (0x6400 | n is
 //     the half 1024 + n) turns two codes into one f16x2 with one LOP3 and one HSUB2/HFMA2, and every 32-value group is
 //     accumulated on its own (two k16 steps) and then scaled in fp32, so the result is the exact-code fp32-sum class
 //     of the reference's fused kernels (tolerance 1e-4 of sum|x*w|), not the fp16-rounded-weight class.
 //   * inside one k16 step the order of k is free as long as A and B agree; each format picks the order that makes its
-//     unpack cheapest and permutes the activations to match with PRMT.
+//     unpack cheapest, and the activations are either staged in that order or permuted to match with PRMT as loaded.
 //   * per-tile partial sums of the NW warps are added in shared memory and written by warp 0.
 #pragma once
 
