@@ -666,6 +666,18 @@ qmv_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUten
                 }
                 ++xsegs;
             };
+            if constexpr (xdirect) {
+                // the activations into L2 while the previous grid runs (see bulk_prefetch_l2), each 128-byte line by
+                // one CTA: every CTA prefetching all of them cost more L2 bandwidth than the latency saved. Measured
+                // on B200 (50-call graphs, weights cycled over 4x L2): 8192x2048 Q4 1 token 4.40 -> 3.97 us; the
+                // configs[1] cases unchanged in sum, larger blocks (the XB kernels) 1.5-2% slower, so not there
+                // either
+                const uint32_t total = (uint32_t)(a.T * a.K * (XF32 ? 4 : 2));
+                const uint32_t piece = ((total + gridDim.x - 1) / gridDim.x + 127u) & ~127u;
+                const uint32_t off = blockIdx.x * piece;
+                if (off < total)
+                    bulk_prefetch_l2(reinterpret_cast<const uint8_t*>(a.x) + off, min(piece, total - off));
+            }
             for (int i = 0; i < pre; ++i) issue_w();   // the weights do not depend on the previous grid
             pdl_wait();                                // the activations may
             // activations of the segments the prefetched stages belong to, in order
