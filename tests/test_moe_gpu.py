@@ -92,7 +92,7 @@ def test_moe_few_tokens_with_repeated_experts(cuda, fmt, T):
     assert err <= 1e-3, (err, m, n)
 
 
-@pytest.mark.parametrize("T", [2, 8])   # 16 slots (the one-slot-per-lane routing) and 64
+@pytest.mark.parametrize("T", [2, 8, 20])   # 16 slots (the one-slot-per-lane routing), 64 (chunked), 160 (CTA-wide)
 def test_moe_expert_parallel_subsets(cuda, T):
     """Four ranks' worth of pools (32 experts each) fill disjoint slots; their union is the full result, and a pool
     never touches slots routed elsewhere (sentinels)."""
@@ -116,12 +116,16 @@ def test_moe_expert_parallel_subsets(cuda, T):
     assert err <= 1e-3, (err, m, n)
 
 
-@pytest.mark.parametrize("T,k", [(4, 8), (11, 3), (2, 16)])
+@pytest.mark.parametrize("T,k", [(4, 8), (11, 3), (2, 16), (16, 8), (100, 1), (43, 3)])
 def test_moe_routing_boundaries(cuda, T, k):
-    """32 slots (the largest list routed one slot per lane), 33 slots over 11 tokens (the CTA-wide routing with the
-    per-segment activation rows), and 16 slots over 2 tokens with experts repeated across and inside tokens."""
+    """32 slots (the largest list routed one slot per lane), 33 slots over 11 tokens (the smallest list the one-warp
+    router takes in 32-slot chunks, with the per-segment activation rows), 16 slots over 2 tokens with experts
+    repeated across and inside tokens, 128 slots (the largest chunked list), 100 one-slot tokens on 9 experts (several
+    segments per expert, experts spread over all four chunks), and 129 slots (the CTA-wide routing). 64 row tiles per
+    expert put these lists on the two-CTA kernel instances (the host's bound gives CTAs 4 or more tiles); the smaller
+    pools of the other tests take the one-CTA instances, which route the same way."""
     rng = np.random.default_rng(70 + T * k)
-    E, N, K = 9, 48, 512
+    E, N, K = 9, 1024, 512
     codes, scales = _pool(rng, O.FMT_Q4, E, N, K)
     q, s = _upload(O.FMT_Q4, codes, scales)
     idx = rng.integers(0, E, size=(T, k)).astype(np.int32)
@@ -135,7 +139,7 @@ def test_moe_routing_boundaries(cuda, T, k):
 @pytest.mark.parametrize("E,N,K,T,k,crowd", [(16, 1040, 512, 96, 2, True), (1000, 64, 256, 64, 8, False),
                                                (40, 520, 512, 600, 1, False)])
 def test_moe_cta_routing(cuda, E, N, K, T, k, crowd):
-    """Lists of more than 32 slots are routed by the whole CTA, and every CTA must build the same segments: one expert
+    """Lists of more than 128 slots are routed by the whole CTA, and every CTA must build the same segments: one expert
     taking 96+ slots (past the per-slot count, the one-warp countdown), 1000 local experts (several passes of the
     expert scan), and 600 slots (more than one per thread). Every slot written (sentinels), repeat runs bit-equal."""
     rng = np.random.default_rng(E + T + k)

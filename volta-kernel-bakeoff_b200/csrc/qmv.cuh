@@ -285,12 +285,12 @@ struct MoeTables {
     int* slots;    // [nslots]     slot ids grouped by segment
     int* seg;      // [nslots]     (local expert << 16) | first position in `slots`, per segment
     int* segc;     // [nslots]     slots of the segment (1-8)
-    int* nseg;     // [2]          segments; (more than 32 slots) the largest load of one expert
+    int* nseg;     // [2]          segments; (CTA-wide routing) the largest load of one expert
     int* cnt;      // [E_local]    (more than 32 slots) slots per local expert
     int* off;      // [E_local]    (more than 32 slots) first position of each expert in `slots`
-    int* segoff;   // [E_local]    (more than 32 slots) first segment of each expert
-    int* tmp;      // [nslots]     (more than 32 slots) (local expert << 16) | atomic ticket, or -1
-    int* list;     // [nslots]     (more than 32 slots) slot ids by ticket inside each expert's range
+    int* segoff;   // [E_local]    (CTA-wide routing) first segment of each expert
+    int* tmp;      // [nslots]     (CTA-wide routing) (local expert << 16) | atomic ticket, or -1
+    int* list;     // [nslots]     (CTA-wide routing) slot ids by ticket inside each expert's range
 };
 // the arrays above, in this order
 __host__ __device__ constexpr int moe_table_words(int E_local, int nslots) { return 5 * nslots + 3 * E_local + 2; }
@@ -339,6 +339,80 @@ __device__ __forceinline__ void moe_route_small(const QmvArgs& a, MoeTables tb, 
         }
     }
     if (lane == 0) *tb.nseg = tot >> 16;
+    __syncwarp();
+}
+
+// 33..MOE_WARP_MAX slots, one warp, in chunks of 32 (slot 32 r + lane). Per chunk, __match_any_sync groups the
+// chunk's slots by expert, and a running count per expert (cnt, updated by each group's leader) gives every slot its
+// place among its expert's slots in index order and marks the expert's first slot. Then one scan over the chunks of
+// (slots, segments) at the experts' first slots orders the experts by first appearance, as moe_route_small does;
+// each first slot publishes its expert's offsets (off) and segments, and every slot stores itself. Nine warp
+// syncs and no CTA barrier: with 64 slots of 128 experts the CTA-wide routing took ~1.8 us after the dependency on
+// B200 (in-kernel clock64 stamps), most of it in its five CTA barriers.
+constexpr int MOE_WARP_MAX = 128;
+
+__device__ __forceinline__ void moe_route_warp(const QmvArgs& a, MoeTables tb, int lane, int nslots) {
+    constexpr int RM = MOE_WARP_MAX / 32;
+    const unsigned all = 0xffffffffu, below = (1u << lane) - 1u;
+    const int R = (nslots + 31) >> 5;   // chunks (2..RM)
+    int e[RM], rk[RM];
+    unsigned own = 0;                   // bit r: slot 32 r + lane is its expert's first slot
+#pragma unroll
+    for (int r = 0; r < RM; ++r) {      // all loads first
+        const int i = 32 * r + lane;
+        int v = i < nslots ? __ldg(a.idx + i) - a.e0 : -1;
+        if (v < 0 || v >= a.E_local) v = -1;
+        e[r] = v;
+        rk[r] = 0;
+    }
+#pragma unroll
+    for (int r = 0; r < RM; ++r)
+        if (e[r] >= 0) tb.cnt[e[r]] = 0;
+    __syncwarp();
+#pragma unroll
+    for (int r = 0; r < RM; ++r) {
+        if (r < R) {   // (uniform over the warp)
+            const unsigned same = __match_any_sync(all, e[r]);
+            const int before = e[r] >= 0 ? tb.cnt[e[r]] : 0;   // slots of this expert in earlier chunks
+            rk[r] = before + __popc(same & below);
+            __syncwarp();
+            if (e[r] >= 0 && lane == __ffs(same) - 1) {
+                if (before == 0) own |= 1u << r;
+                tb.cnt[e[r]] = before + __popc(same);
+            }
+            __syncwarp();
+        }
+    }
+    int carry = 0;   // (slots | segments << 16) of the experts first seen in earlier chunks
+#pragma unroll
+    for (int r = 0; r < RM; ++r) {
+        if (r < R) {
+            const bool o = (own >> r) & 1u;
+            const int c = o ? tb.cnt[e[r]] : 0, segs = (c + QMV_MAXTOK - 1) / QMV_MAXTOK;
+            const int mine = c | (segs << 16);
+            int v = mine;
+#pragma unroll
+            for (int d = 1; d < 32; d <<= 1) {
+                const int u = __shfl_up_sync(all, v, d);
+                if (lane >= d) v += u;
+            }
+            const int excl = carry + v - mine;
+            if (o) {
+                const int first = excl & 0xFFFF, s0 = excl >> 16;
+                tb.off[e[r]] = first;
+                for (int k = 0; k < segs; ++k) {
+                    tb.seg[s0 + k] = (e[r] << 16) | (first + k * QMV_MAXTOK);
+                    tb.segc[s0 + k] = min(QMV_MAXTOK, c - k * QMV_MAXTOK);
+                }
+            }
+            carry += __shfl_sync(all, v, 31);
+        }
+    }
+    __syncwarp();
+#pragma unroll
+    for (int r = 0; r < RM; ++r)
+        if (e[r] >= 0) tb.slots[tb.off[e[r]] + rk[r]] = 32 * r + lane;
+    if (lane == 0) *tb.nseg = carry >> 16;
     __syncwarp();
 }
 
@@ -492,12 +566,16 @@ __host__ __device__ constexpr int qmv_nbars(int nstage) { return 2 * nstage + 4 
 // nearest even, the reference's conversion): no conversion launch, no extra shared memory, and the MMA path is the
 // fp16 one.
 // XB: a dense fp16-in call whose activations come in by the producer's bulk copy (QMV_XSTAGE_MAX).
-template <int F, int MODE, typename OutT, bool XF32 = false, int MINB = 2, bool XB = false>
+// WR: a MoE call of 33..MOE_WARP_MAX slots, routed by one warp in 32-slot chunks (moe_route_warp). The host picks
+// these instances by the slot count, so the others -- one-token calls among them -- keep their code without the
+// chunked router (inlined into every MoE instance it cost ~0.04 us at one token on B200).
+template <int F, int MODE, typename OutT, bool XF32 = false, int MINB = 2, bool XB = false, bool WR = false>
 __global__ void __launch_bounds__(32 * (QMV_NW + 1), MINB)
 qmv_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap ts, const __grid_constant__ QmvArgs a) {
     static_assert(!XF32 || MODE == QMV_DENSE || MODE == QMV_GLU, "fp32 activations: dense and gate/up calls");
     static_assert(!XB || (MODE == QMV_DENSE && !XF32), "bulk-copied activations: dense fp16-in calls");
     static_assert(MINB == 2 || (MODE != QMV_GLU && !XF32), "one-CTA register budget: dense fp16-in and MoE calls");
+    static_assert(!WR || MODE == QMV_MOE, "chunked one-warp routing: MoE calls without peer stores");
     constexpr bool GLU = MODE == QMV_GLU;
     constexpr bool MOE = MODE == QMV_MOE || MODE == QMV_MOE_P2P;
     extern __shared__ uint8_t smem_raw[];
@@ -558,10 +636,11 @@ qmv_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUten
     MoeTables tb{};
     if constexpr (MOE) {
         // the producer warp: barriers, then -- after the dependency, since the previous grid may have written the
-        // index list and the activations -- the resident token rows. Up to 32 slots it also builds the routing
-        // tables alone and goes on to the weight stream while the consumers wait for them; more slots are routed by
-        // the whole CTA.
+        // index list and the activations -- the resident token rows. Up to 32 slots (up to MOE_WARP_MAX in the WR
+        // instances) it also builds the routing tables alone and goes on to the weight stream while the consumers
+        // wait for them; more slots are routed by the whole CTA.
         const int nslots = a.T * a.topk;
+        constexpr int WMAX = WR ? MOE_WARP_MAX : 32;   // the most slots one warp routes
         tb = moe_tables(sm + a.moe_off, a.E_local, nslots);
         if (warp == QMV_NW) {
             if (lane == 0) {
@@ -576,11 +655,12 @@ qmv_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUten
                     bulk_load(xbuf + j * a.xpitch, a.x + (size_t)j * a.K, (uint32_t)(a.K * 2), &xfull[0]);
             }
             if (nslots <= 32) moe_route_small(a, tb, lane, nslots);
-        } else if (nslots > 32) {
+            else if constexpr (WMAX > 32) { if (nslots <= WMAX) moe_route_warp(a, tb, lane, nslots); }
+        } else if (nslots > WMAX) {
             pdl_wait();
         }
-        if (nslots <= 32) {
-            // one warp routed: the producer goes on to the weight stream at once
+        if (nslots <= WMAX) {
+            // one warp routed (moe_route_small, moe_route_warp): the producer goes on to the weight stream at once
             if (warp == QMV_NW) named_arrive(2, 32 * (QMV_NW + 1));
             else named_sync(2, 32 * (QMV_NW + 1));
         } else {

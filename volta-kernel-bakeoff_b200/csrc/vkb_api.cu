@@ -244,10 +244,10 @@ static bool plan_qmv(int fmt, int N, int K, int xrows, int moe_slots, int E_loca
     return true;
 }
 
-template <int F, int MODE, typename OutT, bool XF32 = false, int MINB = 2, bool XB = false>
+template <int F, int MODE, typename OutT, bool XF32 = false, int MINB = 2, bool XB = false, bool WR = false>
 static int launch_qmv(const QmvPlan& p, const CUtensorMap& tq, const CUtensorMap& ts, int grid, cudaStream_t st,
                       int dev) {
-    auto kern = qmv_kernel<F, MODE, OutT, XF32, MINB, XB>;
+    auto kern = qmv_kernel<F, MODE, OutT, XF32, MINB, XB, WR>;
     static std::once_flag once[kMaxDevices];
     static cudaError_t attr_err[kMaxDevices];
     std::call_once(once[dev], [&] {
@@ -381,6 +381,13 @@ static int qmv_entry(const void* q, const void* s, const void* x, void* y, bool 
             if (p2p)   // one CTA per SM
                 return f32 ? launch_qmv<F, QMV_MOE_P2P, float, false, 1>(p, tq, ts, grid, st, dev)
                            : launch_qmv<F, QMV_MOE_P2P, __half, false, 1>(p, tq, ts, grid, st, dev);
+            if (slots > 32 && slots <= MOE_WARP_MAX) {   // routed by one warp in 32-slot chunks
+                if (grid > d.sm_count)
+                    return f32 ? launch_qmv<F, QMV_MOE, float, false, 2, false, true>(p, tq, ts, grid, st, dev)
+                               : launch_qmv<F, QMV_MOE, __half, false, 2, false, true>(p, tq, ts, grid, st, dev);
+                return f32 ? launch_qmv<F, QMV_MOE, float, false, 1, false, true>(p, tq, ts, grid, st, dev)
+                           : launch_qmv<F, QMV_MOE, __half, false, 1, false, true>(p, tq, ts, grid, st, dev);
+            }
             if (grid > d.sm_count)
                 return f32 ? launch_qmv<F, QMV_MOE, float>(p, tq, ts, grid, st, dev)
                            : launch_qmv<F, QMV_MOE, __half>(p, tq, ts, grid, st, dev);
