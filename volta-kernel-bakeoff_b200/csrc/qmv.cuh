@@ -18,7 +18,7 @@
 //     the bandwidth of these on B200. The weight stages are issued
 //     before griddepcontrol.wait, so under programmatic dependent launch the next call's weight stream overlaps the
 //     previous call's tail. The activations (after the wait): dense calls' small blocks are loaded by the consumers
-//     themselves in fragment order (see QMV_XSTAGE_MAX); larger blocks and MoE segments come in as 1-D bulk copies.
+//     themselves in fragment order (see qmv_xstage_max); larger blocks and MoE segments come in as 1-D bulk copies.
 //   * warps 0..NW-1 split each stage's K range and run the m16n8k16 tensor-core MMA with the weights as A (16 rows)
 //     and the tokens as B (8 columns). The codes enter the MMA exactly: the fp16 magic-number trick (0x6400 | n is
 //     the half 1024 + n) turns two codes into one f16x2 with one LOP3 and one HSUB2/HFMA2, and every 32-value group is
@@ -202,8 +202,14 @@ __device__ __forceinline__ constexpr int chunk_hi() { return F == FMT_Q2 ? 8 : 4
 // by the consumer threads themselves, in fragment order. Measured on B200 (µs, 50-call graphs): 8 x 6144 activations
 // staged by the consumers took 2048x6144 2-bit from 4.7 to 5.7 and Q8 from 6.05 to 6.6, while 2 x 6144 took Q4
 // 2560x6144 from 6.2 to 5.6; permuting the bulk copy in place once was slower than both (shared-memory traffic), and
-// one kernel holding both loops ran both slower than the single-loop kernels.
+// one kernel holding both loops ran both slower than the single-loop kernels. Q4 calls keep the consumers' staging up
+// to twice as many values: at 32768 every Q4 case that moved got faster (2560x6144 at 4 tokens 6.37 -> 5.77 µs,
+// 12288x2560 at 8 tokens 8.50 -> 8.22, 2048x6144 at 4 tokens 4.80 -> 4.67), while Q8 and 2-bit had one case faster
+// and one slower each.
 constexpr int QMV_XSTAGE_MAX = 16384;
+__host__ __device__ constexpr int qmv_xstage_max(int fmt) {
+    return fmt == FMT_Q4 ? 2 * QMV_XSTAGE_MAX : QMV_XSTAGE_MAX;
+}
 
 // One group: two k16 MMAs into a fresh fragment, then the per-row fp32 scales. ca: row g's codes in the stage;
 // row g+8 is 8 * cp further.
@@ -565,7 +571,7 @@ __host__ __device__ constexpr int qmv_nbars(int nstage) { return 2 * nstage + 4 
 // and gate/up call's activations themselves after the dependency wait; these they round to fp16 on the way (round to
 // nearest even, the reference's conversion): no conversion launch, no extra shared memory, and the MMA path is the
 // fp16 one.
-// XB: a dense fp16-in call whose activations come in by the producer's bulk copy (QMV_XSTAGE_MAX).
+// XB: a dense fp16-in call whose activations come in by the producer's bulk copy (qmv_xstage_max).
 // WR: a MoE call of 33..MOE_WARP_MAX slots, routed by one warp in 32-slot chunks (moe_route_warp). The host picks
 // these instances by the slot count, so the others -- one-token calls among them -- keep their code without the
 // chunked router (inlined into every MoE instance it cost ~0.04 us at one token on B200).
@@ -823,7 +829,8 @@ qmv_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUten
         // dense and gate/up calls: the consumers stage the token rows themselves, in fragment order (frag_order), so
         // that every group's B registers are one 16-byte load; fp32 activations are rounded to fp16 on the way (round
         // to nearest even, the reference's conversion). Items = (token, 16-byte chunk) pairs over the consumer
-        // threads, coalesced; each thread keeps R items' loads in flight (one round for QMV_XSTAGE_MAX values). Then
+        // threads, coalesced; each thread keeps R items' loads in flight (one round for the blocks of each instance:
+        // up to 16384 values under the two-CTA budget, 32768 under the one-CTA budget). Then
         // one barrier. (Measured on B200 against the producer's bulk copy with the permutation in every group's load:
         // 8192x2048 Q4 1 token 4.6 -> 4.1-4.4 us.)
         constexpr int R = XF32 ? 4 : (MINB == 1 ? 8 : 4);

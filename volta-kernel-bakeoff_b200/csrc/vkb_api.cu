@@ -395,7 +395,7 @@ static int qmv_entry(const void* q, const void* s, const void* x, void* y, bool 
                        : launch_qmv<F, QMV_MOE, __half, false, 1>(p, tq, ts, grid, st, dev);
         }
         if (2 * (p.smem + 1024) > d.smem_per_sm) {   // one CTA per SM: the 96-register variant
-            if ((long long)M * K > QMV_XSTAGE_MAX)       // activations by bulk copy
+            if ((long long)M * K > qmv_xstage_max(F))    // activations by bulk copy
                 return f32 ? launch_qmv<F, QMV_DENSE, float, false, 1, true>(p, tq, ts, grid, st, dev)
                            : launch_qmv<F, QMV_DENSE, __half, false, 1, true>(p, tq, ts, grid, st, dev);
             return f32 ? launch_qmv<F, QMV_DENSE, float, false, 1>(p, tq, ts, grid, st, dev)
