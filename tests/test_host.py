@@ -38,6 +38,20 @@ def test_every_declared_symbol_has_a_binding():
     assert not unbound, unbound
 
 
+def test_missing_library_fails_loudly(monkeypatch):
+    """No fallback: without libvkb.so every entry point of the Python binding raises instead of computing elsewhere."""
+    monkeypatch.setattr(vkb, "_lib", None)
+    monkeypatch.setattr(vkb, "LIB_PATH", os.path.join(ROOT, "no-such-dir", "libvkb.so"))
+    with pytest.raises(ImportError, match="missing"):
+        vkb.lib()
+    import torch
+    q = torch.zeros(64 * 256 // 2, dtype=torch.uint8)
+    s = torch.zeros((64, 256 // 32), dtype=torch.float16)
+    x = torch.zeros((1, 256), dtype=torch.float16)
+    with pytest.raises(ImportError):
+        vkb.gemv(O.FMT_Q4, q, s, x)
+
+
 def test_strerror_and_version():
     assert vkb.lib().vkb_version() >= 100
     assert "unsupported" in vkb.strerror(vkb.EUNSUPPORTED)
