@@ -45,6 +45,10 @@ def test_decode_plans_fit(fmt):
         assert p["tiles"] == (N + 15) // 16 and p["grid"] == min(p["tiles"], LIM["sm_count"])
         two_per_sm = 2 * p["smem"] <= LIM["smem_per_sm"]
         assert not two_per_sm or p["nstage"] >= 4 or p["nstage"] == 16, (N, K, M, p)
+        # the two-CTA footprint (the 56-register kernel instances) only for K <= 2048 covered by one stage; the host
+        # launches the one-CTA instances when two CTAs (plus the runtime's 1 KB each) do not fit an SM
+        if 2 * (p["smem"] + 1024) <= LIM["smem_per_sm"]:
+            assert p["nchunks"] == 1 and K <= 2048, (N, K, M, p)
     assert n > 100
 
 
