@@ -70,6 +70,10 @@ def test_bad_arguments_rejected_before_any_cuda_call():
     assert L.vkb_gemv_q4(one, one, one, one, 64, 256, 0, nul) == vkb.EINVAL
     assert L.vkb_gemv(7, one, one, one, one, 0, 64, 256, 1, nul) == vkb.EUNSUPPORTED
     assert L.vkb_moe_q4(one, one, nul, 1, 8, one, one, 8, 0, 64, 256, nul) == vkb.EINVAL
+    # multi-GPU entry points without a communicator: refused before anything else
+    assert L.vkb_gemm_q4_tc_rowsplit_noalloc(nul, one, one, one, one, 1024, 2048, 64, nul) == vkb.ENOCOMM
+    assert L.vkb_gemm_q4_tc_rowsplit(nul, one, one, one, one, one, 1024, 2048, 64, nul) == vkb.ENOCOMM
+    assert L.vkb_gemm_q4_tc_rowsplit_p2p(nul, one, one, one, one, 1024, 2048, 64, nul) == vkb.ENOCOMM
 
 
 @pytest.mark.parametrize("fmt", [O.FMT_Q4, O.FMT_Q8, O.FMT_Q2])
