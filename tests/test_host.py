@@ -30,6 +30,18 @@ def test_library_exports_every_declared_symbol():
     assert not missing, missing
 
 
+def test_c_abi_is_exactly_the_headers():
+    """Every unmangled function libvkb.so exports is declared in include/ (no undocumented entry points)."""
+    import shutil
+    import subprocess
+    if shutil.which("nm") is None:
+        pytest.skip("nm not available")
+    out = subprocess.run(["nm", "-D", "--defined-only", vkb.LIB_PATH], capture_output=True, text=True, check=True)
+    exported = {f[2] for f in (ln.split() for ln in out.stdout.splitlines())
+                if len(f) == 3 and f[1] == "T" and not f[2].startswith("_")}
+    assert exported == set(_declared_symbols()), exported ^ set(_declared_symbols())
+
+
 def test_every_declared_symbol_has_a_binding():
     """vkb.lib() sets argument and result types for every entry point the headers declare (a ctypes call without them
     would pass 64-bit pointers as C ints)."""
