@@ -164,8 +164,14 @@ int vkb_gemm_q4_tc_rowsplit(vkb_comm_t* comm, const void* q_local, const void* s
                             void* work, int N, int K, int M, vkb_stream_t stream);
 int vkb_gemm_q4_tc_rowsplit_f32(vkb_comm_t* comm, const void* q_local, const void* s_local, const void* x, float* y,
                                 void* work, int N, int K, int M, vkb_stream_t stream);
-/* vkb_gemm_q4_tc_rowsplit (fp16 y) with no workspace argument and no allocation: the workspace is a static device
- * array of the library, 16 MiB per device, looked up once per device. No counterpart in the reference. M * N * 2 must
+/* vkb_gemm_q4_tc_rowsplit (fp16 y) with no workspace argument and no allocation, for callers that cannot allocate
+ * device memory: a launcher with the reference harness's fixed contender signature, which has no workspace argument
+ * (allocating inside it would put cudaMalloc / cudaFree, and cudaFree's device-wide synchronisation, into every
+ * timed call), and a serving process whose device memory belongs to a pool reserved at start-up, where a cudaMalloc
+ * either fails or takes memory the pool has promised elsewhere. The workspace is a static device array of the
+ * library: 16 MiB on every GPU that loads libvkb.so, held until the process exits. The first call on each device
+ * looks up the array's device address (cudaGetSymbolAddress, with that device current; its error is returned): make
+ * that first call before any stream capture. No counterpart in the reference. M * N * 2 must
  * not exceed VKB_ROWSPLIT_NOALLOC_MAX_BYTES (VKB_EUNSUPPORTED otherwise, nothing launched). Calls that overlap in time
  * on one device (other streams, host threads or communicators) share the array and race: serialise them. If the
  * array's lookup fails on one rank, that rank still joins the all-gather (through y) and returns the lookup error.

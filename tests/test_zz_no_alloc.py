@@ -1,5 +1,7 @@
 """vkb_gemm_q4_tc_rowsplit_noalloc: the row-split prompt GEMM with its workspace in the library's static device array
-(no allocation on the call path). On one GPU with a one-rank communicator: rounds of calls in a row (different
+(no allocation on the call path), for callers that cannot allocate device memory -- a launcher with the reference
+harness's fixed signature, which has no workspace argument, or a serving process whose device memory is all reserved
+by its own pool. On one GPU with a one-rank communicator: rounds of calls in a row (different
 shapes, then the first again) against vkb_gemm_q4_tc_rowsplit with a caller-owned workspace and against
 vkb_gemm_q4_tc -- bit for bit --, the device's free memory unchanged across a whole round once the first round has
 done the one-time set-up, and a shape past the array's size refused with nothing written. This file is collected last

@@ -137,13 +137,19 @@ static int moe_ep(vkb_comm_t* c, int fmt, const void* qpool, const void* spool, 
 }
 
 // Workspace of the allocation-free row-split entry point: a file-scope device array (no cudaMalloc anywhere on that
-// path). Its size bounds M * N * 2 bytes. Every byte is written before it is read (block r by this rank's kernel, the
-// others by the all-gather), so nothing has to be cleared between calls; calls that overlap in time (two streams,
-// two host threads, or two communicators in one process on the same device) share it and race.
+// path), for callers that cannot allocate: a launcher with a fixed signature that has no workspace argument, or a
+// process whose device memory is all reserved by its own pool. Every GPU that loads the library holds the 16 MiB
+// until the process exits. Its size bounds M * N * 2 bytes. Every byte is written before it is read (block r by this
+// rank's kernel, the others by the all-gather), so nothing has to be cleared between calls; calls that overlap in
+// time (two streams, two host threads, or two communicators in one process on the same device) share it and race.
+// In host code the name g_rowsplit_scratch is a host-side stand-in, not a device address: only the address that
+// rowsplit_scratch() looks up may be passed to a kernel.
 constexpr size_t kRowsplitScratchBytes = (size_t)16 << 20;
 static __device__ __align__(256) uint8_t g_rowsplit_scratch[kRowsplitScratchBytes];
 
-// Device address of the array on device `dev`, looked up once per device (the symbol is per device context).
+// Device address of the array on device `dev`, looked up once per device (the symbol is per device context) by the
+// first call on that device, with `dev` current (the caller's current device); the entry point's first call on a
+// device should therefore come before any stream capture.
 static int rowsplit_scratch(int dev, void** out) {
     static std::once_flag once[kMaxDevices];
     static void* addr[kMaxDevices];
