@@ -1,4 +1,4 @@
-"""The multi-GPU decomposition on CPU: partition helpers, and the two combines run as world_size-2 gloo ranks over
+"""The multi-GPU decomposition on CPU: partition helpers, and the two combines run as world_size-2 and -4 gloo ranks over
 oracle outputs -- expert parallelism (own slots, zeros elsewhere, summed) and the row split (per-rank [M][N/G] blocks,
 gathered and permuted) -- checked exactly against the one-device oracle. The combine arithmetic restated here is
 what vkb_moe_ep / vkb_gemm_q4_tc_rowsplit do on the GPUs with NCCL."""
@@ -81,12 +81,13 @@ def _rank_main(rank, world, port, q):
         q.put((rank, None, None, repr(e)))
 
 
-def test_combines_gloo_world2():
+@pytest.mark.parametrize("world", [2, 4])
+def test_combines_gloo(world):
     import torch.multiprocessing as mp
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_rank_main, args=(r, 2, port, q)) for r in range(2)]
+    procs = [ctx.Process(target=_rank_main, args=(r, world, port, q)) for r in range(world)]
     for p in procs:
         p.start()
     results = [q.get(timeout=240) for _ in procs]
